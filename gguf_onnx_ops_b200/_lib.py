@@ -1,0 +1,81 @@
+"""ctypes binding of libgguf_onnx_ops.so (the C ABI declared in include/gguf_ops.h).
+
+The shared library is the product; this module only loads it and declares the entry points.
+There is no CPU or PyTorch fallback: if the library cannot be loaded, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libgguf_onnx_ops.so")
+
+GGUF_OK = 0
+GGUF_ERR_INVALID_ARGUMENT = 1
+GGUF_ERR_CUDA = 2
+GGUF_ERR_NOT_IMPLEMENTED = 3
+GGUF_ERR_DEVICE = 4
+
+GGUF_TYPE_Q8_0 = 8
+GGUF_TYPE_IQ2_XXS = 16
+GGUF_TYPE_NVFP4 = 40
+
+# name -> (restype, argtypes); mirrors include/gguf_ops.h
+_P, _I64, _I32, _F32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+SIGNATURES = {
+    "gguf_version": (ctypes.c_char_p, []),
+    "gguf_last_error": (ctypes.c_char_p, []),
+    "gguf_q8_0_gemv": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
+    "gguf_iq2_xxs_gemv": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
+    "gguf_nvfp4_gemv": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "gguf_moe_route": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),
+    "gguf_moe_verify_iq2_xxs": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "gguf_dequantize": (_I32, [_I32, _P, _P, _I64, _I64, _P]),
+    "gguf_device_status": (_I32, [ctypes.POINTER(ctypes.c_int)]),
+    "gguf_set_pdl": (None, [_I32]),
+}
+
+
+class GgufOpsError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+_lib = None
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load the library once (raises OSError with a clear message if it has not been built)."""
+    global _lib
+    if _lib is None:
+        p = path or os.environ.get("GGUF_OPS_LIB", LIB_PATH)
+        if not os.path.exists(p):
+            raise OSError(f"{p} not found: build it with `python -m gguf_onnx_ops_b200.build` "
+                          "(there is no CPU fallback)")
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != GGUF_OK:
+        msg = load().gguf_last_error().decode("utf-8", "replace")
+        if rc == GGUF_ERR_INVALID_ARGUMENT:
+            raise ValueError(msg)
+        if rc == GGUF_ERR_NOT_IMPLEMENTED:
+            raise NotImplementedError(msg)
+        raise GgufOpsError(rc, msg)
+
+
+def device_status() -> tuple[int, int]:
+    """(status, site) of kernel-side bounded waits on the current device; synchronises."""
+    site = ctypes.c_int(0)
+    rc = load().gguf_device_status(ctypes.byref(site))
+    return rc, site.value

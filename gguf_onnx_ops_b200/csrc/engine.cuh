@@ -1,0 +1,364 @@
+// Persistent skinny-GEMM engine for raw GGUF weights on sm_100a.
+//
+//   y[col, row] = sum_k x[col, k] * W[row, k]      (col < R <= 16, row < rows)
+//
+// Work unit = a 16-row weight tile (MMA M side).  One CTA per SM (<= half of the SM's shared
+// memory, so that the next kernel on the stream can co-reside and prefetch under programmatic
+// dependent launch) loops over tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+//
+//   warp KW (producer) : one lane streams each tile's raw bytes into a ring of `stages` shared-
+//                        memory stages with 1-D bulk async copies (TMA engine), completion
+//                        tracked by a "full" mbarrier per stage; it refills a stage once the KW
+//                        consumer warps have arrived on its "empty" mbarrier.  A stage holds
+//                        16 rows x kc elements (one bulk copy per row into a padded row stride,
+//                        or one contiguous copy of the whole tile when rows are not 16-byte
+//                        multiples).  Weight prefetch does not depend on the previous kernel.
+//   warps 0..KW-1      : after griddepcontrol.wait, split the stage's k-groups, decode each group
+//                        in registers (decode.cuh) and issue two mma.m16n8k16 per group per 8
+//                        activation rows; then reduce the KW partial tiles through shared memory
+//                        and store.
+//
+// MODE kDense: y = bf16(acc * post) for the dense GEMVs.
+// MODE kMoe1 / kMoe2: expert-grouped MoE phases over IQ2_XXS expert tensors (MoeVerify); the
+// unique-expert grouping of idx is recomputed by every CTA in shared memory.
+#pragma once
+
+#include "decode.cuh"
+
+namespace gguf_b200 {
+
+constexpr int kModeDense = 0, kModeMoe1 = 1, kModeMoe2 = 2;
+constexpr int kMaxPairs = 128;
+
+struct EngineArgs {
+  // weights
+  const uint8_t* w;  // 16-byte aligned
+  int K;             // reduction length
+  int row_bytes;     // raw bytes per weight row
+  int rows;          // rows per weight matrix (dense: N; MoE: rows of one expert)
+  int tiles;         // ceil(rows / 16) per matrix
+  // staging plan
+  int kc;            // K elements per stage
+  int nsplit;        // K / kc
+  int seg_bytes;     // raw bytes of kc elements of one row
+  int stride;        // shared-memory bytes per staged row
+  int contiguous;    // 1: one bulk copy of the whole tile (nsplit == 1, stride == row_bytes)
+  int stage_bytes;
+  int stages;
+  int off_stage, off_red, off_bar, off_grp;  // shared-memory layout
+  // activations / outputs
+  const bf16* x;     // dense: [R, K]; moe1: z [R, K]; moe2: h [P, K]
+  int R;
+  void* y;           // dense: bf16 [R, rows]; moe1: h bf16 [P, rows]; moe2: part f32 [P, rows]
+  const float* gscale;  // dense NVFP4 only (device scalar), else nullptr
+  float post;        // constant epilogue factor (2^16 for NVFP4, 1 otherwise)
+  // MoE
+  const int32_t* idx;  // [R, topk]
+  int topk, P, E;
+  int32_t* meta;       // moe1: written by CTA 0
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Unique-expert grouping of idx (first-occurrence order, as src/bolt_ops.cu:1233-1261):
+// s_uexp[u] = expert id of group u, s_pair[u*8 + row] = pair index (row*topk + k) or -1.
+// Pairs with an expert id outside [0, E) are ignored.  Returns U (in shared memory).
+__device__ __forceinline__ void moe_group(const EngineArgs& a, uint8_t* smem) {
+  int* s_idx = reinterpret_cast<int*>(smem + a.off_grp);
+  int* s_first = s_idx + kMaxPairs;
+  int* s_rank = s_first + kMaxPairs;
+  int* s_uexp = s_rank + kMaxPairs;
+  int* s_pair = s_uexp + kMaxPairs;  // [kMaxPairs][8]
+  int* s_U = s_pair + kMaxPairs * 8;
+  const int tid = threadIdx.x, nth = blockDim.x;
+  for (int i = tid; i < kMaxPairs * 8; i += nth) s_pair[i] = -1;
+  if (tid < a.P) s_idx[tid] = a.idx[tid];
+  __syncthreads();
+  if (tid < a.P) {
+    const int my = s_idx[tid];
+    int q = -1;
+    if (my >= 0 && my < a.E)
+      for (int j = 0; j <= tid; ++j)
+        if (s_idx[j] == my) {
+          q = j;
+          break;
+        }
+    s_first[tid] = q;
+  }
+  __syncthreads();
+  if (tid < a.P) {
+    if (s_first[tid] == tid) {
+      int r = 0;
+      for (int j = 0; j < tid; ++j) r += (s_first[j] == j);
+      s_rank[tid] = r;
+      s_uexp[r] = s_idx[tid];
+    }
+  }
+  if (tid == 0) {
+    int u = 0;
+    for (int j = 0; j < a.P; ++j) u += (s_first[j] == j);
+    *s_U = u;
+  }
+  __syncthreads();
+  if (tid < a.P && s_first[tid] >= 0) s_pair[s_rank[s_first[tid]] * 8 + tid / a.topk] = tid;
+  __syncthreads();
+}
+
+template <int F, int NT, int KW, int MODE>
+__global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+  uint64_t* empty = full + a.stages;
+  uint8_t* stages = smem + a.off_stage;
+  float* red = reinterpret_cast<float*>(smem + a.off_red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- prologue (independent of the previous kernel) ----
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], KW);
+    }
+    fence_mbar_init();
+  }
+  if constexpr (F == kFmtIQ2) {
+    // codebook replicated 8x: entry e, copy c at e*128 + c*16 -> the 8 lanes of each quarter-warp
+    // read distinct bank groups whatever entries they pick.
+    uint4* lut = reinterpret_cast<uint4*>(smem);
+    const uint4* src = reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[0][0]);
+    for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) lut[i] = src[i >> 3];
+  } else if constexpr (F == kFmtFP4) {
+    uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sl[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));
+  }
+
+  int nitems;
+  const int* s_uexp = nullptr;
+  const int* s_pair = nullptr;
+  if constexpr (MODE == kModeDense) {
+    nitems = a.tiles;
+    __syncthreads();
+    pdl_launch_dependents();
+  } else {
+    // The expert ids come from the previous kernel (the router): wait first.
+    pdl_wait();
+    moe_group(a, smem);  // ends with __syncthreads
+    const int* s_idx = reinterpret_cast<const int*>(smem + a.off_grp);
+    s_uexp = s_idx + 3 * kMaxPairs;
+    s_pair = s_uexp + kMaxPairs;
+    const int U = s_pair[kMaxPairs * 8];
+    nitems = U * a.tiles;
+    if constexpr (MODE == kModeMoe1) {
+      if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < 1 + 9 * a.P; i += blockDim.x) {
+          int v;
+          if (i == 0) v = U;
+          else if (i <= a.P) v = (i - 1 < U) ? s_uexp[i - 1] : -1;
+          else v = s_pair[i - 1 - a.P];
+          a.meta[i] = v;
+        }
+      }
+    }
+    pdl_launch_dependents();
+  }
+
+  auto tile_src = [&](int item, int& rows_valid) -> const uint8_t* {
+    int tile = item, mat = 0;
+    if constexpr (MODE != kModeDense) {
+      tile = item % a.tiles;
+      mat = s_uexp[item / a.tiles];
+    }
+    rows_valid = min(16, a.rows - tile * 16);
+    return a.w + (static_cast<int64_t>(mat) * a.rows + static_cast<int64_t>(tile) * 16) * a.row_bytes;
+  };
+
+  if (warp == KW) {
+    // ================= producer =================
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+        int rv;
+        const uint8_t* src = tile_src(item, rv);
+        for (int sp = 0; sp < a.nsplit; ++sp, ++it) {
+          const int s = static_cast<int>(it % a.stages);
+          if (it >= static_cast<uint32_t>(a.stages)) mbar_wait(&empty[s], ((it / a.stages) - 1) & 1, kSiteEmptyWait);
+          uint8_t* dst = stages + s * a.stage_bytes;
+          if (a.contiguous) {
+            const uint32_t bytes = static_cast<uint32_t>(rv * a.row_bytes);
+            const uint32_t bulk = bytes & ~15u;
+            for (uint32_t b = bulk; b < bytes; ++b) dst[b] = src[b];  // < 16 trailing bytes
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&full[s], bulk);
+            if (bulk) bulk_g2s(dst, src, bulk, &full[s]);
+          } else {
+            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.seg_bytes));
+            const uint8_t* s0 = src + static_cast<int64_t>(sp) * a.seg_bytes;
+            for (int r = 0; r < rv; ++r)
+              bulk_g2s(dst + r * a.stride, s0 + static_cast<int64_t>(r) * a.row_bytes, a.seg_bytes, &full[s]);
+          }
+        }
+      }
+      // drain: the last uses of each stage must have landed before the CTA may exit
+      const uint32_t total = it;
+      const uint32_t first = total > static_cast<uint32_t>(a.stages) ? total - a.stages : 0u;
+      for (uint32_t j = first; j < total; ++j) mbar_wait(&full[j % a.stages], (j / a.stages) & 1, kSiteDrainWait);
+    }
+    return;
+  }
+
+  // ================= consumers =================
+  if constexpr (MODE == kModeDense) pdl_wait();  // x was written by the previous kernel
+  const int g = lane >> 2, t = lane & 3;
+  const int gps = a.kc / 32;  // k-groups per stage
+  const int g0 = (warp * gps) / KW, g1 = ((warp + 1) * gps) / KW;
+  float post = a.post;
+  if constexpr (MODE == kModeDense && F == kFmtFP4) post *= __ldg(a.gscale);
+  const uint32_t lut_lane = static_cast<uint32_t>(lane & 7) * 16u;
+  const uint16_t* fp4lut = reinterpret_cast<const uint16_t*>(smem);
+
+  uint32_t it = 0;
+  for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+    int u = 0, tile = item;
+    if constexpr (MODE != kModeDense) {
+      u = item / a.tiles;
+      tile = item % a.tiles;
+    }
+    // activation row for B-fragment column n = nt*8 + g
+    const bf16* xr[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int col = nt * 8 + g;
+      int xrow;
+      if constexpr (MODE == kModeMoe2) {
+        const int p = col < 8 ? s_pair[u * 8 + col] : -1;
+        xrow = p < 0 ? 0 : p;
+      } else {
+        xrow = min(col, a.R - 1);
+      }
+      xr[nt] = a.x + static_cast<int64_t>(xrow) * a.K;
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+
+    for (int sp = 0; sp < a.nsplit; ++sp, ++it) {
+      const int s = static_cast<int>(it % a.stages);
+      mbar_wait(&full[s], (it / a.stages) & 1, kSiteFullWait);
+      const uint8_t* st = stages + s * a.stage_bytes;
+      const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
+      const int kbase = sp * a.kc;
+      for (int grp = g0; grp < g1; ++grp) {
+        const int k0 = kbase + grp * 32;
+        if constexpr (F == kFmtQ8) {
+          uint32_t A0[4], A1[4];
+          float d0, d1;
+          q8_decode_row(st, r0, grp, t, A0, d0);
+          q8_decode_row(st, r1, grp, t, A1, d1);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint2 xl = ldg64(xr[nt] + k0 + 4 * t);
+            const uint2 xh = ldg64(xr[nt] + k0 + 16 + 4 * t);
+            const float z[4] = {0.f, 0.f, 0.f, 0.f};
+            float D[4];
+            mma_bf16_16816(D, A0[0], A1[0], A0[1], A1[1], xl.x, xl.y, z);
+            mma_bf16_16816(D, A0[2], A1[2], A0[3], A1[3], xh.x, xh.y, D);
+            acc[nt][0] = fmaf(d0, D[0], acc[nt][0]);
+            acc[nt][1] = fmaf(d0, D[1], acc[nt][1]);
+            acc[nt][2] = fmaf(d1, D[2], acc[nt][2]);
+            acc[nt][3] = fmaf(d1, D[3], acc[nt][3]);
+          }
+        } else if constexpr (F == kFmtIQ2) {
+          const uint32_t sbo = static_cast<uint32_t>(grp >> 3) * 66u;
+          const uint32_t rec = sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u;
+          const uint2 q0 = ld_u64_a2(st, r0 + rec);
+          const uint2 q1 = ld_u64_a2(st, r1 + rec);
+          const float d0 = fp16_bits_to_f32(ld_u16(st, r0 + sbo));
+          const float d1 = fp16_bits_to_f32(ld_u16(st, r1 + sbo));
+          const uint32_t gi0 = (q0.x >> (8 * t)) & 0xFFu, gi1 = (q1.x >> (8 * t)) & 0xFFu;
+          const uint4 m0 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi0 << 7));
+          const uint4 m1 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi1 << 7));
+          uint32_t A0[4], A1[4];
+          iq2_apply_signs(m0, q0.y, 7u * t, A0);
+          iq2_apply_signs(m1, q1.y, 7u * t, A1);
+          const float db0 = iq2_db(d0, q0.y), db1 = iq2_db(d1, q1.y);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint4 xv = ldg128(xr[nt] + k0 + 8 * t);
+            const float z[4] = {0.f, 0.f, 0.f, 0.f};
+            float D[4];
+            mma_bf16_16816(D, A0[0], A1[0], A0[1], A1[1], xv.x, xv.y, z);
+            mma_bf16_16816(D, A0[2], A1[2], A0[3], A1[3], xv.z, xv.w, D);
+            acc[nt][0] = fmaf(db0, D[0], acc[nt][0]);
+            acc[nt][1] = fmaf(db0, D[1], acc[nt][1]);
+            acc[nt][2] = fmaf(db1, D[2], acc[nt][2]);
+            acc[nt][3] = fmaf(db1, D[3], acc[nt][3]);
+          }
+        } else {  // NVFP4: group = sub-blocks 2h, 2h+1 of block grp/2
+          const uint32_t bo = static_cast<uint32_t>(grp >> 1) * 36u;
+          const uint32_t h2 = static_cast<uint32_t>(grp & 1) * 2u;
+          const uint32_t sc0 = ld_u16(st, r0 + bo + h2), sc1 = ld_u16(st, r1 + bo + h2);
+#pragma unroll
+          for (int s2 = 0; s2 < 2; ++s2) {
+            const uint32_t nib = bo + 4u + (h2 + s2) * 8u + 2u * t;
+            const uint32_t v0 = ld_u16(st, r0 + nib), v1 = ld_u16(st, r1 + nib);
+            const uint32_t S0 = fp4lut[(sc0 >> (8 * s2)) & 0xFFu], S1 = fp4lut[(sc1 >> (8 * s2)) & 0xFFu];
+            uint32_t l0, h0, l1, h1;
+            fp4_patterns(v0, l0, h0);
+            fp4_patterns(v1, l1, h1);
+            const uint32_t S0x2 = S0 | (S0 << 16), S1x2 = S1 | (S1 << 16);
+            l0 = hmul2_bits(l0, S0x2);
+            h0 = hmul2_bits(h0, S0x2);
+            l1 = hmul2_bits(l1, S1x2);
+            h1 = hmul2_bits(h1, S1x2);
+            const int ks = k0 + 16 * s2;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint32_t b0 = ldg32(xr[nt] + ks + 2 * t);
+              const uint32_t b1 = ldg32(xr[nt] + ks + 8 + 2 * t);
+              mma_bf16_16816(acc[nt], l0, l1, h0, h1, b0, b1, acc[nt]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---- cross-warp reduction of the 16 x (8*NT) tile ----
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float* rw = red + (warp * NT + nt) * 128;
+      rw[g * 8 + 2 * t] = acc[nt][0];
+      rw[g * 8 + 2 * t + 1] = acc[nt][1];
+      rw[(g + 8) * 8 + 2 * t] = acc[nt][2];
+      rw[(g + 8) * 8 + 2 * t + 1] = acc[nt][3];
+    }
+    named_bar_sync(1, KW * 32);
+    for (int i = threadIdx.x; i < NT * 128; i += KW * 32) {
+      const int nt = i >> 7, rl = (i & 127) >> 3, col = nt * 8 + (i & 7);
+      float v = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < KW; ++w2) v += red[(w2 * NT + nt) * 128 + (i & 127)];
+      const int row = tile * 16 + rl;
+      if (row >= a.rows || col >= a.R) continue;
+      if constexpr (MODE == kModeDense) {
+        reinterpret_cast<bf16*>(a.y)[static_cast<int64_t>(col) * a.rows + row] = __float2bfloat16(v * post);
+      } else {
+        const int p = s_pair[u * 8 + col];
+        if (p < 0) continue;
+        const float vb = round_bf16(v);
+        if constexpr (MODE == kModeMoe1) {
+          const float r = fmaxf(vb, 0.f);
+          reinterpret_cast<bf16*>(a.y)[static_cast<int64_t>(p) * a.rows + row] = __float2bfloat16(r * r);
+        } else {
+          reinterpret_cast<float*>(a.y)[static_cast<int64_t>(p) * a.rows + row] = vb;
+        }
+      }
+    }
+    named_bar_sync(1, KW * 32);
+  }
+}
+
+}  // namespace gguf_b200

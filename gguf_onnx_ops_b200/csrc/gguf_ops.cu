@@ -1,0 +1,362 @@
+// libgguf_onnx_ops: C ABI (include/gguf_ops.h) over the sm_100a GGUF decode kernels.
+//
+// Host responsibilities per call: validate the op contract (same constraints and messages as
+// the reference ops in src/bolt_ops.cu), pick the staging plan of the engine, and enqueue the
+// kernels on the caller's stream with cudaLaunchKernelEx (programmatic dependent launch
+// attribute on by default).  No allocation, no synchronisation.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/gguf_ops.h"
+#include "engine.cuh"
+#include "small_kernels.cuh"
+
+namespace gguf_b200 {
+
+namespace {
+
+thread_local std::string t_last_error;
+std::atomic<int> g_pdl{1};
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+int cuda_fail(const char* op, cudaError_t e) { return fail(GGUF_ERR_CUDA, std::string(op) + ": " + cudaGetErrorString(e)); }
+
+constexpr int kKW = 8;                      // consumer warps per CTA
+constexpr int kThreads = (kKW + 1) * 32;    // + 1 producer warp
+constexpr int kSmemBudget = 112 * 1024;     // <= half an SM: two kernels' CTAs can co-reside
+constexpr int kSmemBudgetMax = 220 * 1024;  // fallback for very long rows
+constexpr int kStageTarget = 20 * 1024;
+
+struct DeviceInfo {
+  int sms = 0;
+};
+DeviceInfo g_dev[64];
+
+int current_sms(int* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= 64) return fail(GGUF_ERR_CUDA, "device ordinal out of range");
+  if (g_dev[dev].sms == 0) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail("cudaDeviceGetAttribute", e);
+    g_dev[dev].sms = n;
+  }
+  *sms = g_dev[dev].sms;
+  return GGUF_OK;
+}
+
+// Raises the dynamic shared-memory limit of `fn` once per device.
+template <typename Fn>
+int ensure_smem(Fn fn, size_t bytes, std::atomic<uint64_t>& done_mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done_mask.load() & bit) return GGUF_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudgetMax);
+  if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
+  (void)bytes;
+  done_mask.fetch_or(bit);
+  return GGUF_OK;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (g_pdl.load()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Staging plan
+// ---------------------------------------------------------------------------------------------
+template <int F>
+int make_plan(EngineArgs& a, int K, int row_bytes, int NT, bool moe, size_t* smem_out) {
+  using Fi = FmtInfo<F>;
+  a.K = K;
+  a.row_bytes = row_bytes;
+  const int lut = F == kFmtIQ2 ? 256 * 8 * 16 : (F == kFmtFP4 ? 512 : 0);
+  const int red = kKW * NT * 128 * 4;
+  const int grp = moe ? (4 * kMaxPairs + kMaxPairs * 8 + 4) * 4 : 0;
+  bool seg = (row_bytes % 16 == 0) && (K % Fi::kSeg == 0);
+  int kc = K;
+  if (seg) {
+    // largest multiple of kSeg dividing K whose 16-row stage stays near kStageTarget
+    kc = Fi::kSeg;
+    for (int c = Fi::kSeg; c <= K; c += Fi::kSeg) {
+      if (K % c) continue;
+      if (16 * (c / Fi::kBlock * Fi::kBytes) <= kStageTarget || c == Fi::kSeg) kc = c;
+    }
+  }
+  a.kc = kc;
+  a.nsplit = K / kc;
+  a.seg_bytes = kc / Fi::kBlock * Fi::kBytes;
+  if (seg) {
+    // padded row stride: 16-byte multiple with stride/4 == 4 (mod 8) words, so the 8 rows a warp
+    // touches per load start in 8 different 4-bank groups.
+    int st = (a.seg_bytes + 15) & ~15;
+    if (st % 32 == 0) st += 16;
+    a.stride = st;
+    a.contiguous = 0;
+  } else {
+    a.stride = row_bytes;
+    a.contiguous = 1;
+  }
+  a.stage_bytes = ((16 * a.stride + 16) + 127) & ~127;  // +16: unaligned-read overrun pad
+  const int fixed = lut + red + grp + 2 * 8 * 8 + 256;
+  int budget = kSmemBudget;
+  int stages = (budget - fixed) / a.stage_bytes;
+  if (stages < 2) {
+    budget = kSmemBudgetMax;
+    stages = (budget - fixed) / a.stage_bytes;
+  }
+  if (stages < 1) return fail(GGUF_ERR_INVALID_ARGUMENT, "K too large for the shared-memory staging plan");
+  a.stages = std::min(stages, 8);
+  size_t off = (lut + 127) & ~127;
+  a.off_stage = static_cast<int>(off);
+  off += static_cast<size_t>(a.stages) * a.stage_bytes;
+  a.off_red = static_cast<int>(off);
+  off += red;
+  off = (off + 15) & ~size_t(15);
+  a.off_bar = static_cast<int>(off);
+  off += 2 * a.stages * 8;
+  a.off_grp = static_cast<int>(off);
+  off += grp;
+  *smem_out = off;
+  return GGUF_OK;
+}
+
+bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+template <int F, int NT>
+int run_dense(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
+  EngineArgs a = {};
+  size_t smem = 0;
+  int rc = make_plan<F>(a, K, K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes, NT, false, &smem);
+  if (rc) return rc;
+  a.w = static_cast<const uint8_t*>(w);
+  a.rows = N;
+  a.tiles = (N + 15) / 16;
+  a.x = static_cast<const bf16*>(x);
+  a.R = R;
+  a.y = y;
+  a.gscale = gscale;
+  a.post = F == kFmtFP4 ? 65536.0f : 1.0f;
+  int sms = 0;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = engine_kernel<F, NT, kKW, kModeDense>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  const int grid = std::min(a.tiles, sms);
+  cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("gemv launch", e);
+  return GGUF_OK;
+}
+
+std::string dims(int64_t R, int64_t N, int64_t K) {
+  char b[128];
+  snprintf(b, sizeof(b), " (got R=%lld N=%lld K=%lld)", (long long)R, (long long)N, (long long)K);
+  return b;
+}
+
+bool int_range(int64_t v) { return v > 0 && v < (1ll << 31); }
+
+}  // namespace
+}  // namespace gguf_b200
+
+using namespace gguf_b200;
+
+extern "C" {
+
+const char* gguf_version(void) { return "gguf_onnx_ops_b200 0.1 (sm_100a)"; }
+
+const char* gguf_last_error(void) { return t_last_error.c_str(); }
+
+void gguf_set_pdl(int enable) { g_pdl.store(enable ? 1 : 0); }
+
+int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K, void* stream) {
+  t_last_error.clear();
+  if (!x || !w || !y) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: null tensor pointer");
+  if (K <= 0 || K % 64 != 0 || R < 1 || R > 16 || !int_range(N) || !int_range(K))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: needs B [N, (K/32)*34], K % 64 == 0 and 1..16 rows" + dims(R, N, K));
+  if (!aligned(w, 16) || !aligned(x, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: x and w must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return R <= 8 ? run_dense<kFmtQ8, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)
+                : run_dense<kFmtQ8, 2>(x, w, nullptr, y, (int)R, (int)N, (int)K, s);
+}
+
+int gguf_iq2_xxs_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K, void* stream) {
+  t_last_error.clear();
+  if (!x || !w || !y) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: null tensor pointer");
+  if (K <= 0 || K % 256 != 0 || R < 1 || R > 16 || !int_range(N) || !int_range(K))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: needs B [N, (K/256)*66], K % 256 == 0 and 1..16 rows" + dims(R, N, K));
+  if (!aligned(w, 16) || !aligned(x, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: x and w must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return R <= 8 ? run_dense<kFmtIQ2, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)
+                : run_dense<kFmtIQ2, 2>(x, w, nullptr, y, (int)R, (int)N, (int)K, s);
+}
+
+int gguf_nvfp4_gemv(const void* x, const void* w, const float* gscale, void* y, int64_t R, int64_t N, int64_t K,
+                    void* stream) {
+  t_last_error.clear();
+  if (!x || !w || !y || !gscale) return fail(GGUF_ERR_INVALID_ARGUMENT, "Nvfp4Gemv gguf=1: null tensor pointer");
+  if (K <= 0 || K % 64 != 0 || R < 1 || R > 16 || !int_range(N) || !int_range(K))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "Nvfp4Gemv gguf=1: needs w [N, (K/64)*36], K % 64 == 0 and 1..16 rows" + dims(R, N, K));
+  if (!aligned(w, 16) || !aligned(x, 16) || !aligned(gscale, 4))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "Nvfp4Gemv gguf=1: x and w must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return R <= 8 ? run_dense<kFmtFP4, 1>(x, w, gscale, y, (int)R, (int)N, (int)K, s)
+                : run_dense<kFmtFP4, 2>(x, w, gscale, y, (int)R, (int)N, (int)K, s);
+}
+
+int gguf_moe_route(const void* x, const float* gate_w, const float* bias, int32_t* idx, float* weights, float* scores,
+                   int64_t R, int64_t K, int64_t E, int64_t topk, float scale, void* stream) {
+  t_last_error.clear();
+  if (!x || !gate_w || !bias || !idx || !weights || !scores)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeRouteGGUF: null tensor pointer");
+  if (E < 1 || E > 512 || K <= 0 || K % 256 != 0 || topk < 1 || topk > 32 || topk > E || R < 1 || R > (1 << 24))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeRoute: unsupported shape (needs E <= 512, K % 256 == 0, 1 <= topk <= min(32, E))");
+  if (!aligned(x, 16) || !aligned(gate_w, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeRouteGGUF: x and gate_w must be 16-byte aligned");
+  const int clusters = static_cast<int>((R + kRouteRows - 1) / kRouteRows);
+  cudaError_t e = launch(route_kernel, dim3(clusters * kRouteCtas), dim3(kRouteWarps * 32), 0, static_cast<cudaStream_t>(stream),
+                         static_cast<const bf16*>(x), gate_w, bias, (int)R, (int)K, (int)E, (int)topk, scale, idx, weights,
+                         scores);
+  if (e != cudaSuccess) return cuda_fail("MoeRouteGGUF launch", e);
+  return GGUF_OK;
+}
+
+int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w,
+                            void* out, void* h, float* part, int32_t* meta, int64_t R, int64_t E, int64_t I, int64_t topk,
+                            void* stream) {
+  t_last_error.clear();
+  constexpr int H = 1024;
+  if (!z || !idx || !weights || !fc1_w || !fc2_w || !out || !h || !part || !meta)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: null tensor pointer");
+  const int64_t P = R * topk;
+  if (R < 1 || R > 8 || topk < 1 || P > 128) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: rows must be in [1,8] and rows*topk <= 128");
+  if (I <= 0 || I % 256 != 0 || I > (1 << 20) || E < 1 || E > (1 << 20))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size alignment mismatch (iq2=3 needs I % 256 == 0)");
+  if (!aligned(fc1_w, 16) || !aligned(fc2_w, 16) || !aligned(z, 16) || !aligned(h, 16) || !aligned(part, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: tensors must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  // fc1: h = relu2(z . W1[e]^T), W1 [E, I, H/256*66]
+  {
+    EngineArgs a = {};
+    size_t smem = 0;
+    if ((rc = make_plan<kFmtIQ2>(a, H, H / 256 * 66, 1, true, &smem))) return rc;
+    a.w = static_cast<const uint8_t*>(fc1_w);
+    a.rows = static_cast<int>(I);
+    a.tiles = static_cast<int>((I + 15) / 16);
+    a.x = static_cast<const bf16*>(z);
+    a.R = static_cast<int>(R);
+    a.y = h;
+    a.post = 1.0f;
+    a.idx = idx;
+    a.topk = static_cast<int>(topk);
+    a.P = static_cast<int>(P);
+    a.E = static_cast<int>(E);
+    a.meta = meta;
+    static std::atomic<uint64_t> done{0};
+    auto kern = engine_kernel<kFmtIQ2, 1, kKW, kModeMoe1>;
+    if ((rc = ensure_smem(kern, smem, done))) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(P * a.tiles, sms));
+    cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify fc1 launch", e);
+  }
+  // fc2: part = h . W2[e]^T, W2 [E, H, I/256*66]
+  {
+    EngineArgs a = {};
+    size_t smem = 0;
+    if ((rc = make_plan<kFmtIQ2>(a, static_cast<int>(I), static_cast<int>(I / 256 * 66), 1, true, &smem))) return rc;
+    a.w = static_cast<const uint8_t*>(fc2_w);
+    a.rows = H;
+    a.tiles = H / 16;
+    a.x = static_cast<const bf16*>(h);
+    a.R = static_cast<int>(R);
+    a.y = part;
+    a.post = 1.0f;
+    a.idx = idx;
+    a.topk = static_cast<int>(topk);
+    a.P = static_cast<int>(P);
+    a.E = static_cast<int>(E);
+    a.meta = meta;
+    static std::atomic<uint64_t> done{0};
+    auto kern = engine_kernel<kFmtIQ2, 1, kKW, kModeMoe2>;
+    if ((rc = ensure_smem(kern, smem, done))) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(P * a.tiles, sms));
+    cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify fc2 launch", e);
+  }
+  cudaError_t e = launch(moe_finalize_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, s, static_cast<const float*>(part),
+                         weights, idx, static_cast<int>(topk), H, static_cast<int>(E), static_cast<bf16*>(out));
+  if (e != cudaSuccess) return cuda_fail("MoeVerify finalize launch", e);
+  return GGUF_OK;
+}
+
+int gguf_dequantize(int type, const void* w, float* out, int64_t rows, int64_t K, void* stream) {
+  t_last_error.clear();
+  if (!w || !out || rows < 0 || K <= 0) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize: bad arguments");
+  if (!aligned(w, 4)) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize: w must be 4-byte aligned");
+  if (rows == 0) return GGUF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t groups = rows * (K / 32);
+  const dim3 grid(static_cast<unsigned>((groups + 255) / 256));
+  cudaError_t e;
+  switch (type) {
+    case GGUF_TYPE_Q8_0:
+      if (K % 32) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize Q8_0: K % 32 != 0");
+      e = launch(dequant_kernel<kFmtQ8>, grid, dim3(256), 0, s, static_cast<const uint8_t*>(w), out, rows, (int)K, (int)(K / 32 * 34));
+      break;
+    case GGUF_TYPE_IQ2_XXS:
+      if (K % 256) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize IQ2_XXS: K % 256 != 0");
+      e = launch(dequant_kernel<kFmtIQ2>, grid, dim3(256), 0, s, static_cast<const uint8_t*>(w), out, rows, (int)K, (int)(K / 256 * 66));
+      break;
+    case GGUF_TYPE_NVFP4:
+      if (K % 64) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize NVFP4: K % 64 != 0");
+      e = launch(dequant_kernel<kFmtFP4>, grid, dim3(256), 0, s, static_cast<const uint8_t*>(w), out, rows, (int)K, (int)(K / 64 * 36));
+      break;
+    default:
+      return fail(GGUF_ERR_NOT_IMPLEMENTED, "dequantize: unsupported GGUF type");
+  }
+  if (e != cudaSuccess) return cuda_fail("dequantize launch", e);
+  return GGUF_OK;
+}
+
+int gguf_device_status(int* device_error_site) {
+  t_last_error.clear();
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail("cudaDeviceSynchronize", e);
+  int err = 0, site = 0, zero = 0;
+  if ((e = cudaMemcpyFromSymbol(&err, g_dev_error, sizeof(int))) != cudaSuccess) return cuda_fail("status read", e);
+  if ((e = cudaMemcpyFromSymbol(&site, g_dev_error_site, sizeof(int))) != cudaSuccess) return cuda_fail("status read", e);
+  if ((e = cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int))) != cudaSuccess) return cuda_fail("status clear", e);
+  if ((e = cudaMemcpyToSymbol(g_dev_error_site, &zero, sizeof(int))) != cudaSuccess) return cuda_fail("status clear", e);
+  if (device_error_site) *device_error_site = site;
+  return err ? GGUF_ERR_DEVICE : GGUF_OK;
+}
+
+}  // extern "C"

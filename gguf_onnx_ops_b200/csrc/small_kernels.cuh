@@ -1,0 +1,225 @@
+// Router (MoeRouteGGUF), MoE finalize and dequantise kernels.
+#pragma once
+
+#include "decode.cuh"
+
+namespace gguf_b200 {
+
+// ---------------------------------------------------------------------------------------------
+// MoeRouteGGUF: one thread-block cluster of kRouteCtas CTAs per block of kRouteRows rows.
+// CTA c of a cluster computes the sigmoid scores of experts [c*E/n, (c+1)*E/n) for the cluster's
+// rows (gate row read once from HBM, rounded to bf16 in registers as src/bolt_ops.cu:441-448;
+// fp32 dot products in a fixed order), writes them to `scores`, then the cluster barrier
+// (release/acquire at cluster scope) makes every CTA's scores visible to the whole cluster and
+// warp w of CTA c selects the top-k of row (cluster row base + c*warps + w): iterative arg-max of
+// score + bias with ties to the lower expert index (src/bolt_ops.cu:459-510).
+// ---------------------------------------------------------------------------------------------
+constexpr int kRouteCtas = 8, kRouteRows = 8, kRouteWarps = 8;
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+__global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps * 32)
+    route_kernel(const bf16* __restrict__ x, const float* __restrict__ gw, const float* __restrict__ bias, int R, int K,
+                 int E, int topk, float scale, int32_t* __restrict__ idx_out, float* __restrict__ w_out,
+                 float* __restrict__ scores) {
+  const int cluster = blockIdx.x / kRouteCtas, rank = blockIdx.x % kRouteCtas;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = cluster * kRouteRows;
+  const int nrows = min(kRouteRows, R - row0);
+  const int e_lo = (rank * E) / kRouteCtas, e_hi = ((rank + 1) * E) / kRouteCtas;
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int e = e_lo + warp; e < e_hi; e += kRouteWarps) {
+    const float* wr = gw + static_cast<int64_t>(e) * K;
+    float acc[kRouteRows];
+#pragma unroll
+    for (int r = 0; r < kRouteRows; ++r) acc[r] = 0.f;
+    for (int k = lane * 8; k < K; k += 256) {
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(wr + k));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(wr + k + 4));
+      const float wb[8] = {round_bf16(w0.x), round_bf16(w0.y), round_bf16(w0.z), round_bf16(w0.w),
+                           round_bf16(w1.x), round_bf16(w1.y), round_bf16(w1.z), round_bf16(w1.w)};
+#pragma unroll
+      for (int r = 0; r < kRouteRows; ++r) {
+        if (r < nrows) {
+          const uint4 xv = ldg128(x + static_cast<int64_t>(row0 + r) * K + k);
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[r] = fmaf(bf16_lo(xw[i]), wb[2 * i], acc[r]);
+            acc[r] = fmaf(bf16_hi(xw[i]), wb[2 * i + 1], acc[r]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRouteRows; ++r) {
+      float v = acc[r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && r < nrows) scores[static_cast<int64_t>(row0 + r) * E + e] = 1.0f / (1.0f + expf(-v));
+    }
+  }
+  cluster_sync_all();
+  const int r = rank * kRouteWarps + warp;  // kRouteCtas * kRouteWarps >= kRouteRows
+  if (r >= nrows) return;
+  const int row = row0 + r;
+  const float* sr = scores + static_cast<int64_t>(row) * E;
+  float val[16], sc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      sc[i] = __ldcg(sr + e);
+      val[i] = sc[i] + __ldg(bias + e);
+    } else {
+      sc[i] = 0.f;
+      val[i] = -INFINITY;
+    }
+  }
+  int my_idx = -1;
+  float my_sc = 0.f, sum = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    float bv = -INFINITY, bs = 0.f;
+    int bi = -1;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (val[i] > bv) {  // ascending expert order within the lane: first max wins
+        bv = val[i];
+        bs = sc[i];
+        bi = lane + 32 * i;
+      }
+    float wv = bv;
+    int wi = bi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+      if (oi >= 0 && (wi < 0 || ov > wv || (ov == wv && oi < wi))) {
+        wv = ov;
+        wi = oi;
+      }
+    }
+    const float s = wi >= 0 ? __shfl_sync(0xffffffffu, bs, wi & 31) : 0.f;
+    if (wi >= 0 && (wi & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i == (wi >> 5)) val[i] = -INFINITY;
+    }
+    if (lane == j) {
+      my_idx = wi;
+      my_sc = s;
+    }
+    sum += s;
+  }
+  const float denom = sum + 1e-20f;
+  if (lane < topk) {
+    idx_out[static_cast<int64_t>(row) * topk + lane] = my_idx;
+    w_out[static_cast<int64_t>(row) * topk + lane] = my_sc / denom * scale;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// MoeVerify finalize: out[t, n] = bf16(sum_j w[t, j] * part[t*topk + j, n]), f32, j ascending
+// (src/bolt_ops.cu:627-662).  Pairs whose expert id is out of range contribute nothing.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ part, const float* __restrict__ w,
+                                                           const int32_t* __restrict__ idx, int topk, int H, int E,
+                                                           bf16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x;
+  for (int v = threadIdx.x; v < H / 4; v += blockDim.x) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int k = 0; k < topk; ++k) {
+      const int p = t * topk + k;
+      const int e = __ldg(idx + p);
+      if (e < 0 || e >= E) continue;
+      const float wk = __ldg(w + p);
+      const float4 pv = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(p) * H) + v);
+      a0 += wk * pv.x;
+      a1 += wk * pv.y;
+      a2 += wk * pv.z;
+      a3 += wk * pv.w;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(a0, a1);
+    o.y = pack_bf16x2(a2, a3);
+    reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * H)[v] = o;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Dequantise: one thread per (row, k-group); emulates the four quad lanes of the engine with the
+// same decoders, then applies the post-MMA scale in fp32 (bit-identical to gguf-py).
+// ---------------------------------------------------------------------------------------------
+template <int F>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ w, float* __restrict__ out,
+                                                      int64_t rows, int K, int row_bytes) {
+  const int G = K / 32;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid >= rows * G) return;
+  const int64_t row = gid / G;
+  const int grp = static_cast<int>(gid % G);
+  // base = the weight tensor (16-byte aligned); offsets are absolute byte offsets.
+  const uint32_t row_off = 0;
+  const uint8_t* base = w + row * row_bytes;  // row starts are 2-byte aligned: realign below
+  const uint8_t* abase = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(base) & ~uintptr_t(3));
+  const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(base) & 3);
+  float* o = out + row * K + grp * 32;
+  (void)row_off;
+  if constexpr (F == kFmtQ8) {
+    for (int t = 0; t < 4; ++t) {
+      uint32_t a[4];
+      float d;
+      q8_decode_row(abase, mis, grp, t, a, d);
+      o[4 * t + 0] = bf16_lo(a[0]) * d;
+      o[4 * t + 1] = bf16_hi(a[0]) * d;
+      o[4 * t + 2] = bf16_lo(a[1]) * d;
+      o[4 * t + 3] = bf16_hi(a[1]) * d;
+      o[16 + 4 * t + 0] = bf16_lo(a[2]) * d;
+      o[16 + 4 * t + 1] = bf16_hi(a[2]) * d;
+      o[16 + 4 * t + 2] = bf16_lo(a[3]) * d;
+      o[16 + 4 * t + 3] = bf16_hi(a[3]) * d;
+    }
+  } else if constexpr (F == kFmtIQ2) {
+    const uint32_t sbo = mis + static_cast<uint32_t>(grp >> 3) * 66u;
+    const uint2 q = ld_u64_a2(abase, sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u);
+    const float d = fp16_bits_to_f32(ld_u16(abase, sbo));
+    const float db = iq2_db(d, q.y);
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t gi = (q.x >> (8 * t)) & 0xFFu;
+      const uint4 mag = __ldg(reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[gi][0]));
+      uint32_t a[4];
+      iq2_apply_signs(mag, q.y, 7u * t, a);
+      for (int p = 0; p < 4; ++p) {
+        o[8 * t + 2 * p] = bf16_lo(a[p]) * db;
+        o[8 * t + 2 * p + 1] = bf16_hi(a[p]) * db;
+      }
+    }
+  } else {
+    const uint32_t bo = mis + static_cast<uint32_t>(grp >> 1) * 36u;
+    const uint32_t h2 = static_cast<uint32_t>(grp & 1) * 2u;
+    const uint32_t sc = ld_u16(abase, bo + h2);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const uint32_t S = fp4_scale_bf16_bits((sc >> (8 * s2)) & 0xFFu);
+      const uint32_t Sx2 = S | (S << 16);
+      for (int t = 0; t < 4; ++t) {
+        const uint32_t v = ld_u16(abase, bo + 4u + (h2 + s2) * 8u + 2u * t);
+        uint32_t lo, hi;
+        fp4_patterns(v, lo, hi);
+        lo = hmul2_bits(lo, Sx2);
+        hi = hmul2_bits(hi, Sx2);
+        float* os = o + 16 * s2;
+        os[2 * t] = bf16_lo(lo) * 65536.0f;
+        os[2 * t + 1] = bf16_hi(lo) * 65536.0f;
+        os[8 + 2 * t] = bf16_lo(hi) * 65536.0f;
+        os[8 + 2 * t + 1] = bf16_hi(hi) * 65536.0f;
+      }
+    }
+  }
+}
+
+}  // namespace gguf_b200

@@ -1,0 +1,191 @@
+"""Host-side mirror of the reference's ONNX Runtime custom-op interface for the hot path.
+
+Each function takes the op's inputs (torch CUDA tensors, ``None`` for an omitted optional input
+``""``) and attributes, validates them with the reference's constraints and messages, allocates
+the outputs with the reference's shapes (as ``KernelContext::GetOutput`` would) and calls the
+C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
+
+    Q8Gemv(x, w, scales=None, gguf=1)                  -> y        src/bolt_ops.cu:1592-1643, :2018-2027
+    Q4Gemv(x, w, scales=None, iq2=3)                   -> y        src/bolt_ops.cu:1592-1643, :2028-2037
+    Nvfp4Gemv(x, w, w_scale, gscale, gguf=1)           -> y        src/bolt_ops.cu:1411-1469, :2004-2016
+    MoeRouteGGUF(x, gate_w, bias, topk, scale)         -> idx, weights, scores    src/bolt_ops.cu:512-546
+    MoeVerify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s=None, topk, iq2=3) -> out, h, part, meta
+                                                                   src/bolt_ops.cu:1327-1409, :1981-1996
+
+Only the GGUF layouts are implemented (``gguf=1`` / ``iq2=3``); the legacy layouts raise
+NotImplementedError.  The lower-level ``*_into`` functions write into caller-provided outputs
+(no allocation), for graph capture and benchmarking.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, load
+
+Q8_0_BYTES, IQ2_XXS_BYTES, NVFP4_BYTES = 34, 66, 36
+
+
+def _stream(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need(t, name, dtype, op):
+    if t is None:
+        raise ValueError(f"{op}: Missing required tensor input {name}")
+    if not t.is_cuda:
+        raise ValueError(f"{op}: {name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{op}: {name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{op}: {name} must be contiguous")
+
+
+# ------------------------------------------------------------------------------------------------
+# GEMVs
+# ------------------------------------------------------------------------------------------------
+def q8_0_gemv_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, R: int, N: int, K: int, stream=None) -> None:
+    check(load().gguf_q8_0_gemv(_ptr(x), _ptr(w), _ptr(y), R, N, K, _stream(stream)))
+
+
+def iq2_xxs_gemv_into(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, R: int, N: int, K: int, stream=None) -> None:
+    check(load().gguf_iq2_xxs_gemv(_ptr(x), _ptr(w), _ptr(y), R, N, K, _stream(stream)))
+
+
+def nvfp4_gemv_into(x, w, gscale, y, R: int, N: int, K: int, stream=None) -> None:
+    check(load().gguf_nvfp4_gemv(_ptr(x), _ptr(w), _ptr(gscale), _ptr(y), R, N, K, _stream(stream)))
+
+
+def _gemv_shapes(x: torch.Tensor, w: torch.Tensor):
+    K = x.shape[-1]
+    R = x.numel() // K if K else 0
+    N = w.shape[0]
+    return R, N, K
+
+
+def Q8Gemv(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor | None = None, gguf: int = 1) -> torch.Tensor:
+    """y[..., N] = x[..., K] @ deq(W)^T with raw GGUF Q8_0 blocks W [N, (K/32)*34]."""
+    if gguf != 1:
+        raise NotImplementedError("Q8Gemv: only the raw GGUF Q8_0 layout (gguf=1) is implemented")
+    _need(x, "x", torch.bfloat16, "Q8Gemv")
+    _need(w, "w", torch.uint8, "Q8Gemv")
+    R, N, K = _gemv_shapes(x, w)
+    if K % 64 != 0 or w.numel() != N * (K // 32) * Q8_0_BYTES or R < 1 or R > 16:
+        raise ValueError("Q8Gemv gguf=1: needs B [N, (K/32)*34] and 1..16 rows")
+    y = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    q8_0_gemv_into(x, w, y, R, N, K)
+    return y
+
+
+def Q4Gemv(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor | None = None, iq2: int = 3) -> torch.Tensor:
+    """y[..., N] = x[..., K] @ deq(W)^T with raw GGUF IQ2_XXS super-blocks W [N, (K/256)*66]."""
+    if iq2 != 3:
+        raise NotImplementedError("Q4Gemv: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented")
+    _need(x, "x", torch.bfloat16, "Q4Gemv")
+    _need(w, "w", torch.uint8, "Q4Gemv")
+    R, N, K = _gemv_shapes(x, w)
+    if K % 256 != 0 or w.numel() != N * (K // 256) * IQ2_XXS_BYTES or R < 1 or R > 16:
+        raise ValueError("Q4Gemv iq2=3: needs B [N, (K/256)*66] and 1..16 rows")
+    y = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    iq2_xxs_gemv_into(x, w, y, R, N, K)
+    return y
+
+
+def Nvfp4Gemv(x: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor | None, gscale: torch.Tensor,
+              gguf: int = 1) -> torch.Tensor:
+    """y[..., N] = gscale * (x[..., K] @ deq(W)^T) with raw GGUF NVFP4 blocks W [N, (K/64)*36]."""
+    if gguf != 1:
+        raise NotImplementedError("Nvfp4Gemv: only the raw GGUF NVFP4 layout (gguf=1) is implemented")
+    _need(x, "x", torch.bfloat16, "Nvfp4Gemv")
+    _need(w, "w", torch.uint8, "Nvfp4Gemv")
+    _need(gscale, "gscale", torch.float32, "Nvfp4Gemv")
+    R, N, K = _gemv_shapes(x, w)
+    if K % 64 != 0 or w.numel() != N * (K // 64) * NVFP4_BYTES or R < 1 or R > 16:
+        raise ValueError("Nvfp4Gemv gguf=1: needs w [N, (K/64)*36] and 1..16 rows")
+    y = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    nvfp4_gemv_into(x, w, gscale, y, R, N, K)
+    return y
+
+
+# ------------------------------------------------------------------------------------------------
+# Router + MoE
+# ------------------------------------------------------------------------------------------------
+def moe_route_into(x, gate_w, bias, idx, weights, scores, R, K, E, topk, scale, stream=None) -> None:
+    check(load().gguf_moe_route(_ptr(x), _ptr(gate_w), _ptr(bias), _ptr(idx), _ptr(weights), _ptr(scores),
+                                R, K, E, topk, float(scale), _stream(stream)))
+
+
+def MoeRouteGGUF(x: torch.Tensor, gate_w: torch.Tensor, bias: torch.Tensor, topk: int, scale: float):
+    """Sigmoid router with F32 GGUF gate weights (rounded to bf16) and bias-corrected top-k."""
+    _need(x, "x", torch.bfloat16, "MoeRouteGGUF")
+    _need(gate_w, "gate_w", torch.float32, "MoeRouteGGUF")
+    _need(bias, "bias", torch.float32, "MoeRouteGGUF")
+    R, K = x.shape
+    E = gate_w.shape[0]
+    if E > 512 or K % 256 != 0 or topk > 32 or gate_w.shape[1] != K or bias.numel() != E:
+        raise ValueError("MoeRoute: unsupported shape")
+    idx = torch.empty(R, topk, dtype=torch.int32, device=x.device)
+    wts = torch.empty(R, topk, dtype=torch.float32, device=x.device)
+    scores = torch.empty(R, E, dtype=torch.float32, device=x.device)
+    moe_route_into(x, gate_w, bias, idx, wts, scores, R, K, E, topk, scale)
+    return idx, wts, scores
+
+
+def moe_verify_into(z, idx, w, fc1_w, fc2_w, out, h, part, meta, R, E, I, topk, stream=None) -> None:
+    check(load().gguf_moe_verify_iq2_xxs(_ptr(z), _ptr(idx), _ptr(w), _ptr(fc1_w), _ptr(fc2_w), _ptr(out), _ptr(h),
+                                         _ptr(part), _ptr(meta), R, E, I, topk, _stream(stream)))
+
+
+def MoeVerify(z, idx, w, fc1_w, fc1_s=None, fc2_w=None, fc2_s=None, *, topk: int, iq2: int = 3):
+    """Expert-grouped relu^2 MoE over raw GGUF IQ2_XXS expert tensors (iq2=3).
+
+    Returns (out [R,1024] bf16, h [R*topk, I] bf16, part [R*topk, 1024] f32, meta [1 + 9*R*topk] i32).
+    """
+    if iq2 != 3:
+        raise NotImplementedError("MoeVerify: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented")
+    _need(z, "z", torch.bfloat16, "MoeVerify")
+    _need(idx, "idx", torch.int32, "MoeVerify")
+    _need(w, "weights", torch.float32, "MoeVerify")
+    _need(fc1_w, "fc1_w", torch.uint8, "MoeVerify")
+    _need(fc2_w, "fc2_w", torch.uint8, "MoeVerify")
+    R = z.shape[0]
+    P = R * topk
+    if R < 1 or R > 8 or P > 128:
+        raise ValueError("MoeVerify: rows must be in [1,8] and rows*topk <= 128")
+    if z.shape[1] != 1024:
+        raise ValueError("MoeVerify: latent size must be 1024")
+    E, I = fc1_w.shape[0], fc1_w.shape[1]
+    if I % 256 != 0 or fc1_w.numel() != E * I * (1024 // 256) * IQ2_XXS_BYTES \
+            or fc2_w.numel() != E * 1024 * (I // 256) * IQ2_XXS_BYTES:
+        raise ValueError("MoeVerify: inter size alignment mismatch")
+    out = torch.empty(R, 1024, dtype=torch.bfloat16, device=z.device)
+    h = torch.empty(P, I, dtype=torch.bfloat16, device=z.device)
+    part = torch.empty(P, 1024, dtype=torch.float32, device=z.device)
+    meta = torch.empty(1 + P + P * 8, dtype=torch.int32, device=z.device)
+    moe_verify_into(z, idx, w, fc1_w, fc2_w, out, h, part, meta, R, E, I, topk)
+    return out, h, part, meta
+
+
+# ------------------------------------------------------------------------------------------------
+# Debug / parity
+# ------------------------------------------------------------------------------------------------
+def dequantize(w: torch.Tensor, gguf_type: int, K: int) -> torch.Tensor:
+    """Raw GGUF rows [rows, row_bytes] -> f32 [rows, K] with the GEMV's device decoders."""
+    rows = w.shape[0]
+    out = torch.empty(rows, K, dtype=torch.float32, device=w.device)
+    check(load().gguf_dequantize(gguf_type, _ptr(w), _ptr(out), rows, K, _stream()))
+    return out
+
+
+def set_pdl(enable: bool) -> None:
+    load().gguf_set_pdl(1 if enable else 0)
+
+
+def device_status():
+    return _lib.device_status()

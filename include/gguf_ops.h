@@ -1,0 +1,120 @@
+/*
+ * gguf_ops.h -- C ABI of libgguf_onnx_ops.so, the B200 (sm_100a) implementation of the decode-time
+ * GGUF GEMV / MoE hot path of tianleiwu/gguf_onnx_ops.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream (cudaStream_t passed as
+ * void*), enqueues its kernels on that stream, never synchronises, never allocates device
+ * memory and returns a status code (0 = success).  On failure, gguf_last_error() returns a
+ * thread-local message naming the op and the violated constraint, in the style of the
+ * reference's ORT error strings.  These are the functions that the ONNX Runtime custom-op shim
+ * (RegisterCustomOps, gguf_onnx_ops_b200/csrc/ort_ops.cc) calls from each op's ComputeV2, with the
+ * ORT tensors' data pointers and KernelContext_GetGPUComputeStream.
+ *
+ * Tensor conventions (identical to the reference ops):
+ *   activations : bf16, row-major [R, K] (R = number of flattened leading rows)
+ *   weights     : raw GGUF bytes, row-major [N, (K / block) * type_size], 16-byte aligned base
+ *   outputs     : bf16 [R, N]
+ */
+#ifndef GGUF_OPS_H_
+#define GGUF_OPS_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GGUF_OPS_API __attribute__((visibility("default")))
+
+/* Status codes. */
+enum {
+  GGUF_OK = 0,
+  GGUF_ERR_INVALID_ARGUMENT = 1, /* shape / attribute / alignment contract violated (ORT_INVALID_ARGUMENT / ORT_FAIL) */
+  GGUF_ERR_CUDA = 2,             /* a CUDA launch or runtime call failed */
+  GGUF_ERR_NOT_IMPLEMENTED = 3,  /* legacy (non-GGUF) layout requested */
+  GGUF_ERR_DEVICE = 4            /* a kernel reported a device-side error (bounded wait expired) */
+};
+
+/* GGUF tensor type ids (ggml numbering, docs/GGUF_ONNX_Custom_Ops.md:13-18). */
+enum { GGUF_TYPE_Q8_0 = 8, GGUF_TYPE_IQ2_XXS = 16, GGUF_TYPE_NVFP4 = 40 };
+
+/* Library version string. */
+GGUF_OPS_API const char* gguf_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+GGUF_OPS_API const char* gguf_last_error(void);
+
+/*
+ * Q8Gemv, gguf=1:  y[R,N] = x[R,K] @ deq(W)^T,  W raw Q8_0 [N, (K/32)*34].
+ * Replaces QGemvState<8>::ComputeV2 gguf=1 branch (src/bolt_ops.cu:1614-1616, :1629-1630).
+ * Contract: K % 64 == 0, 1 <= R <= 16 (the reference accepts 1..8; 9..16 is a strict superset).
+ */
+GGUF_OPS_API int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K,
+                                void* stream);
+
+/*
+ * Q4Gemv, iq2=3:  y[R,N] = x[R,K] @ deq(W)^T,  W raw IQ2_XXS [N, (K/256)*66].
+ * Replaces QGemvState<4>::ComputeV2 iq2=3 branch (src/bolt_ops.cu:1608-1610, :1623-1624).
+ * Contract: K % 256 == 0, 1 <= R <= 16.
+ */
+GGUF_OPS_API int gguf_iq2_xxs_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K,
+                                   void* stream);
+
+/*
+ * Nvfp4Gemv, gguf=1:  y[R,N] = gscale[0] * (x[R,K] @ deq(W)^T),  W raw NVFP4 [N, (K/64)*36],
+ * gscale: device f32 [1].
+ * Replaces Nvfp4GemvState::ComputeV2 gguf=1 branch (src/bolt_ops.cu:1424-1433).
+ * Contract: K % 64 == 0, 1 <= R <= 16.  Scale bytes decode as gguf-py's unsigned E4M3 (bit 7
+ * ignored, 0x00 and 0x7F -> 0).
+ */
+GGUF_OPS_API int gguf_nvfp4_gemv(const void* x, const void* w, const float* gscale, void* y, int64_t R, int64_t N,
+                                 int64_t K, void* stream);
+
+/*
+ * MoeRouteGGUF:  scores[R,E] = sigmoid(x[R,K] @ bf16(gate_w)^T);  idx[R,topk] = top-k of scores + bias
+ * (descending, ties to the lower expert index);  weights = s_sel / (sum s_sel + 1e-20) * scale.
+ * x bf16 [R,K]; gate_w f32 [E,K]; bias f32 [E] -> idx i32 [R,topk], weights f32 [R,topk], scores f32 [R,E].
+ * Replaces MoeRouteStateT<float>::ComputeV2 (src/bolt_ops.cu:512-546).
+ * Contract: E <= 512, K % 256 == 0, 1 <= topk <= 32, topk <= E, R >= 1.
+ */
+GGUF_OPS_API int gguf_moe_route(const void* x, const float* gate_w, const float* bias, int32_t* idx, float* weights,
+                                float* scores, int64_t R, int64_t K, int64_t E, int64_t topk, float scale,
+                                void* stream);
+
+/*
+ * MoeVerify, iq2=3 (expert-grouped relu^2 MoE over raw IQ2_XXS expert tensors):
+ *   for each pair p = (t, j), e = idx[t,j]:  h[p] = bf16(relu(bf16(z[t] . W1[e]^T))^2)
+ *                                            part[p] = bf16(h[p] . W2[e]^T)   (stored as f32)
+ *   out[t] = bf16(sum_j weights[t,j] * part[t*topk + j])   (f32 sum, j ascending)
+ * z bf16 [R,1024]; idx i32 [R,topk]; weights f32 [R,topk]; fc1_w u8 [E, I, 4*66]; fc2_w u8 [E, 1024, (I/256)*66]
+ * -> out bf16 [R,1024]; h bf16 [R*topk, I]; part f32 [R*topk, 1024]; meta i32 [1 + 9*R*topk]
+ * (meta[0] = number of unique experts U, meta[1..U] their ids, meta[1+P+u*8+t] = pair of row t for expert u or -1).
+ * Replaces MoeVerifyState::ComputeV2 iq2=3 (src/bolt_ops.cu:1327-1409).
+ * Contract: 1 <= R <= 8, R*topk <= 128, I % 256 == 0, every idx in [0, E).
+ */
+GGUF_OPS_API int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                                         const void* fc2_w, void* out, void* h, float* part, int32_t* meta, int64_t R,
+                                         int64_t E, int64_t I, int64_t topk, void* stream);
+
+/*
+ * Dequantise raw GGUF rows to f32 with the same device decoders the GEMVs use (debug / parity
+ * entry point; no counterpart op in the reference).  type = GGUF_TYPE_*; w [rows, row_bytes(K)];
+ * out f32 [rows, K].  Results are bit-identical to gguf-py 0.19.0 dequantize.
+ */
+GGUF_OPS_API int gguf_dequantize(int type, const void* w, float* out, int64_t rows, int64_t K, void* stream);
+
+/*
+ * Device-side status: returns the first error code recorded by a kernel on the current device
+ * since the last call (0 if none) and clears it.  Synchronises the device; for tests and
+ * diagnostics, not for the hot path.
+ */
+GGUF_OPS_API int gguf_device_status(int* device_error_site);
+
+/* Tuning: enable (1) / disable (0) programmatic dependent launch for subsequent calls (default 1). */
+GGUF_OPS_API void gguf_set_pdl(int enable);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GGUF_OPS_H_ */

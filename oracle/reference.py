@@ -1,0 +1,84 @@
+"""CPU reference computations for the hot-path ops (test infrastructure).
+
+* ``gemv_ref``  -- ``y = x @ deq(W)^T`` (``tests/test_bolt_ops.py:237-238``), accumulated in fp64.
+* ``moe_ref``   -- the per-(row, expert) relu^2 MoE loop (``tests/test_bolt_ops.py:253-259``) with
+  the op's bf16 rounding points: h = bf16(z.W1), h = bf16(relu(h)^2), p = bf16(h.W2),
+  out = bf16(sum_j w_j p_j) with the sum in fp32 over j ascending (``src/bolt_ops.cu:627-662``).
+* ``route_ref`` -- sigmoid router with bf16-rounded gate weights (``src/bolt_ops.cu:399-404``),
+  bias-corrected top-k with ties to the lower index (``src/bolt_ops.cu:489``), weights
+  ``s / (sum s + 1e-20) * scale`` (``src/bolt_ops.cu:505-508``); logits in fp64.
+* ``rel_l2``    -- the reference's metric ``||a-b|| / ||b||`` (``tests/test_bolt_ops.py:62-64``).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .quants import bf16_round, bf16_to_f32
+
+
+def rel_l2(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-12))
+
+
+def _x_f32(x) -> np.ndarray:
+    x = np.asarray(x)
+    if x.dtype == np.uint16:  # bf16 bit patterns
+        return bf16_to_f32(x)
+    return x.astype(np.float32)
+
+
+def gemv_ref(x, w_deq: np.ndarray) -> np.ndarray:
+    """x: [R, K] (bf16 bits as uint16, or float); w_deq: fp32 [N, K] -> fp64 [R, N]."""
+    return _x_f32(x).astype(np.float64) @ np.asarray(w_deq, dtype=np.float64).T
+
+
+def moe_ref(z, idx: np.ndarray, w: np.ndarray, d1: np.ndarray, d2: np.ndarray):
+    """z: [R, H] bf16 bits; idx: [R, k] int32; w: [R, k] fp32; d1: fp32 [E, I, H]; d2: fp32 [E, H, I].
+
+    Returns (out_f32 [R, H] before the final bf16 rounding, h [R*k, I] fp32 holding bf16 values,
+    part [R*k, H] fp32 holding bf16 values).  Only the experts referenced by idx are touched.
+    """
+    zf = _x_f32(z).astype(np.float64)
+    R, k = idx.shape
+    H = zf.shape[1]
+    I = d1.shape[1]
+    out = np.zeros((R, H), dtype=np.float32)
+    h_all = np.zeros((R * k, I), dtype=np.float32)
+    p_all = np.zeros((R * k, H), dtype=np.float32)
+    for t in range(R):
+        for j in range(k):
+            e = int(idx[t, j])
+            h = bf16_round((zf[t] @ d1[e].astype(np.float64).T).astype(np.float32))
+            h = bf16_round(np.maximum(h, np.float32(0)) ** 2)
+            p = bf16_round((h.astype(np.float64) @ d2[e].astype(np.float64).T).astype(np.float32))
+            out[t] += np.float32(w[t, j]) * p
+            h_all[t * k + j] = h
+            p_all[t * k + j] = p
+    return out, h_all, p_all
+
+
+def route_ref(x, gate_w: np.ndarray, bias: np.ndarray, topk: int, scale: float, tie_eps: float = 1e-6):
+    """x: [R, K] bf16 bits; gate_w: fp32 [E, K]; bias: fp32 [E].
+
+    Returns (idx [R, topk] int32, weights [R, topk] fp64, scores [R, E] fp64, near_tie [R] bool).
+    ``near_tie[r]`` marks rows whose k-th and (k+1)-th bias-corrected scores are closer than
+    ``tie_eps``; their index set may legitimately differ under a different fp32 summation order.
+    """
+    xf = _x_f32(x).astype(np.float64)
+    gw = bf16_round(np.asarray(gate_w, dtype=np.float32)).astype(np.float64)
+    logits = xf @ gw.T
+    scores = 1.0 / (1.0 + np.exp(-logits))
+    val = scores + np.asarray(bias, dtype=np.float32).astype(np.float64)[None, :]
+    R, E = val.shape
+    order = np.lexsort((np.broadcast_to(np.arange(E), (R, E)), -val), axis=1)  # desc value, asc index
+    idx = order[:, :topk].astype(np.int32)
+    sel = np.take_along_axis(scores, idx, axis=1)
+    weights = sel / (sel.sum(axis=1, keepdims=True) + 1e-20) * scale
+    near = np.zeros(R, dtype=bool)
+    if topk < E:
+        vs = np.take_along_axis(val, order, axis=1)
+        near = (vs[:, topk - 1] - vs[:, topk]) < tie_eps
+    return idx, weights, scores, near

@@ -1,0 +1,135 @@
+"""Generate the committed golden fixtures in tests/golden/ (run in the build container only).
+
+Every expected value here comes from the reference's own CPU path, not from the repo's oracle:
+
+* dequantised weights: ``gguf.quants.dequantize`` of gguf-py 0.19.0, the call the reference's test
+  harness makes (tests/test_bolt_ops.py:225-230);
+* GEMV outputs: that dequantisation followed by a torch fp32 ``x.float() @ deq.T``
+  (tests/test_bolt_ops.py:237-238);
+* MoE outputs: the reference harness's per-(row, expert) loop (tests/test_bolt_ops.py:253-259) on
+  gguf-py dequantised experts (kept in fp32: the repo's kernels consume the exact weights);
+* router outputs: the harness's torch router (tests/test_bolt_ops.py:116-119) on bf16-rounded gate
+  weights, as MoeRouteGGUF specifies (src/bolt_ops.cu:441-448);
+* the IQ2_XXS codebook: parsed from the reference's src/iq2xxs_grid.h (kIq2xxsGrid, line 6, and
+  kIq2xxsGridBf16, line 75).
+
+Inputs use the reference test builders (iq2_native_blocks, the Q8 block builder, the NVFP4 block
+builder of tests/test_bolt_ops.py:210-215, :290-294, :274-275) with numpy RNG, plus the BASELINE
+config distributions at reduced sizes.
+
+    python tests/golden/make_golden.py [--reference /root/reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import re
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from oracle import inputs as I  # noqa: E402  (input builders only; expected values come from gguf/torch)
+from tests.golden.cases import GEMV_CASES, moe_inputs, route_inputs, sha  # noqa: E402
+
+
+def gguf_deq(raw: np.ndarray, qt) -> np.ndarray:
+    from gguf import quants
+
+    return np.asarray(quants.dequantize(np.ascontiguousarray(raw), qt), dtype=np.float32).reshape(raw.shape[0], -1)
+
+
+def bf16_tensor(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16)
+
+
+def parse_reference_grid(ref: str):
+    src = open(os.path.join(ref, "src", "iq2xxs_grid.h")).read()
+    u64 = re.search(r"kIq2xxsGrid\[256\]\s*=\s*\{(.*?)\};", src, re.S).group(1)
+    grid64 = np.array([int(v, 16) for v in re.findall(r"0x([0-9a-fA-F]+)", u64)], dtype=np.uint64)
+    b16 = re.search(r"kIq2xxsGridBf16\[256\]\[4\]\s*=\s*\{(.*)\};", src, re.S).group(1)
+    gridbf = np.array([int(v, 16) for v in re.findall(r"0x([0-9a-fA-F]+)u", b16)], dtype=np.uint32).reshape(256, 4)
+    assert grid64.size == 256
+    return grid64, gridbf
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    from gguf import GGMLQuantizationType as Q
+
+    # 1. IQ2_XXS codebook of the reference
+    g64, gbf = parse_reference_grid(args.reference)
+    np.savez_compressed(os.path.join(HERE, "iq2xxs_grid.npz"), grid_u64=g64, grid_bf16x2=gbf)
+
+    # 2. dequantisation goldens (reference test builders)
+    g = I.rng(1001)
+    q8 = I.q8_test_blocks(g, 24, 1024)
+    iq2 = I.iq2_test_blocks(g, (24,), 1024)
+    fp4 = g.integers(0, 256, size=(24, 1024 // 64, 36), dtype=np.uint8)
+    fp4[:, :, :4] = g.integers(0x30, 0x48, size=(24, 1024 // 64, 4), dtype=np.uint8)  # tests/test_bolt_ops.py:275
+    fp4 = fp4.reshape(24, -1)
+    fp4_all = np.zeros((4, 1024 // 64, 36), dtype=np.uint8)  # every scale byte 0..255, every nibble
+    fp4_all[:, :, 4:] = g.integers(0, 256, size=(4, 1024 // 64, 32), dtype=np.uint8)
+    fp4_all[:, :, :4] = np.arange(256, dtype=np.uint8).reshape(4, 16, 4)
+    fp4_all = fp4_all.reshape(4, -1)
+    np.savez_compressed(
+        os.path.join(HERE, "dequant.npz"),
+        q8_raw=q8, q8_deq=gguf_deq(q8, Q.Q8_0),
+        iq2_raw=iq2, iq2_deq=gguf_deq(iq2, Q.IQ2_XXS),
+        fp4_raw=fp4, fp4_deq=gguf_deq(fp4, Q.NVFP4),
+        fp4all_raw=fp4_all, fp4all_deq=gguf_deq(fp4_all, Q.NVFP4),
+    )
+
+    # 3. GEMV goldens: x @ gguf_deq(W)^T in torch fp32 (the harness's CPU reference)
+    cases = {}
+    qts = {"q8_0": Q.Q8_0, "iq2_xxs": Q.IQ2_XXS, "nvfp4": Q.NVFP4}
+    for name, (op, R, N, K, seed) in GEMV_CASES.items():
+        x, w, extra = I.gemv_case(op, R, N, K, seed=seed)
+        deq = torch.from_numpy(gguf_deq(w, qts[op]))
+        y = (bf16_tensor(x).float() @ deq.T)
+        if op == "nvfp4":
+            y = y * float(extra["gscale"][0])
+        cases[f"{name}_x"] = x
+        cases[f"{name}_w"] = w
+        cases[f"{name}_y"] = y.numpy()
+    np.savez_compressed(os.path.join(HERE, "gemv.npz"), **cases)
+
+    # 4. router goldens: config C3 shape, and the harness's E=240 topk=9 scale=5 (K reduced to 1024)
+    rcases = {}
+    for name in ("c3", "harness"):
+        x, gw, b, topk, scale = route_inputs(name)
+        sc = (bf16_tensor(x).float() @ torch.from_numpy(gw).bfloat16().float().T).sigmoid()
+        ridx = torch.topk(sc + torch.from_numpy(b), topk, dim=-1)[1]
+        rw = sc.gather(1, ridx)
+        rw = rw / (rw.sum(-1, keepdim=True) + 1e-20) * scale
+        rcases.update({f"{name}_idx": ridx.numpy().astype(np.int32), f"{name}_w": rw.numpy(),
+                       f"{name}_scores": sc.numpy(), f"{name}_sha": np.array(sha(x, gw, b))})
+    np.savez_compressed(os.path.join(HERE, "route.npz"), **rcases)
+
+    # 5. MoE golden: the harness loop (tests/test_bolt_ops.py:253-259) on gguf-py dequantised experts
+    z, idx, wts, b1, b2, (R, E, H, Idim, topk) = moe_inputs()
+    d1 = torch.from_numpy(gguf_deq(b1.reshape(E * Idim, -1), Q.IQ2_XXS).reshape(E, Idim, H))
+    d2 = torch.from_numpy(gguf_deq(b2.reshape(E * H, -1), Q.IQ2_XXS).reshape(E, H, Idim))
+    zt = bf16_tensor(z)
+    ref = torch.zeros(R, H)
+    for t in range(R):
+        for j in range(topk):
+            e = int(idx[t, j])
+            h = (zt[t].float() @ d1[e].T).bfloat16().float()
+            h = (torch.relu(h) ** 2).bfloat16().float()
+            ref[t] += float(wts[t, j]) * (h @ d2[e].T).bfloat16().float()
+    np.savez_compressed(os.path.join(HERE, "moe.npz"), out=ref.numpy(), sha=np.array(sha(z, idx, wts, b1, b2)))
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,107 @@
+"""The C-ABI library: it loads, exports every symbol include/gguf_ops.h declares, and rejects bad
+arguments with the reference's error style -- all without touching a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from gguf_onnx_ops_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gguf_ops.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return re.findall(r"GGUF_OPS_API\s+[\w\s\*]+?\b(gguf_\w+)\s*\(", src)
+
+
+def test_header_declares_the_hot_path():
+    names = set(declared())
+    for n in ("gguf_q8_0_gemv", "gguf_iq2_xxs_gemv", "gguf_nvfp4_gemv", "gguf_moe_route", "gguf_moe_verify_iq2_xxs",
+              "gguf_dequantize", "gguf_last_error", "gguf_device_status"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for n in declared():
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.gguf_version()
+
+
+FAKE = 0x10000  # 16-byte aligned, never dereferenced: validation fails before any CUDA call
+
+
+@pytest.mark.parametrize("fn,args,msg", [
+    ("gguf_q8_0_gemv", (FAKE, FAKE, FAKE, 17, 4096, 4096, None), "Q8Gemv gguf=1"),
+    ("gguf_q8_0_gemv", (FAKE, FAKE, FAKE, 0, 4096, 4096, None), "1..16 rows"),
+    ("gguf_q8_0_gemv", (FAKE, FAKE, FAKE, 1, 4096, 4000, None), "K % 64"),
+    ("gguf_q8_0_gemv", (FAKE + 2, FAKE, FAKE, 1, 4096, 4096, None), "aligned"),
+    ("gguf_q8_0_gemv", (None, FAKE, FAKE, 1, 4096, 4096, None), "null"),
+    ("gguf_iq2_xxs_gemv", (FAKE, FAKE, FAKE, 1, 14336, 4000, None), "Q4Gemv iq2=3"),
+    ("gguf_iq2_xxs_gemv", (FAKE, FAKE, FAKE, 99, 14336, 4096, None), "1..16 rows"),
+    ("gguf_nvfp4_gemv", (FAKE, FAKE, None, FAKE, 1, 1024, 5120, None), "Nvfp4Gemv gguf=1"),
+    ("gguf_nvfp4_gemv", (FAKE, FAKE, FAKE, FAKE, 1, 1024, 5000, None), "K % 64"),
+    ("gguf_moe_route", (FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 8, 1024, 513, 6, 1.0, None), "MoeRoute"),
+    ("gguf_moe_route", (FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 8, 1000, 128, 6, 1.0, None), "K % 256"),
+    ("gguf_moe_route", (FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 8, 1024, 128, 33, 1.0, None), "topk"),
+    ("gguf_moe_verify_iq2_xxs", (FAKE,) * 9 + (9, 128, 1792, 6, None), "rows must be in [1,8]"),
+    ("gguf_moe_verify_iq2_xxs", (FAKE,) * 9 + (8, 128, 1792, 17, None), "rows*topk <= 128"),
+    ("gguf_moe_verify_iq2_xxs", (FAKE,) * 9 + (8, 128, 1800, 6, None), "inter size"),
+])
+def test_invalid_arguments_rejected(lib, fn, args, msg):
+    rc = getattr(lib, fn)(*args)
+    assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT
+    assert msg in lib.gguf_last_error().decode()
+
+
+def test_unknown_dequant_type(lib):
+    assert lib.gguf_dequantize(2, FAKE, FAKE, 4, 64, None) == _lib.GGUF_ERR_NOT_IMPLEMENTED
+
+
+def test_check_raises_typed_errors(lib):
+    lib.gguf_q8_0_gemv(FAKE, FAKE, FAKE, 17, 64, 64, None)
+    with pytest.raises(ValueError, match="Q8Gemv"):
+        _lib.check(_lib.GGUF_ERR_INVALID_ARGUMENT)
+
+
+def test_no_silent_fallback_without_gpu(lib):
+    """Valid arguments on a machine without a usable GPU must fail loudly (CUDA error), never compute."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    rc = lib.gguf_q8_0_gemv(FAKE, FAKE, FAKE, 1, 64, 64, None)
+    assert rc == _lib.GGUF_ERR_CUDA
+    assert lib.gguf_last_error()
+
+
+def test_ops_reject_legacy_layouts():
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    x = torch.zeros(1, 64, dtype=torch.bfloat16)
+    w = torch.zeros(8, 68, dtype=torch.uint8)
+    with pytest.raises(NotImplementedError):
+        ops.Q8Gemv(x, w, gguf=0)
+    with pytest.raises(NotImplementedError):
+        ops.Q4Gemv(x, w, iq2=2)
+    with pytest.raises(NotImplementedError):
+        ops.Nvfp4Gemv(x, w, None, torch.ones(1), gguf=0)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        ops.Q8Gemv(x, w)
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(OSError, match="no CPU fallback"):
+        _lib.load(str(tmp_path / "nope.so"))
+    monkeypatch.setattr(_lib, "_lib", None)
+    ctypes.CDLL  # noqa: B018

@@ -1,0 +1,116 @@
+"""The CPU oracle pinned against the reference's CPU path (gguf-py 0.19.0 + torch), via the committed
+golden fixtures and live gguf-py calls.  No GPU needed."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from oracle import inputs as I
+from tests.golden.cases import GEMV_CASES, moe_inputs, route_inputs, sha
+from tests.util import rel
+
+
+def bits_equal(a, b):
+    return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", ["q8", "iq2", "fp4", "fp4all"])
+def test_dequant_matches_golden(golden, fmt):
+    d = golden("dequant.npz")
+    fn = {"q8": O.dequant_q8_0, "iq2": O.dequant_iq2_xxs, "fp4": O.dequant_nvfp4, "fp4all": O.dequant_nvfp4}[fmt]
+    assert bits_equal(fn(d[f"{fmt}_raw"]), d[f"{fmt}_deq"])
+
+
+def test_dequant_matches_live_gguf():
+    from gguf import GGMLQuantizationType as Q
+    from gguf import quants
+
+    g = I.rng(5)
+    for raw, qt, fn in ((I.q8_0_weights(g, 33, 256), Q.Q8_0, O.dequant_q8_0),
+                        (I.iq2_xxs_weights(g, (17,), 512), Q.IQ2_XXS, O.dequant_iq2_xxs),
+                        (I.nvfp4_weights(g, 9, 320, 0, 255), Q.NVFP4, O.dequant_nvfp4)):
+        ref = np.asarray(quants.dequantize(raw, qt), np.float32).reshape(raw.shape[0], -1)
+        assert bits_equal(fn(raw), ref)
+
+
+def test_quantize_q8_0_matches_gguf():
+    from gguf import GGMLQuantizationType as Q
+    from gguf import quants
+
+    w = (I.rng(6).standard_normal((16, 512)) * 0.02).astype(np.float32)
+    w[3, :32] = 0.0  # all-zero block: d = 0
+    assert np.array_equal(O.quantize_q8_0(w), quants.quantize(w, Q.Q8_0))
+
+
+def test_grid_matches_reference_codebook(golden):
+    g = golden("iq2xxs_grid.npz")
+    ref = g["grid_u64"].astype(np.uint64)
+    ref_bytes = ((ref[:, None] >> (np.arange(8, dtype=np.uint64) * 8)[None, :]) & 0xFF).astype(np.uint8)
+    assert np.array_equal(O.iq2xxs_grid(), ref_bytes)
+
+
+def test_sign_byte_is_ksigns():
+    from gguf.quants import IQ2_XXS
+
+    assert np.array_equal(O.iq2xxs_sign_byte(np.arange(128)), np.frombuffer(IQ2_XXS.ksigns, dtype=np.uint8))
+
+
+def test_ue4m3_table_semantics():
+    t = O.ue4m3_table()
+    assert t[0] == 0 and t[0x7F] == 0 and t[0x80] == 0
+    assert t[0x38] == 0.5  # e4m3 1.0, halved (doubled nibble table)
+    assert t[0xB8] == t[0x38]  # bit 7 ignored
+    assert t[0xFF] == 240.0  # gguf-py quirk: 0xFF is not zeroed
+
+
+@pytest.mark.parametrize("name", list(GEMV_CASES))
+def test_gemv_ref_matches_golden(golden, name):
+    d = golden("gemv.npz")
+    op, R, N, K, seed = GEMV_CASES[name]
+    x, w, extra = I.gemv_case(op, R, N, K, seed=seed)
+    assert np.array_equal(x, d[f"{name}_x"]) and np.array_equal(w, d[f"{name}_w"]), "input builder drifted"
+    deq = {"q8_0": O.dequant_q8_0, "iq2_xxs": O.dequant_iq2_xxs, "nvfp4": O.dequant_nvfp4}[op](w)
+    y = O.gemv_ref(x, deq) * (float(extra["gscale"][0]) if op == "nvfp4" else 1.0)
+    assert rel(y, d[f"{name}_y"]) < 1e-6
+
+
+@pytest.mark.parametrize("name", ["c3", "harness"])
+def test_route_ref_matches_golden(golden, name):
+    d = golden("route.npz")
+    x, gw, b, topk, scale = route_inputs(name)
+    assert sha(x, gw, b) == str(d[f"{name}_sha"]), "input builder drifted"
+    idx, wts, scores, near = O.route_ref(x, gw, b, topk, scale)
+    # rows whose k-th / (k+1)-th bias-corrected scores are within 1e-6 may legitimately swap the
+    # boundary expert under another summation order: compare their selected scores instead
+    ok = ~near
+    assert ok.sum() >= len(ok) - 1
+    assert np.array_equal(idx[ok], d[f"{name}_idx"][ok])  # torch.topk order: descending value
+    assert np.allclose(np.sort(wts[near], 1), np.sort(d[f"{name}_w"][near], 1), rtol=1e-5, atol=1e-6)
+    assert rel(wts, d[f"{name}_w"]) < 1e-5
+    assert rel(scores, d[f"{name}_scores"]) < 1e-6
+
+
+def test_route_ref_ties_to_lower_index():
+    x = np.zeros((1, 256), dtype=np.uint16)  # all-zero input: every score is sigmoid(0) = 0.5
+    gw = np.ones((16, 256), dtype=np.float32)
+    b = np.zeros(16, dtype=np.float32)
+    idx, wts, _, near = O.route_ref(x, gw, b, 4, 2.0)
+    assert idx.tolist() == [[0, 1, 2, 3]] and near.all()
+    assert np.allclose(wts, 0.5)
+
+
+def test_moe_ref_matches_golden(golden):
+    d = golden("moe.npz")
+    z, idx, w, b1, b2, (R, E, H, Idim, topk) = moe_inputs()
+    assert sha(z, idx, w, b1, b2) == str(d["sha"]), "input builder drifted"
+    d1 = O.dequant_iq2_xxs(b1.reshape(E * Idim, -1)).reshape(E, Idim, H)
+    d2 = O.dequant_iq2_xxs(b2.reshape(E * H, -1)).reshape(E, H, Idim)
+    out, h, part = O.moe_ref(z, idx, w, d1, d2)
+    # fp64 vs torch fp32 sums may flip an occasional bf16 rounding of h / part
+    assert rel(out, d["out"]) < 2e-3
+
+
+def test_bf16_round_matches_torch():
+    v = (I.rng(9).standard_normal(4096) * 100).astype(np.float32)
+    assert np.array_equal(O.bf16_round(v), torch.from_numpy(v).bfloat16().float().numpy())
