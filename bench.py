@@ -1,0 +1,502 @@
+#!/usr/bin/env python
+"""Weight-stream bandwidth of the GGUF decode GEMV / MoE hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--quick]
+
+Headline (one JSON line on rank 0): BASELINE config 1 -- Q4Gemv iq2=3 (IQ2_XXS), R=1, K=4096,
+N=14336 -- as weight-stream GB/s (algorithmic bytes = the weight tensor, 15,138,816 B per call).
+
+* A step = one CUDA-graph replay of `rounds` passes over `copies` distinct weight copies
+  (copies * 15.1 MB > 2 x L2, so every call streams from HBM); calls are launched with
+  programmatic dependent launch.  value = weight bytes of all ranks / max-over-ranks time.
+* e2e = the same metric through the public C ABI with host buffers: each step copies x from pinned
+  host memory, runs one pass over the weight copies and reads every y back to pinned host memory
+  (all inside the captured step).
+* roofline = achieved GB/s of the GEMV kernel vs the measured HBM copy bandwidth in
+  MEASURED_PEAKS.json; traffic (DRAM bytes per launch) comes from the committed ncu summary
+  profiles/traffic.json when present.
+* cpu_baseline = the oracle port of the reference's CPU path (gguf-py dequantise + fp32 matmul)
+  on a bounded row sample, all host threads.
+* configs = every BASELINE config at 1 GPU (skipped with --quick or N > 1).
+
+N > 1 (torchrun): config 1 does not shard (replicas only): every rank runs the same workload on its
+own GPU; the timing is the max over ranks.
+``--impl reference`` times the reference's CPU path (oracle port) on the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+HEADLINE = dict(cfg="C1", op="iq2_xxs", R=1, N=14336, K=4096)
+ROW_BYTES = {"q8_0": lambda K: K // 32 * 34, "iq2_xxs": lambda K: K // 256 * 66, "nvfp4": lambda K: K // 64 * 36}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--quick", action="store_true", help="headline only")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------
+# distributed plumbing
+# ------------------------------------------------------------------------------------------------
+def dist_setup(n):
+    import torch
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks (NVML, sampled in a thread during the timed region)
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max = [], 0, None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 -- clocks are reported as unavailable
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def report(self):
+        if not self.nv or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max, "reasons": ["unavailable"]}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------
+# synthetic weights on the device (BASELINE distributions)
+# ------------------------------------------------------------------------------------------------
+def gen_weights(op, N, K, seed, dev):
+    """Raw GGUF bytes [N, row_bytes] with the BASELINE config distributions, built on the device."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    if op == "q8_0":  # Q8_0 of N(0, 0.02): d = amax/127, q = roundf(v / d) (ggml rounding), d as fp16
+        w = torch.randn(N, K // 32, 32, generator=g, device=dev) * 0.02
+        d = w.abs().amax(-1, keepdim=True) / 127
+        inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+        v = w * inv
+        q = (torch.sign(v) * torch.floor(v.abs() + 0.5)).to(torch.int8)
+        blk = torch.cat([d.half().view(torch.uint8), q.view(torch.uint8)], -1)
+        return blk.reshape(N, -1).contiguous()
+    if op == "iq2_xxs":  # fp16 d = |N(0,1)| * 0.002, then 64 uniform bytes
+        blk = torch.randint(0, 256, (N, K // 256, 66), generator=g, device=dev, dtype=torch.uint8)
+        d = (torch.randn(N, K // 256, 1, generator=g, device=dev).abs() * 0.002).half()
+        blk[..., :2] = d.view(torch.uint8)
+        return blk.reshape(N, -1).contiguous()
+    if op == "nvfp4":  # 4 UE4M3 scales uniform over the codes of [2^-4, 2^2], then 32 uniform bytes
+        blk = torch.randint(0, 256, (N, K // 64, 36), generator=g, device=dev, dtype=torch.uint8)
+        blk[..., :4] = torch.randint(0x18, 0x49, (N, K // 64, 4), generator=g, device=dev, dtype=torch.uint8)
+        return blk.reshape(N, -1).contiguous()
+    raise ValueError(op)
+
+
+def replicate(t, copies):
+    import torch
+
+    out = [t]
+    for _ in range(copies - 1):
+        c = torch.empty_like(t)
+        c.copy_(t)
+        out.append(c)
+    return out
+
+
+def n_copies(bytes_per):
+    return max(1, math.ceil(2.2 * L2_BYTES / bytes_per)) if bytes_per < 2.2 * L2_BYTES else 1
+
+
+# ------------------------------------------------------------------------------------------------
+# timing helpers
+# ------------------------------------------------------------------------------------------------
+def capture(fn):
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # warm-up outside capture (sets kernel attributes)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, steps, warmup, world=1):
+    import torch
+
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return e0.elapsed_time(e1)  # ms
+
+
+def gemv_call(op, x, w, y, gs, R, N, K):
+    from gguf_onnx_ops_b200 import ops
+
+    if op == "q8_0":
+        ops.q8_0_gemv_into(x, w, y, R, N, K)
+    elif op == "iq2_xxs":
+        ops.iq2_xxs_gemv_into(x, w, y, R, N, K)
+    else:
+        ops.nvfp4_gemv_into(x, w, gs, y, R, N, K)
+
+
+def bench_gemv(op, R, N, K, steps, warmup, dev, target_step_ms=8.0, world=1, sampler=None):
+    """Returns dict(us_per_call, gbs, calls, ...) for a dense GGUF GEMV config."""
+    import torch
+
+    wbytes = N * ROW_BYTES[op](K)
+    copies = n_copies(wbytes)
+    base = gen_weights(op, N, K, seed=1, dev=dev)
+    ws = replicate(base, copies)
+    del base
+    x = (torch.randn(R, K, device=dev)).bfloat16()
+    ys = [torch.empty(R, N, dtype=torch.bfloat16, device=dev) for _ in range(copies)]
+    gs = torch.tensor([1.0 / 448.0], device=dev)
+
+    def one_pass():
+        for w, y in zip(ws, ys):
+            gemv_call(op, x, w, y, gs, R, N, K)
+
+    # calibrate rounds per step so one step lasts ~target_step_ms
+    g1 = capture(one_pass)
+    ms1 = time_graph(g1, 5, 2) / 5
+    rounds = max(1, int(round(target_step_ms / max(ms1, 1e-3))))
+
+    def step():
+        for _ in range(rounds):
+            one_pass()
+
+    g = capture(step) if rounds > 1 else g1
+    if sampler is not None:
+        with sampler:
+            ms = time_graph(g, steps, warmup, world)
+    else:
+        ms = time_graph(g, steps, warmup, world)
+    ms = max_over_ranks(ms, world)
+    calls = steps * rounds * copies
+    us = ms * 1e3 / calls
+    out = dict(us_per_call=us, gbs=wbytes / (us * 1e-6) / 1e9, weight_bytes=wbytes, copies=copies, rounds=rounds,
+               calls=calls, ms_total=ms, ms_per_step=ms / steps, step_ms_graph_single_pass=ms1)
+    del g, g1
+    return out, (ws, x, ys, gs, wbytes, copies)
+
+
+def bench_e2e_gemv(op, R, N, K, steps, warmup, dev, state):
+    """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host."""
+    import torch
+
+    ws, x, ys, gs, wbytes, copies = state
+    xh = torch.randn(R, K).bfloat16().pin_memory()
+    yh = torch.empty(copies, R, N, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+
+    def step():
+        xd.copy_(xh, non_blocking=True)
+        for i, (w, y) in enumerate(zip(ws, ys)):
+            gemv_call(op, xd, w, y, gs, R, N, K)
+            yh[i].copy_(y, non_blocking=True)
+
+    g = capture(step)
+    ms = time_graph(g, steps, warmup)
+    ms_step = ms / steps
+    return dict(value=wbytes * copies / (ms_step * 1e-3) / 1e9, unit="GB/s", h2d_bytes_per_step=R * K * 2,
+                d2h_bytes_per_step=copies * R * N * 2, ms_per_step=ms_step)
+
+
+def bench_moe(R, steps, warmup, dev):
+    """Config C3: MoeRouteGGUF -> MoeVerify iq2=3 (E=128, I=1792, topk=6) over distinct expert copies."""
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    E, H, I, topk = 128, 1024, 1792, 6
+    w1 = gen_weights("iq2_xxs", E * I, H, seed=2, dev=dev).reshape(E, I, -1)
+    w2 = gen_weights("iq2_xxs", E * H, I, seed=3, dev=dev).reshape(E, H, -1)
+    per_copy = w1.numel() + w2.numel() + E * H * 4
+    copies = n_copies(per_copy)
+    w1s, w2s = replicate(w1, copies), replicate(w2, copies)
+    gwt = (torch.randn(E, H, device=dev) * 0.02)
+    gws = replicate(gwt, copies)
+    bias = torch.randn(E, device=dev) * 0.01
+    x = torch.randn(R, H, device=dev).bfloat16()
+    z = torch.randn(R, H, device=dev).bfloat16()
+    P = R * topk
+    idx = [torch.empty(R, topk, dtype=torch.int32, device=dev) for _ in range(copies)]
+    wt = [torch.empty(R, topk, dtype=torch.float32, device=dev) for _ in range(copies)]
+    sc = torch.empty(R, E, dtype=torch.float32, device=dev)
+    out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+    h = torch.empty(P, I, dtype=torch.bfloat16, device=dev)
+    part = torch.empty(P, H, dtype=torch.float32, device=dev)
+    meta = torch.empty(1 + 9 * P, dtype=torch.int32, device=dev)
+
+    def one_pass():
+        for c in range(copies):
+            ops.moe_route_into(x, gws[c], bias, idx[c], wt[c], sc, R, H, E, topk, 1.0)
+            ops.moe_verify_into(z, idx[c], wt[c], w1s[c], w2s[c], out, h, part, meta, R, E, I, topk)
+
+    g1 = capture(one_pass)
+    ms1 = time_graph(g1, 5, 2) / 5
+    rounds = max(1, int(round(8.0 / max(ms1, 1e-3))))
+
+    def step():
+        for _ in range(rounds):
+            one_pass()
+
+    g = capture(step) if rounds > 1 else g1
+    ms = time_graph(g, steps, warmup)
+    U = len(torch.unique(idx[0]))
+    bytes_call = E * H * 4 + U * (I * (H // 256) * 66 + H * (I // 256) * 66)
+    calls = steps * rounds * copies
+    us = ms * 1e3 / calls
+    return dict(us_per_call=us, gbs=bytes_call / (us * 1e-6) / 1e9, weight_bytes=bytes_call, unique_experts=U,
+                copies=copies, rounds=rounds, kernels_per_call=5)
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU baseline: the reference's CPU path (gguf-py dequantise + fp32 matmul), oracle port
+# ------------------------------------------------------------------------------------------------
+def cpu_baseline(op, R, N, K, budget_s=10.0):
+    import concurrent.futures as cf
+
+    import torch
+
+    import oracle as O
+    from oracle import inputs as I
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    deq = {"q8_0": O.dequant_q8_0, "iq2_xxs": O.dequant_iq2_xxs, "nvfp4": O.dequant_nvfp4}[op]
+    g = I.rng(0)
+    x = I.bf16_normal(g, (R, K))
+    xf = torch.from_numpy((x.astype(np.uint32) << 16).view(np.float32))
+    chunk = 256
+
+    def make(rows):
+        if op == "q8_0":
+            return I.q8_0_weights(g, rows, K)
+        if op == "iq2_xxs":
+            return I.iq2_xxs_weights(g, (rows,), K)
+        return I.nvfp4_weights(g, rows, K)
+
+    pool = cf.ThreadPoolExecutor(max_workers=cores)
+
+    def run(w):
+        parts = list(pool.map(deq, [w[i:i + chunk] for i in range(0, w.shape[0], chunk)]))
+        d = torch.from_numpy(np.concatenate(parts))
+        return xf @ d.T
+
+    w = make(chunk * cores)
+    t0 = time.perf_counter()
+    run(w)
+    t1 = time.perf_counter() - t0
+    rows = int(min(N, max(chunk, chunk * cores * budget_s / max(t1, 1e-3) / 4)))
+    rows = max(chunk, rows // chunk * chunk)
+    w = make(rows)
+    t0 = time.perf_counter()
+    run(w)
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    bytes_ = rows * ROW_BYTES[op](K)
+    return dict(value=bytes_ / dt / 1e9, unit="GB/s", cores=cores, kind="port",
+                sample=f"{rows} of {N} rows, R={R}, K={K}: numpy dequantise ({cores} threads) + torch fp32 matmul",
+                seconds=dt)
+
+
+# ------------------------------------------------------------------------------------------------
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f)
+        return t.get("C1_R1", {}).get("dram_bytes_per_launch")
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def main():
+    args = parse_args()
+    import torch
+
+    hd = HEADLINE
+    if args.impl == "reference":  # host CPU only; under torchrun rank 0 alone runs and prints
+        rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", args.gpus))
+    else:
+        rank, world, local = dist_setup(args.gpus)
+    metric = "weight-stream HBM GB/s per GEMV/MoE op call (Q4Gemv iq2=3, IQ2_XXS, R=1, K=4096, N=14336)"
+    config = {"workload": "BASELINE config 1: Q4Gemv iq2=3 (IQ2_XXS) R=1 K=4096 N=14336",
+              "parallelism": "replicas" if world > 1 else "single", "global_batch": hd["R"] * world,
+              "l2": "distinct weight copies per pass, total > 2x L2 (126 MB)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        runs = []
+        for i in range(args.warmup + args.steps):
+            cb = cpu_baseline(hd["op"], hd["R"], hd["N"], hd["K"], budget_s=max(1.0, 120.0 / (args.warmup + args.steps)))
+            if i >= args.warmup:
+                runs.append(cb)
+        v = statistics.median(r["value"] for r in runs)
+        line = {"impl": "reference", "metric": metric, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": statistics.median(r["seconds"] for r in runs) * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": config,
+                "cpu_baseline": {"value": v, "unit": "GB/s", "cores": runs[0]["cores"], "kind": "port",
+                                 "sample": runs[0]["sample"]},
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    import gguf_onnx_ops_b200
+
+    gguf_onnx_ops_b200.load()
+    sampler = ClockSampler(local)
+    res, state = bench_gemv(hd["op"], hd["R"], hd["N"], hd["K"], args.steps, args.warmup, dev, world=world,
+                            sampler=sampler)
+    value = res["gbs"] * world
+    peak, src = peaks()
+    line = {"metric": metric, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+            "us_per_call": res["us_per_call"],
+            "roofline": {"bound": "hbm", "achieved": res["gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": res["gbs"] / peak, "traffic": traffic_per_launch(), "peak_source": src,
+                         "algorithmic_bytes_per_launch": res["weight_bytes"]},
+            "gpu_launches": res["calls"], "clocks": sampler.report()}
+    if rank == 0:
+        line["e2e"] = bench_e2e_gemv(hd["op"], hd["R"], hd["N"], hd["K"], args.steps, args.warmup, dev, state)
+    del state
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline(hd["op"], hd["R"], hd["N"], hd["K"])
+        if not args.quick:
+            cfgs = {}
+            for name, op, R, N, K in ([("C0", "q8_0", 1, 4096, 4096)] +
+                                      [("C1", "iq2_xxs", R, 14336, 4096) for R in (1, 4, 8)] +
+                                      [("C2", "nvfp4", R, 13824, 5120) for R in (1, 8, 16)] +
+                                      [("C4", "q8_0", R, 131072, 4096) for R in (1, 4, 8, 16)]):
+                r, st = bench_gemv(op, R, N, K, max(5, args.steps // 2), args.warmup, dev)
+                del st
+                torch.cuda.empty_cache()
+                cfgs[f"{name}_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()
+                                        if k in ("us_per_call", "gbs", "weight_bytes", "copies", "rounds")}
+                cfgs[f"{name}_R{R}"]["frac_of_peak"] = round(r["gbs"] / peak, 4)
+            for R in (1, 4, 8):
+                r = bench_moe(R, max(5, args.steps // 2), args.warmup, dev)
+                r["frac_of_peak"] = r["gbs"] / peak
+                cfgs[f"C3_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()}
+                torch.cuda.empty_cache()
+            line["configs"] = cfgs
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

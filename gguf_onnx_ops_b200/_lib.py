@@ -35,6 +35,7 @@ SIGNATURES = {
     "gguf_dequantize": (_I32, [_I32, _P, _P, _I64, _I64, _P]),
     "gguf_device_status": (_I32, [ctypes.POINTER(ctypes.c_int)]),
     "gguf_set_pdl": (None, [_I32]),
+    "gguf_set_fast_paths": (None, [_I32]),
 }
 
 

@@ -59,6 +59,15 @@ __device__ __forceinline__ uint2 ld_u64_a2(const uint8_t* base, uint32_t off) {
   const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
   return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
 }
+// Exact-width variants for global memory: never touch a byte outside [off, off + 4/8).
+__device__ __forceinline__ uint32_t ld_u32_a2_exact(const uint8_t* base, uint32_t off) {
+  if ((off & 2u) == 0u) return *reinterpret_cast<const uint32_t*>(base + off);
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(base + off);
+  return static_cast<uint32_t>(h[0]) | (static_cast<uint32_t>(h[1]) << 16);
+}
+__device__ __forceinline__ uint2 ld_u64_a2_exact(const uint8_t* base, uint32_t off) {
+  return make_uint2(ld_u32_a2_exact(base, off), ld_u32_a2_exact(base, off + 4u));
+}
 __device__ __forceinline__ float fp16_bits_to_f32(uint32_t h) { return __half2float(__ushort_as_half(static_cast<unsigned short>(h))); }
 
 // ---------------------------------------------------------------------------------------------
@@ -78,11 +87,14 @@ __device__ __forceinline__ void q8_to_bf16x4(uint32_t q, uint32_t& w01, uint32_t
 
 // Group decode for one row: `row` points at the row's first byte of the staged K segment,
 // grp = group index within that segment.  Outputs the lane's 4 A words and the block scale.
+// kExact: read exactly the bytes of the block (global memory); otherwise a padded shared-memory
+// stage is read with aligned words.
+template <bool kExact = false>
 __device__ __forceinline__ void q8_decode_row(const uint8_t* base, uint32_t row_off, int grp, int t, uint32_t (&a)[4],
                                               float& d) {
   const uint32_t bo = row_off + static_cast<uint32_t>(grp) * 34u;
-  const uint32_t lo = ld_u32_a2(base, bo + 2u + 4u * t);
-  const uint32_t hi = ld_u32_a2(base, bo + 18u + 4u * t);
+  const uint32_t lo = kExact ? ld_u32_a2_exact(base, bo + 2u + 4u * t) : ld_u32_a2(base, bo + 2u + 4u * t);
+  const uint32_t hi = kExact ? ld_u32_a2_exact(base, bo + 18u + 4u * t) : ld_u32_a2(base, bo + 18u + 4u * t);
   d = fp16_bits_to_f32(ld_u16(base, bo));
   q8_to_bf16x4(lo, a[0], a[1]);
   q8_to_bf16x4(hi, a[2], a[3]);

@@ -175,16 +175,18 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineAr
   };
 
   if (warp == KW) {
-    // ================= producer =================
-    if (lane == 0) {
-      uint32_t it = 0;
-      for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-        int rv;
-        const uint8_t* src = tile_src(item, rv);
-        for (int sp = 0; sp < a.nsplit; ++sp, ++it) {
-          const int s = static_cast<int>(it % a.stages);
+    // ================= producer warp =================
+    // lane 0 waits for a free stage and posts the expected byte count; in segmented mode the 16
+    // per-row copies are then issued by lanes 0..15 in parallel.
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+      int rv;
+      const uint8_t* src = tile_src(item, rv);
+      for (int sp = 0; sp < a.nsplit; ++sp, ++it) {
+        const int s = static_cast<int>(it % a.stages);
+        uint8_t* dst = stages + s * a.stage_bytes;
+        if (lane == 0) {
           if (it >= static_cast<uint32_t>(a.stages)) mbar_wait(&empty[s], ((it / a.stages) - 1) & 1, kSiteEmptyWait);
-          uint8_t* dst = stages + s * a.stage_bytes;
           if (a.contiguous) {
             const uint32_t bytes = static_cast<uint32_t>(rv * a.row_bytes);
             const uint32_t bulk = bytes & ~15u;
@@ -194,13 +196,16 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineAr
             if (bulk) bulk_g2s(dst, src, bulk, &full[s]);
           } else {
             mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.seg_bytes));
-            const uint8_t* s0 = src + static_cast<int64_t>(sp) * a.seg_bytes;
-            for (int r = 0; r < rv; ++r)
-              bulk_g2s(dst + r * a.stride, s0 + static_cast<int64_t>(r) * a.row_bytes, a.seg_bytes, &full[s]);
           }
         }
+        __syncwarp();
+        if (!a.contiguous && lane < rv)
+          bulk_g2s(dst + lane * a.stride, src + static_cast<int64_t>(sp) * a.seg_bytes + static_cast<int64_t>(lane) * a.row_bytes,
+                   a.seg_bytes, &full[s]);
       }
-      // drain: the last uses of each stage must have landed before the CTA may exit
+    }
+    // drain: the last uses of each stage must have landed before the CTA may exit
+    if (lane == 0) {
       const uint32_t total = it;
       const uint32_t first = total > static_cast<uint32_t>(a.stages) ? total - a.stages : 0u;
       for (uint32_t j = first; j < total; ++j) mbar_wait(&full[j % a.stages], (j / a.stages) & 1, kSiteDrainWait);

@@ -15,6 +15,7 @@
 
 #include "../../include/gguf_ops.h"
 #include "engine.cuh"
+#include "iq2_r1.cuh"
 #include "small_kernels.cuh"
 
 namespace gguf_b200 {
@@ -23,6 +24,7 @@ namespace {
 
 thread_local std::string t_last_error;
 std::atomic<int> g_pdl{1};
+std::atomic<int> g_fast{1};  // specialised kernels (R = 1 paths); 0 forces the generic engine
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -30,7 +32,7 @@ int fail(int code, const std::string& msg) {
 }
 int cuda_fail(const char* op, cudaError_t e) { return fail(GGUF_ERR_CUDA, std::string(op) + ": " + cudaGetErrorString(e)); }
 
-constexpr int kKW = 8;                      // consumer warps per CTA
+constexpr int kKW = 16;                     // consumer warps per CTA
 constexpr int kThreads = (kKW + 1) * 32;    // + 1 producer warp
 constexpr int kSmemBudget = 112 * 1024;     // <= half an SM: two kernels' CTAs can co-reside
 constexpr int kSmemBudgetMax = 220 * 1024;  // fallback for very long rows
@@ -175,6 +177,37 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
   return GGUF_OK;
 }
 
+// IQ2_XXS, one activation row: block-diagonal super-block kernel (iq2_r1.cuh).
+template <int kW, int kSPW>
+int run_iq2_r1(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
+  Iq2R1Args a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.x = static_cast<const bf16*>(x);
+  a.y = static_cast<bf16*>(y);
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 256 * 66;
+  a.tiles = (N + 15) / 16;
+  int st = (a.row_bytes + 15) & ~15;
+  if (st % 32 == 0) st += 16;
+  a.stride = st;
+  a.stage_bytes = ((16 * st + 16) + 127) & ~127;
+  const int lut = 256 * 8 * 16, red = 2 * kW * 16 * 4;
+  a.stages = std::max(2, std::min(6, (kSmemBudget - lut - red - 256) / a.stage_bytes));
+  a.off_stage = lut;
+  a.off_red = lut + a.stages * a.stage_bytes;
+  a.off_bar = a.off_red + red;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = iq2_r1_kernel<kW, kSPW>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3((kW + 1) * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("Q4Gemv iq2=3 launch", e);
+  return GGUF_OK;
+}
+
 std::string dims(int64_t R, int64_t N, int64_t K) {
   char b[128];
   snprintf(b, sizeof(b), " (got R=%lld N=%lld K=%lld)", (long long)R, (long long)N, (long long)K);
@@ -196,6 +229,8 @@ const char* gguf_last_error(void) { return t_last_error.c_str(); }
 
 void gguf_set_pdl(int enable) { g_pdl.store(enable ? 1 : 0); }
 
+void gguf_set_fast_paths(int enable) { g_fast.store(enable ? 1 : 0); }
+
 int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K, void* stream) {
   t_last_error.clear();
   if (!x || !w || !y) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: null tensor pointer");
@@ -214,6 +249,11 @@ int gguf_iq2_xxs_gemv(const void* x, const void* w, void* y, int64_t R, int64_t 
     return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: needs B [N, (K/256)*66], K % 256 == 0 and 1..16 rows" + dims(R, N, K));
   if (!aligned(w, 16) || !aligned(x, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: x and w must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (R == 1 && g_fast.load()) {
+    if (K == 4096) return run_iq2_r1<16, 1>(x, w, y, (int)N, (int)K, s);
+    if (K == 8192) return run_iq2_r1<16, 2>(x, w, y, (int)N, (int)K, s);
+    if (K == 2048) return run_iq2_r1<8, 1>(x, w, y, (int)N, (int)K, s);
+  }
   return R <= 8 ? run_dense<kFmtIQ2, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)
                 : run_dense<kFmtIQ2, 2>(x, w, nullptr, y, (int)R, (int)N, (int)K, s);
 }

@@ -163,18 +163,15 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
   if (gid >= rows * G) return;
   const int64_t row = gid / G;
   const int grp = static_cast<int>(gid % G);
-  // base = the weight tensor (16-byte aligned); offsets are absolute byte offsets.
-  const uint32_t row_off = 0;
   const uint8_t* base = w + row * row_bytes;  // row starts are 2-byte aligned: realign below
   const uint8_t* abase = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(base) & ~uintptr_t(3));
   const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(base) & 3);
   float* o = out + row * K + grp * 32;
-  (void)row_off;
   if constexpr (F == kFmtQ8) {
     for (int t = 0; t < 4; ++t) {
       uint32_t a[4];
       float d;
-      q8_decode_row(abase, mis, grp, t, a, d);
+      q8_decode_row<true>(abase, mis, grp, t, a, d);
       o[4 * t + 0] = bf16_lo(a[0]) * d;
       o[4 * t + 1] = bf16_hi(a[0]) * d;
       o[4 * t + 2] = bf16_lo(a[1]) * d;
@@ -186,7 +183,7 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
     }
   } else if constexpr (F == kFmtIQ2) {
     const uint32_t sbo = mis + static_cast<uint32_t>(grp >> 3) * 66u;
-    const uint2 q = ld_u64_a2(abase, sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u);
+    const uint2 q = ld_u64_a2_exact(abase, sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u);
     const float d = fp16_bits_to_f32(ld_u16(abase, sbo));
     const float db = iq2_db(d, q.y);
     for (int t = 0; t < 4; ++t) {
@@ -213,10 +210,13 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
         lo = hmul2_bits(lo, Sx2);
         hi = hmul2_bits(hi, Sx2);
         float* os = o + 16 * s2;
-        os[2 * t] = bf16_lo(lo) * 65536.0f;
-        os[2 * t + 1] = bf16_hi(lo) * 65536.0f;
-        os[8 + 2 * t] = bf16_lo(hi) * 65536.0f;
-        os[8 + 2 * t + 1] = bf16_hi(hi) * 65536.0f;
+        // E2M1 code 0x8 is a negative zero; gguf-py's table maps it to +0.0 (the GEMV sums are
+        // unaffected, the dequantised bits are canonicalised here)
+        auto z = [](float f, uint32_t nib) { return (nib & 7u) ? f : 0.0f; };
+        os[2 * t] = z(bf16_lo(lo) * 65536.0f, v);
+        os[2 * t + 1] = z(bf16_hi(lo) * 65536.0f, v >> 8);
+        os[8 + 2 * t] = z(bf16_lo(hi) * 65536.0f, v >> 4);
+        os[8 + 2 * t + 1] = z(bf16_hi(hi) * 65536.0f, v >> 12);
       }
     }
   }

@@ -187,5 +187,10 @@ def set_pdl(enable: bool) -> None:
     load().gguf_set_pdl(1 if enable else 0)
 
 
+def set_fast_paths(enable: bool) -> None:
+    """Enable / disable the shape-specialised kernels (the generic engine handles every shape)."""
+    load().gguf_set_fast_paths(1 if enable else 0)
+
+
 def device_status():
     return _lib.device_status()

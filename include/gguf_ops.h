@@ -113,6 +113,10 @@ GGUF_OPS_API int gguf_device_status(int* device_error_site);
 /* Tuning: enable (1) / disable (0) programmatic dependent launch for subsequent calls (default 1). */
 GGUF_OPS_API void gguf_set_pdl(int enable);
 
+/* Tuning / testing: enable (1, default) or disable (0) the shape-specialised kernels (e.g. the
+ * single-row IQ2_XXS path); disabled, every call uses the generic engine. */
+GGUF_OPS_API void gguf_set_fast_paths(int enable);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,7 +36,8 @@ def gemv_ref(x, w_deq: np.ndarray) -> np.ndarray:
 
 
 def moe_ref(z, idx: np.ndarray, w: np.ndarray, d1: np.ndarray, d2: np.ndarray):
-    """z: [R, H] bf16 bits; idx: [R, k] int32; w: [R, k] fp32; d1: fp32 [E, I, H]; d2: fp32 [E, H, I].
+    """z: [R, H] bf16 bits; idx: [R, k] int32; w: [R, k] fp32; d1[e]: fp32 [I, H]; d2[e]: fp32 [H, I]
+    (arrays indexed by expert, or dicts holding only the experts idx references).
 
     Returns (out_f32 [R, H] before the final bf16 rounding, h [R*k, I] fp32 holding bf16 values,
     part [R*k, H] fp32 holding bf16 values).  Only the experts referenced by idx are touched.
@@ -44,7 +45,7 @@ def moe_ref(z, idx: np.ndarray, w: np.ndarray, d1: np.ndarray, d2: np.ndarray):
     zf = _x_f32(z).astype(np.float64)
     R, k = idx.shape
     H = zf.shape[1]
-    I = d1.shape[1]
+    I = d1[int(idx[0, 0])].shape[0]
     out = np.zeros((R, H), dtype=np.float32)
     h_all = np.zeros((R * k, I), dtype=np.float32)
     p_all = np.zeros((R * k, H), dtype=np.float32)

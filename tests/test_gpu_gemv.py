@@ -1,0 +1,198 @@
+"""GPU parity of the GGUF GEMVs (through the C ABI) against the CPU oracle and the golden fixtures.
+
+Tolerance: rel-L2 <= 5e-3 of the fp64 oracle (north-star bound for bf16 outputs); the kernels see
+the exact dequantised weights, so the observed error is the bf16 rounding of y (~1e-3).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from gguf_onnx_ops_b200 import _lib, ops
+from oracle import inputs as I
+from tests.golden.cases import GEMV_CASES
+from tests.util import bf16_t, np_f32, rel, u8_t
+
+pytestmark = pytest.mark.gpu
+
+TOL = 5e-3
+DEQ = {"q8_0": O.dequant_q8_0, "iq2_xxs": O.dequant_iq2_xxs, "nvfp4": O.dequant_nvfp4}
+
+
+def run_gemv(op, x, w, extra, dev):
+    xt, wt = bf16_t(x, dev), u8_t(w, dev)
+    if op == "q8_0":
+        y = ops.Q8Gemv(xt, wt, gguf=1)
+    elif op == "iq2_xxs":
+        y = ops.Q4Gemv(xt, wt, iq2=3)
+    else:
+        y = ops.Nvfp4Gemv(xt, wt, None, torch.from_numpy(extra["gscale"]).to(dev), gguf=1)
+    torch.cuda.synchronize()
+    return np_f32(y)
+
+
+def oracle_y(op, x, w, extra, rows=None):
+    wsel = w if rows is None else w[rows]
+    y = O.gemv_ref(x, DEQ[op](wsel))
+    return y * (float(extra["gscale"][0]) if op == "nvfp4" else 1.0)
+
+
+def assert_device_ok():
+    rc, site = _lib.device_status()
+    assert rc == 0, f"device-side error at site {site}"
+
+
+@pytest.mark.parametrize("name", list(GEMV_CASES))
+def test_golden_cases(cuda, golden, name):
+    d = golden("gemv.npz")
+    op, R, N, K, seed = GEMV_CASES[name]
+    x, w = d[f"{name}_x"], d[f"{name}_w"]
+    extra = {"gscale": np.array([1.0 / 448.0], np.float32)}
+    y = run_gemv(op, x, w, extra, cuda)
+    assert rel(y, d[f"{name}_y"]) < TOL
+    assert rel(y, oracle_y(op, x, w, extra)) < TOL
+
+
+@pytest.mark.parametrize("op", ["q8_0", "iq2_xxs", "nvfp4"])
+@pytest.mark.parametrize("R", [1, 2, 3, 5, 7, 8, 9, 12, 16])
+def test_all_row_counts(cuda, op, R):
+    K = {"q8_0": 1024, "iq2_xxs": 1024, "nvfp4": 1280}[op]
+    x, w, extra = I.gemv_case(op, R, 200, K, seed=100 + R)
+    y = run_gemv(op, x, w, extra, cuda)
+    assert rel(y, oracle_y(op, x, w, extra)) < TOL
+
+
+@pytest.mark.parametrize("op,N,K", [
+    ("q8_0", 1, 64), ("q8_0", 17, 320), ("q8_0", 33, 4160), ("q8_0", 5, 16384),  # contiguous + tail paths
+    ("iq2_xxs", 1, 256), ("iq2_xxs", 23, 768), ("iq2_xxs", 31, 1792), ("iq2_xxs", 9, 8192),
+    ("nvfp4", 1, 64), ("nvfp4", 19, 192), ("nvfp4", 45, 5120), ("nvfp4", 7, 16384),
+])
+def test_ragged_and_odd_shapes(cuda, op, N, K):
+    x, w, extra = I.gemv_case(op, 3, N, K, seed=N * 7 + K)
+    y = run_gemv(op, x, w, extra, cuda)
+    assert rel(y, oracle_y(op, x, w, extra)) < TOL
+
+
+@pytest.mark.parametrize("op", ["q8_0", "iq2_xxs", "nvfp4"])
+def test_massive_activations(cuda, op):
+    """Outlier activations (the reference's XSCALE=3000 case) must not overflow anything."""
+    g = I.rng(77)
+    K = 2048
+    x = I.bf16_normal(g, (8, K), 3000.0)
+    _, w, extra = I.gemv_case(op, 1, 96, K, seed=78)
+    y = run_gemv(op, x, w, extra, cuda)
+    assert np.isfinite(y).all()
+    assert rel(y, oracle_y(op, x, w, extra)) < TOL
+
+
+def test_nvfp4_all_scale_bytes(cuda, golden):
+    d = golden("dequant.npz")
+    w = d["fp4all_raw"]  # scale bytes 0x00..0xFF incl. 0x7F and >= 0x80 (gguf-py semantics)
+    g = I.rng(3)
+    x = I.bf16_normal(g, (2, 1024))
+    extra = {"gscale": np.array([0.37], np.float32)}
+    y = run_gemv("nvfp4", x, w, extra, cuda)
+    ref = O.gemv_ref(x, d["fp4all_deq"]) * 0.37
+    assert rel(y, ref) < TOL
+
+
+# BASELINE configs at full size: oracle on a random subset of rows; every row against the
+# bit-exact device dequantisation followed by an fp32 matmul.
+CONFIG_CASES = [("C0", "q8_0", 1, 4096, 4096)] + [("C1", "iq2_xxs", R, 14336, 4096) for R in (1, 4, 8)] + \
+               [("C2", "nvfp4", R, 13824, 5120) for R in (1, 8, 16)]
+
+
+@pytest.mark.parametrize("cfg,op,R,N,K", CONFIG_CASES)
+def test_baseline_configs(cuda, cfg, op, R, N, K):
+    x, w, extra = I.gemv_case(op, R, N, K, seed=0)
+    y = run_gemv(op, x, w, extra, cuda)
+    rows = np.sort(I.rng(1).choice(N, size=512, replace=False))
+    assert rel(y[:, rows], oracle_y(op, x, w, extra, rows)) < TOL
+    gt = {"q8_0": _lib.GGUF_TYPE_Q8_0, "iq2_xxs": _lib.GGUF_TYPE_IQ2_XXS, "nvfp4": _lib.GGUF_TYPE_NVFP4}[op]
+    deq = ops.dequantize(u8_t(w, cuda), gt, K)
+    full = bf16_t(x, cuda).float() @ deq.T
+    if op == "nvfp4":
+        full = full * float(extra["gscale"][0])
+    assert rel(y, np_f32(full)) < TOL
+    assert_device_ok()
+
+
+def test_lm_head_shape_r16(cuda):
+    """C4 shape (N = 131072) at R=16, oracle on a row subset."""
+    x, w, extra = I.gemv_case("q8_0", 16, 131072, 4096, seed=4)
+    y = run_gemv("q8_0", x, w, extra, cuda)
+    rows = np.sort(I.rng(2).choice(131072, size=256, replace=False))
+    assert rel(y[:, rows], oracle_y("q8_0", x, w, extra, rows)) < TOL
+
+
+@pytest.mark.parametrize("op", ["q8_0", "iq2_xxs", "nvfp4"])
+def test_chained_calls_with_pdl(cuda, op):
+    """y of call i is x of call i+1 (N == K): programmatic dependent launch must still order the
+    consumer's activation reads after the producer kernel; results equal the non-PDL chain."""
+    K = 1024
+    chain = [I.gemv_case(op, 4, K, K, seed=500 + i) for i in range(6)]
+    x0 = bf16_t(chain[0][0], cuda)
+    ws = [u8_t(c[1], cuda) for c in chain]
+    gs = torch.tensor([1.0 / 64.0], device=cuda)
+
+    def run(pdl):
+        ops.set_pdl(pdl)
+        x = x0
+        for wt in ws:
+            if op == "q8_0":
+                x = ops.Q8Gemv(x, wt)
+            elif op == "iq2_xxs":
+                x = ops.Q4Gemv(x, wt)
+            else:
+                x = ops.Nvfp4Gemv(x, wt, None, gs)
+        torch.cuda.synchronize()
+        return x.clone()
+
+    try:
+        a = run(True)
+        b = run(False)
+    finally:
+        ops.set_pdl(True)
+    assert torch.equal(a, b)
+    assert_device_ok()
+
+
+def test_graph_capture_replay(cuda):
+    x, w, _ = I.gemv_case("iq2_xxs", 4, 2048, 4096, seed=9)
+    xt, wt = bf16_t(x, cuda), u8_t(w, cuda)
+    y = torch.empty(4, 2048, dtype=torch.bfloat16, device=cuda)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ops.iq2_xxs_gemv_into(xt, wt, y, 4, 2048, 4096)  # warm-up (sets kernel attributes)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ops.iq2_xxs_gemv_into(xt, wt, y, 4, 2048, 4096)
+    y.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert rel(np_f32(y), oracle_y("iq2_xxs", x, w, {})) < TOL
+
+
+def test_invalid_row_count_raises(cuda):
+    x = torch.zeros(17, 256, dtype=torch.bfloat16, device=cuda)
+    w = torch.zeros(16, 66, dtype=torch.uint8, device=cuda)
+    with pytest.raises(ValueError, match="1..16 rows"):
+        ops.Q4Gemv(x, w)
+
+
+@pytest.mark.parametrize("N,K", [(1, 2048), (37, 2048), (200, 4096), (14336, 4096), (77, 8192)])
+def test_iq2_single_row_fast_path(cuda, N, K):
+    """The R=1 IQ2_XXS kernel (block-diagonal super-block MMA) against the oracle and the generic engine."""
+    x, w, extra = I.gemv_case("iq2_xxs", 1, N, K, seed=N + K)
+    y_fast = run_gemv("iq2_xxs", x, w, extra, cuda)
+    rows = np.arange(N) if N <= 512 else np.sort(I.rng(3).choice(N, size=512, replace=False))
+    assert rel(y_fast[:, rows], oracle_y("iq2_xxs", x, w, extra, rows)) < TOL
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_gemv("iq2_xxs", x, w, extra, cuda)
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y_fast, y_gen) < 2e-3
+    assert_device_ok()

@@ -1,0 +1,138 @@
+"""GPU parity of MoeRouteGGUF and MoeVerify iq2=3 (through the C ABI) against the CPU oracle and
+the golden fixtures.
+
+Router: expert indices bit-exact (rows with a bias-corrected near-tie below 1e-6 compared by
+selected score), weights rel <= 1e-5.  MoeVerify: out within rel-L2 <= 5e-3 of the oracle (which
+keeps the op's bf16 rounding points), h / part elementwise close, meta exact.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from gguf_onnx_ops_b200 import _lib, ops
+from oracle import inputs as I
+from tests.golden.cases import moe_inputs, route_inputs
+from tests.util import bf16_t, np_f32, rel, u8_t
+
+pytestmark = pytest.mark.gpu
+
+
+def route_gpu(x, gw, b, topk, scale, dev):
+    idx, w, sc = ops.MoeRouteGGUF(bf16_t(x, dev), torch.from_numpy(gw).to(dev), torch.from_numpy(b).to(dev), topk, scale)
+    torch.cuda.synchronize()
+    return idx.cpu().numpy(), w.cpu().numpy(), sc.cpu().numpy()
+
+
+def check_route(x, gw, b, topk, scale, dev):
+    idx, w, sc = route_gpu(x, gw, b, topk, scale, dev)
+    ridx, rw, rsc, near = O.route_ref(x, gw, b, topk, scale)
+    ok = ~near
+    assert np.array_equal(idx[ok], ridx[ok])
+    assert np.allclose(np.sort(w[near], 1), np.sort(rw[near], 1), rtol=1e-5, atol=1e-6)
+    assert rel(w, rw) < 1e-5
+    assert rel(sc, rsc) < 1e-6
+    return idx, w
+
+
+@pytest.mark.parametrize("name", ["c3", "harness"])
+def test_route_golden(cuda, golden, name):
+    d = golden("route.npz")
+    x, gw, b, topk, scale = route_inputs(name)
+    idx, w = check_route(x, gw, b, topk, scale, cuda)
+    _, _, _, near = O.route_ref(x, gw, b, topk, scale)
+    assert np.array_equal(idx[~near], d[f"{name}_idx"][~near])
+    assert rel(w, d[f"{name}_w"]) < 1e-5
+
+
+@pytest.mark.parametrize("R,E,K,topk,scale", [(1, 128, 1024, 6, 1.0), (4, 128, 1024, 6, 1.0), (8, 128, 1024, 6, 1.0),
+                                              (3, 240, 4096, 9, 5.0), (8, 496, 2048, 9, 2.5), (21, 128, 1024, 6, 1.0),
+                                              (5, 512, 256, 32, 1.0), (2, 7, 256, 1, 1.0), (9, 13, 512, 13, 0.5)])
+def test_route_shapes(cuda, R, E, K, topk, scale):
+    g = I.rng(R * 1000 + E)
+    x = I.bf16_normal(g, (R, K))
+    gw = (g.standard_normal((E, K)) * 0.02).astype(np.float32)
+    b = (g.standard_normal(E) * 0.01).astype(np.float32)
+    check_route(x, gw, b, topk, scale, cuda)
+
+
+def test_route_ties_to_lower_index(cuda):
+    x = np.zeros((3, 256), dtype=np.uint16)
+    gw = np.ones((40, 256), dtype=np.float32)
+    b = np.zeros(40, dtype=np.float32)
+    idx, w, _ = route_gpu(x, gw, b, 5, 1.0, cuda)
+    assert (idx == np.arange(5)).all()
+    assert np.allclose(w, 0.2)
+
+
+def moe_gpu(z, idx, w, w1, w2, topk, dev):
+    out, h, part, meta = ops.MoeVerify(bf16_t(z, dev), torch.from_numpy(idx).to(dev), torch.from_numpy(w).to(dev),
+                                       u8_t(w1, dev), None, u8_t(w2, dev), None, topk=topk, iq2=3)
+    torch.cuda.synchronize()
+    return np_f32(out), np_f32(h), part.cpu().numpy(), meta.cpu().numpy()
+
+
+def check_moe(z, idx, w, w1, w2, topk, dev):
+    E, Idim = w1.shape[0], w1.shape[1]
+    H = 1024
+    out, h, part, meta = moe_gpu(z, idx, w, w1, w2, topk, dev)
+    used = [int(e) for e in np.unique(idx)]
+    d1 = {e: O.dequant_iq2_xxs(w1[e]) for e in used}  # expert id -> fp32 [I, H]
+    d2 = {e: O.dequant_iq2_xxs(w2[e]) for e in used}
+    rout, rh, rpart = O.moe_ref(z, idx, w, d1, d2)
+    assert rel(out, O.bf16_round(rout)) < 5e-3
+    assert rel(h, rh) < 5e-3 and rel(part, rpart) < 5e-3
+    # meta: [U, uniq ids in first-occurrence order, pair table]
+    flat = idx.reshape(-1)
+    order = []
+    for e in flat:
+        if e not in order:
+            order.append(int(e))
+    P = flat.size
+    assert meta[0] == len(order) and meta[1:1 + len(order)].tolist() == order
+    table = meta[1 + P:].reshape(P, 8)
+    for p, e in enumerate(flat):
+        assert table[order.index(int(e)), p // topk] == p
+    return out
+
+
+def test_moe_golden(cuda, golden):
+    d = golden("moe.npz")
+    z, idx, w, b1, b2, (R, E, H, Idim, topk) = moe_inputs()
+    out = check_moe(z, idx, w, b1, b2, topk, cuda)
+    assert rel(out, d["out"]) < 5e-3
+
+
+@pytest.mark.parametrize("R", [1, 4, 8])
+def test_moe_config_c3_routed(cuda, R):
+    """Config C3 end to end: MoeRouteGGUF -> MoeVerify iq2=3, E=128, I=1792, topk=6."""
+    c = I.moe_case(R)
+    idx, w = check_route(c["x"], c["gate_w"], c["bias"], 6, 1.0, cuda)
+    check_moe(c["z"], idx, w.astype(np.float32), c["w1"], c["w2"], 6, cuda)
+
+
+@pytest.mark.parametrize("R,E,Idim,topk", [(8, 12, 2048, 6), (8, 16, 256, 16), (1, 240, 1536, 9), (3, 5, 512, 5)])
+def test_moe_shapes(cuda, R, E, Idim, topk):
+    g = I.rng(R * 100 + E)
+    z = I.bf16_normal(g, (R, 1024), 0.5)
+    idx = np.stack([g.permutation(E)[:topk] for _ in range(R)]).astype(np.int32)
+    w = g.random((R, topk)).astype(np.float32)
+    w1 = I.iq2_test_blocks(g, (E, Idim), 1024)
+    w2 = I.iq2_test_blocks(g, (E, 1024), Idim)
+    check_moe(z, idx, w, w1, w2, topk, cuda)
+
+
+def test_moe_rejects_bad_rows(cuda):
+    z = torch.zeros(9, 1024, dtype=torch.bfloat16, device=cuda)
+    idx = torch.zeros(9, 6, dtype=torch.int32, device=cuda)
+    w = torch.zeros(9, 6, dtype=torch.float32, device=cuda)
+    w1 = torch.zeros(4, 256, 264, dtype=torch.uint8, device=cuda)
+    w2 = torch.zeros(4, 1024, 66, dtype=torch.uint8, device=cuda)
+    with pytest.raises(ValueError, match=r"rows must be in \[1,8\]"):
+        ops.MoeVerify(z, idx, w, w1, None, w2, None, topk=6)
+
+
+def test_device_status_clean(cuda):
+    rc, site = _lib.device_status()
+    assert rc == 0, site
