@@ -65,8 +65,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 // Unique-expert grouping of idx (first-occurrence order, as src/bolt_ops.cu:1233-1261):
 // s_uexp[u] = expert id of group u, s_pair[u*8 + row] = pair index (row*topk + k) or -1.
 // Pairs with an expert id outside [0, E) are ignored.  Returns U (in shared memory).
-__device__ __forceinline__ void moe_group(const EngineArgs& a, uint8_t* smem) {
-  int* s_idx = reinterpret_cast<int*>(smem + a.off_grp);
+__device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int topk, int* s_idx) {
   int* s_first = s_idx + kMaxPairs;
   int* s_rank = s_first + kMaxPairs;
   int* s_uexp = s_rank + kMaxPairs;
@@ -74,12 +73,12 @@ __device__ __forceinline__ void moe_group(const EngineArgs& a, uint8_t* smem) {
   int* s_U = s_pair + kMaxPairs * 8;
   const int tid = threadIdx.x, nth = blockDim.x;
   for (int i = tid; i < kMaxPairs * 8; i += nth) s_pair[i] = -1;
-  if (tid < a.P) s_idx[tid] = a.idx[tid];
+  if (tid < P) s_idx[tid] = idx[tid];
   __syncthreads();
-  if (tid < a.P) {
+  if (tid < P) {
     const int my = s_idx[tid];
     int q = -1;
-    if (my >= 0 && my < a.E)
+    if (my >= 0 && my < E)
       for (int j = 0; j <= tid; ++j)
         if (s_idx[j] == my) {
           q = j;
@@ -88,7 +87,7 @@ __device__ __forceinline__ void moe_group(const EngineArgs& a, uint8_t* smem) {
     s_first[tid] = q;
   }
   __syncthreads();
-  if (tid < a.P) {
+  if (tid < P) {
     if (s_first[tid] == tid) {
       int r = 0;
       for (int j = 0; j < tid; ++j) r += (s_first[j] == j);
@@ -98,12 +97,47 @@ __device__ __forceinline__ void moe_group(const EngineArgs& a, uint8_t* smem) {
   }
   if (tid == 0) {
     int u = 0;
-    for (int j = 0; j < a.P; ++j) u += (s_first[j] == j);
+    for (int j = 0; j < P; ++j) u += (s_first[j] == j);
     *s_U = u;
   }
   __syncthreads();
-  if (tid < a.P && s_first[tid] >= 0) s_pair[s_rank[s_first[tid]] * 8 + tid / a.topk] = tid;
+  if (tid < P && s_first[tid] >= 0) s_pair[s_rank[s_first[tid]] * 8 + tid / topk] = tid;
   __syncthreads();
+}
+
+// One IQ2_XXS k-group (32-element sub-block) of a staged 16-row tile for lane (g, t): rows g and
+// g+8 (byte offsets r0, r1 in the stage), grid entry t of each record, B fragments read from
+// xr[nt] + k0 + 8t.  kCoherent: the activation rows were written earlier in the same kernel, so
+// they are read through L2 (ld.global.cg) instead of the read-only path.
+template <int NT, bool kCoherent>
+__device__ __forceinline__ void iq2_group_mma(const uint8_t* smem, const uint8_t* st, uint32_t r0, uint32_t r1, int grp,
+                                              int t, uint32_t lut_lane, const bf16* const (&xr)[NT], int k0,
+                                              float (&acc)[NT][4]) {
+  const uint32_t sbo = static_cast<uint32_t>(grp >> 3) * 66u;
+  const uint32_t rec = sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u;
+  const uint2 q0 = ld_u64_a2(st, r0 + rec);
+  const uint2 q1 = ld_u64_a2(st, r1 + rec);
+  const float d0 = fp16_bits_to_f32(ld_u16(st, r0 + sbo));
+  const float d1 = fp16_bits_to_f32(ld_u16(st, r1 + sbo));
+  const uint32_t gi0 = (q0.x >> (8 * t)) & 0xFFu, gi1 = (q1.x >> (8 * t)) & 0xFFu;
+  const uint4 m0 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi0 << 7));
+  const uint4 m1 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi1 << 7));
+  uint32_t A0[4], A1[4];
+  iq2_apply_signs(m0, q0.y, 7u * t, A0);
+  iq2_apply_signs(m1, q1.y, 7u * t, A1);
+  const float db0 = iq2_db(d0, q0.y), db1 = iq2_db(d1, q1.y);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint4 xv = kCoherent ? __ldcg(reinterpret_cast<const uint4*>(xr[nt] + k0 + 8 * t)) : ldg128(xr[nt] + k0 + 8 * t);
+    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+    float D[4];
+    mma_bf16_16816(D, A0[0], A1[0], A0[1], A1[1], xv.x, xv.y, z);
+    mma_bf16_16816(D, A0[2], A1[2], A0[3], A1[3], xv.z, xv.w, D);
+    acc[nt][0] = fmaf(db0, D[0], acc[nt][0]);
+    acc[nt][1] = fmaf(db0, D[1], acc[nt][1]);
+    acc[nt][2] = fmaf(db1, D[2], acc[nt][2]);
+    acc[nt][3] = fmaf(db1, D[3], acc[nt][3]);
+  }
 }
 
 template <int F, int NT, int KW, int MODE>
@@ -144,7 +178,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineAr
   } else {
     // The expert ids come from the previous kernel (the router): wait first.
     pdl_wait();
-    moe_group(a, smem);  // ends with __syncthreads
+    moe_group(a.idx, a.P, a.E, a.topk, reinterpret_cast<int*>(smem + a.off_grp));  // ends with __syncthreads
     const int* s_idx = reinterpret_cast<const int*>(smem + a.off_grp);
     s_uexp = s_idx + 3 * kMaxPairs;
     s_pair = s_uexp + kMaxPairs;
@@ -275,31 +309,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineAr
             acc[nt][3] = fmaf(d1, D[3], acc[nt][3]);
           }
         } else if constexpr (F == kFmtIQ2) {
-          const uint32_t sbo = static_cast<uint32_t>(grp >> 3) * 66u;
-          const uint32_t rec = sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u;
-          const uint2 q0 = ld_u64_a2(st, r0 + rec);
-          const uint2 q1 = ld_u64_a2(st, r1 + rec);
-          const float d0 = fp16_bits_to_f32(ld_u16(st, r0 + sbo));
-          const float d1 = fp16_bits_to_f32(ld_u16(st, r1 + sbo));
-          const uint32_t gi0 = (q0.x >> (8 * t)) & 0xFFu, gi1 = (q1.x >> (8 * t)) & 0xFFu;
-          const uint4 m0 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi0 << 7));
-          const uint4 m1 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi1 << 7));
-          uint32_t A0[4], A1[4];
-          iq2_apply_signs(m0, q0.y, 7u * t, A0);
-          iq2_apply_signs(m1, q1.y, 7u * t, A1);
-          const float db0 = iq2_db(d0, q0.y), db1 = iq2_db(d1, q1.y);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            const uint4 xv = ldg128(xr[nt] + k0 + 8 * t);
-            const float z[4] = {0.f, 0.f, 0.f, 0.f};
-            float D[4];
-            mma_bf16_16816(D, A0[0], A1[0], A0[1], A1[1], xv.x, xv.y, z);
-            mma_bf16_16816(D, A0[2], A1[2], A0[3], A1[3], xv.z, xv.w, D);
-            acc[nt][0] = fmaf(db0, D[0], acc[nt][0]);
-            acc[nt][1] = fmaf(db0, D[1], acc[nt][1]);
-            acc[nt][2] = fmaf(db1, D[2], acc[nt][2]);
-            acc[nt][3] = fmaf(db1, D[3], acc[nt][3]);
-          }
+          iq2_group_mma<NT, false>(smem, st, r0, r1, grp, t, lut_lane, xr, k0, acc);
         } else {  // NVFP4: group = sub-blocks 2h, 2h+1 of block grp/2
           const uint32_t bo = static_cast<uint32_t>(grp >> 1) * 36u;
           const uint32_t h2 = static_cast<uint32_t>(grp & 1) * 2u;

@@ -15,7 +15,8 @@
 
 #include "../../include/gguf_ops.h"
 #include "engine.cuh"
-#include "iq2_r1.cuh"
+#include "slice_r1.cuh"
+#include "moe_fused.cuh"
 #include "small_kernels.cuh"
 
 namespace gguf_b200 {
@@ -177,23 +178,25 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
   return GGUF_OK;
 }
 
-// IQ2_XXS, one activation row: block-diagonal super-block kernel (iq2_r1.cuh).
-template <int kW, int kSPW>
-int run_iq2_r1(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
-  Iq2R1Args a = {};
+// One activation row: slice kernel (slice_r1.cuh), K = 256 * kW * kSPW, rows 16-byte multiples.
+template <int F, int kW, int kSPW>
+int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s) {
+  SliceArgs a = {};
   a.w = static_cast<const uint8_t*>(w);
   a.x = static_cast<const bf16*>(x);
+  a.gscale = gscale;
   a.y = static_cast<bf16*>(y);
   a.N = N;
   a.K = K;
-  a.row_bytes = K / 256 * 66;
+  a.row_bytes = K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes;
   a.tiles = (N + 15) / 16;
   int st = (a.row_bytes + 15) & ~15;
   if (st % 32 == 0) st += 16;
   a.stride = st;
-  a.stage_bytes = ((16 * st + 16) + 127) & ~127;
-  const int lut = 256 * 8 * 16, red = 2 * kW * 16 * 4;
-  a.stages = std::max(2, std::min(6, (kSmemBudget - lut - red - 256) / a.stage_bytes));
+  a.stage_bytes = ((16 * st + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
+  const int lut = (SliceFmt<F>::kLut + 127) & ~127, red = 2 * kW * 16 * 4;
+  a.stages = std::min(8, (kSmemBudgetMax - lut - red - 256) / a.stage_bytes);
+  if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "K too large for the single-row staging plan");
   a.off_stage = lut;
   a.off_red = lut + a.stages * a.stage_bytes;
   a.off_bar = a.off_red + red;
@@ -201,11 +204,23 @@ int run_iq2_r1(const void* x, const void* w, void* y, int N, int K, cudaStream_t
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   static std::atomic<uint64_t> done{0};
-  auto kern = iq2_r1_kernel<kW, kSPW>;
+  auto kern = slice_r1_kernel<F, kW, kSPW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
   cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3((kW + 1) * 32), smem, s, a);
-  if (e != cudaSuccess) return cuda_fail("Q4Gemv iq2=3 launch", e);
+  if (e != cudaSuccess) return cuda_fail("single-row GEMV launch", e);
   return GGUF_OK;
+}
+
+// Dispatches R = 1 to the slice kernel when K and the row size allow it; returns -1 otherwise.
+template <int F>
+int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s) {
+  if (!g_fast.load() || (K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes) % 16 != 0) return -1;
+  switch (K) {
+    case 2048: return run_slice_r1<F, 8, 1>(x, w, gscale, y, N, K, s);
+    case 4096: return run_slice_r1<F, 16, 1>(x, w, gscale, y, N, K, s);
+    case 5120: return run_slice_r1<F, 20, 1>(x, w, gscale, y, N, K, s);
+    default: return -1;
+  }
 }
 
 std::string dims(int64_t R, int64_t N, int64_t K) {
@@ -238,6 +253,10 @@ int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, 
     return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: needs B [N, (K/32)*34], K % 64 == 0 and 1..16 rows" + dims(R, N, K));
   if (!aligned(w, 16) || !aligned(x, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: x and w must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (R == 1) {
+    const int rc = try_slice_r1<kFmtQ8>(x, w, nullptr, y, (int)N, (int)K, s);
+    if (rc >= 0) return rc;
+  }
   return R <= 8 ? run_dense<kFmtQ8, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)
                 : run_dense<kFmtQ8, 2>(x, w, nullptr, y, (int)R, (int)N, (int)K, s);
 }
@@ -249,10 +268,9 @@ int gguf_iq2_xxs_gemv(const void* x, const void* w, void* y, int64_t R, int64_t 
     return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: needs B [N, (K/256)*66], K % 256 == 0 and 1..16 rows" + dims(R, N, K));
   if (!aligned(w, 16) || !aligned(x, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q4Gemv iq2=3: x and w must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (R == 1 && g_fast.load()) {
-    if (K == 4096) return run_iq2_r1<16, 1>(x, w, y, (int)N, (int)K, s);
-    if (K == 8192) return run_iq2_r1<16, 2>(x, w, y, (int)N, (int)K, s);
-    if (K == 2048) return run_iq2_r1<8, 1>(x, w, y, (int)N, (int)K, s);
+  if (R == 1) {
+    const int rc = try_slice_r1<kFmtIQ2>(x, w, nullptr, y, (int)N, (int)K, s);
+    if (rc >= 0) return rc;
   }
   return R <= 8 ? run_dense<kFmtIQ2, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)
                 : run_dense<kFmtIQ2, 2>(x, w, nullptr, y, (int)R, (int)N, (int)K, s);
@@ -267,6 +285,10 @@ int gguf_nvfp4_gemv(const void* x, const void* w, const float* gscale, void* y, 
   if (!aligned(w, 16) || !aligned(x, 16) || !aligned(gscale, 4))
     return fail(GGUF_ERR_INVALID_ARGUMENT, "Nvfp4Gemv gguf=1: x and w must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (R == 1) {
+    const int rc = try_slice_r1<kFmtFP4>(x, w, gscale, y, (int)N, (int)K, s);
+    if (rc >= 0) return rc;
+  }
   return R <= 8 ? run_dense<kFmtFP4, 1>(x, w, gscale, y, (int)R, (int)N, (int)K, s)
                 : run_dense<kFmtFP4, 2>(x, w, gscale, y, (int)R, (int)N, (int)K, s);
 }
@@ -287,7 +309,61 @@ int gguf_moe_route(const void* x, const float* gate_w, const float* bias, int32_
   return GGUF_OK;
 }
 
-int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w,
+namespace gguf_b200 {
+namespace {
+// MoeVerify iq2=3 as: zero the phase counters (first 4P bytes of out), one fused persistent kernel
+// (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.
+int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w, void* out,
+                  void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s) {
+  constexpr int H = 1024;
+  const int P = R * topk;
+  MoeFusedArgs a = {};
+  a.w1 = static_cast<const uint8_t*>(fc1_w);
+  a.w2 = static_cast<const uint8_t*>(fc2_w);
+  a.z = static_cast<const bf16*>(z);
+  a.idx = idx;
+  a.h = static_cast<bf16*>(h);
+  a.part = part;
+  a.meta = meta;
+  a.done = static_cast<int*>(out);
+  a.R = R;
+  a.topk = topk;
+  a.P = P;
+  a.E = E;
+  a.H = H;
+  a.I = I;
+  a.rb1 = H / 256 * 66;
+  a.rb2 = I / 256 * 66;
+  a.T1 = I / 16;
+  a.T2 = H / 16;
+  a.stage_bytes = ((16 * std::max(a.rb1, a.rb2) + 16) + 127) & ~127;
+  const int lut = 256 * 8 * 16, red = kKW * 128 * 4, grp = (5 * kMaxPairs + kMaxPairs * 8 + 8) * 4;
+  a.stages = std::min(8, (kSmemBudgetMax - lut - red - grp - 256) / a.stage_bytes);
+  if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
+  a.off_stage = lut;
+  a.off_red = lut + a.stages * a.stage_bytes;
+  a.off_bar = a.off_red + red;
+  a.off_grp = a.off_bar + 2 * a.stages * 8;
+  const size_t smem = a.off_grp + grp;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(P) * sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
+  static std::atomic<uint64_t> done{0};
+  auto kern = moe_fused_kernel<kKW>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
+  e = launch(kern, dim3(sms), dim3(kThreads), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+  e = launch(moe_finalize_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, s, static_cast<const float*>(part), weights,
+             idx, topk, H, E, static_cast<bf16*>(out));
+  if (e != cudaSuccess) return cuda_fail("MoeVerify finalize launch", e);
+  return GGUF_OK;
+}
+}  // namespace
+}  // namespace gguf_b200
+
+extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w,
                             void* out, void* h, float* part, int32_t* meta, int64_t R, int64_t E, int64_t I, int64_t topk,
                             void* stream) {
   t_last_error.clear();
@@ -301,6 +377,8 @@ int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const float* weig
   if (!aligned(fc1_w, 16) || !aligned(fc2_w, 16) || !aligned(z, 16) || !aligned(h, 16) || !aligned(part, 16))
     return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: tensors must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g_fast.load())
+    return run_moe_fused(z, idx, weights, fc1_w, fc2_w, out, h, part, meta, (int)R, (int)E, (int)I, (int)topk, s);
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   // fc1: h = relu2(z . W1[e]^T), W1 [E, I, H/256*66]

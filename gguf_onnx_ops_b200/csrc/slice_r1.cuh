@@ -1,0 +1,365 @@
+// Single-activation-row GEMV (R = 1, the decode case) for Q8_0, IQ2_XXS and NVFP4.
+//
+// Each of the kW consumer warps owns kSPW fixed 256-element K slices of every 16-row weight tile,
+// so its B fragments (x) stay in registers for the whole kernel.  With one activation row seven
+// of the eight MMA columns of m16n8k16 would be idle; they are used instead to separate eight
+// "groups" of 32 (or 16) elements: column c of the B operand holds x restricted to group c (a
+// block-diagonal B), so C[row, c] is the row's dot product with group c alone and a per-group
+// scale is applied once in fp32 after the MMAs.
+//
+// k-slot mapping: MMA slots (2t, 2t+1) <-> group t, slots (2t+8, 2t+9) <-> group t+4, each MMA
+// taking one element pair of every group.  Lane (g, t) therefore decodes groups t and t+4 of rows
+// g and g+8 ("records" 0..3 = [g, t], [g, t+4], [g+8, t], [g+8, t+4]) and supplies x[group t] as
+// b0 when g == t and x[group t+4] as b1 when g == t+4 (zero otherwise).  Its C registers hold
+// columns 2t and 2t+1 of rows g and g+8.
+//
+//   IQ2_XXS : slice = one super-block, group = 32-element sub-block.  A = exact signed grid
+//             magnitudes (codebook in shared memory, 8x replicated); per-group scale
+//             d*(0.5+s)*0.25 in the epilogue.  16 MMAs per slice.
+//   Q8_0    : slice = 8 blocks, group = block.  Each byte u = q + 128 is split into nibbles and
+//             each nibble pair becomes an exact bf16x2 with one LOP3:
+//             (v & 0x000F000F) | 0x43004300 = bf16(128 + lo), the high nibble gives bf16(2048 + 16 hi)
+//             (0x4500 | hi).  The MMA then sums (2176 + u) x = (q + 2304) x over the group; the
+//             epilogue subtracts 2304 * sum(x of the group) and scales by d.  32 MMAs per slice.
+//   NVFP4   : slice = 4 blocks = two halves of 8 sub-blocks of 16 (group = sub-block).  A nibble n
+//             gives the bf16 bit pattern of E2M1(n) * 2^-126 with (n * 0x1040) & 0x81C0; one
+//             bf16 multiply by the sub-block's UE4M3 scale * 2^110 makes it exact and normal
+//             (<= 6 significant bits), the epilogue multiplies by 2^16 * gscale.  16 MMAs per slice.
+//
+// Stage = one 16-row tile with the full K (per-row bulk copies into a padded stride).  The kW
+// partial sums of a tile are combined through a double-buffered shared-memory array (one named
+// barrier per tile).
+#pragma once
+
+#include "decode.cuh"
+
+namespace gguf_b200 {
+
+struct SliceArgs {
+  const uint8_t* w;
+  const bf16* x;
+  const float* gscale;  // NVFP4 only
+  bf16* y;
+  int N, K, row_bytes, tiles;
+  int stride, stage_bytes, stages;
+  int off_stage, off_red, off_bar;
+};
+
+template <int F>
+struct SliceFmt;
+template <>
+struct SliceFmt<kFmtIQ2> {
+  static constexpr int kSliceBytes = 66, kLut = 256 * 8 * 16;
+};
+template <>
+struct SliceFmt<kFmtQ8> {
+  static constexpr int kSliceBytes = 8 * 34, kLut = 0;
+};
+template <>
+struct SliceFmt<kFmtFP4> {
+  static constexpr int kSliceBytes = 4 * 36, kLut = 512;
+};
+
+// 8 bytes at a 2-byte aligned offset; `al` = offset is 4-byte aligned (warp-uniform)
+__device__ __forceinline__ uint2 lds8(const uint8_t* base, uint32_t off, bool al) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(base + (off & ~3u));
+  if (al) return make_uint2(w[0], w[1]);
+  const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+  return make_uint2(__funnelshift_r(w0, w1, 16), __funnelshift_r(w1, w2, 16));
+}
+// 32 bytes at a 2-byte aligned offset (alignment may differ per lane; branch free)
+__device__ __forceinline__ void lds32b(const uint8_t* base, uint32_t off, uint32_t (&q)[8]) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(base + (off & ~3u));
+  const uint32_t sh = (off & 2u) * 8u;
+  uint32_t prev = w[0];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t nxt = w[i + 1];
+    q[i] = __funnelshift_r(prev, nxt, sh);
+    prev = nxt;
+  }
+}
+// c ^ (a & m): a masked field merged into constant bits c (c may overlap the field: XOR there)
+__device__ __forceinline__ uint32_t lop_xm(uint32_t a, uint32_t m, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(r) : "r"(a), "r"(m), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t pair_lo(uint32_t w0, uint32_t w1) { return __byte_perm(w0, w1, 0x5410); }  // (w0.lo, w1.lo)
+__device__ __forceinline__ uint32_t pair_hi(uint32_t w0, uint32_t w1) { return __byte_perm(w0, w1, 0x7632); }  // (w0.hi, w1.hi)
+
+template <int F, int kW, int kSPW>
+__global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+  uint64_t* empty = full + a.stages;
+  uint8_t* stages = smem + a.off_stage;
+  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [2][kW][16]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kW) {
+    // ---------------- producer warp: one 16-row tile per stage, one bulk copy per row ----------------
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++it) {
+      const int s = static_cast<int>(it % a.stages);
+      const int rv = min(16, a.N - tile * 16);
+      if (lane == 0) {
+        if (it >= static_cast<uint32_t>(a.stages)) mbar_wait(&empty[s], ((it / a.stages) - 1) & 1, kSiteEmptyWait);
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes));
+      }
+      __syncwarp();
+      if (lane < rv)
+        bulk_g2s(stages + s * a.stage_bytes + lane * a.stride, a.w + (static_cast<int64_t>(tile) * 16 + lane) * a.row_bytes,
+                 a.row_bytes, &full[s]);
+    }
+    if (lane == 0) {
+      const uint32_t total = it;
+      const uint32_t first = total > static_cast<uint32_t>(a.stages) ? total - a.stages : 0u;
+      for (uint32_t j = first; j < total; ++j) mbar_wait(&full[j % a.stages], (j / a.stages) & 1, kSiteDrainWait);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  // format tables, built while the first tiles are in flight
+  if constexpr (F == kFmtIQ2) {  // codebook replicated 8x: conflict-free 16-byte lookups
+    uint4* lut = reinterpret_cast<uint4*>(smem);
+    const uint4* src = reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[0][0]);
+    for (int i = threadIdx.x; i < 256 * 8; i += kW * 32) lut[i] = src[i >> 3];
+  } else if constexpr (F == kFmtFP4) {
+    uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
+    for (int i = threadIdx.x; i < 256; i += kW * 32) sl[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));
+  }
+  if constexpr (SliceFmt<F>::kLut > 0) named_bar_sync(1, kW * 32);
+
+  const int g = lane >> 2, t = lane & 3;
+  const bool dlo = (g == t), dhi = (g == t + 4);
+  pdl_wait();  // x is produced by the previous kernel
+
+  // ---- B fragments of this warp's slices, in MMA order ----
+  uint32_t xa[kSPW][16], xb[kSPW][16];
+  float xoff[kSPW][2];  // Q8: 2304 * sum(x) of the lane's C columns (groups 2t, 2t+1)
+#pragma unroll
+  for (int j = 0; j < kSPW; ++j) {
+    const bf16* xs = a.x + (warp * kSPW + j) * 256;
+    if constexpr (F == kFmtFP4) {
+      // half h, group t: 16 elements; MMA order (0,2) (8,10) (1,3) (9,11) (4,6) (12,14) (5,7) (13,15)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0, u0 = v0, u1 = v0;
+        if (dlo) v0 = ldg128(xs + h * 128 + 16 * t), v1 = ldg128(xs + h * 128 + 16 * t + 8);
+        if (dhi) u0 = ldg128(xs + h * 128 + 16 * (t + 4)), u1 = ldg128(xs + h * 128 + 16 * (t + 4) + 8);
+        const uint32_t A[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        uint32_t* oa = &xa[j][8 * h];
+        uint32_t* ob = &xb[j][8 * h];
+        oa[0] = pair_lo(A[0], A[1]); oa[1] = pair_lo(A[4], A[5]); oa[2] = pair_hi(A[0], A[1]); oa[3] = pair_hi(A[4], A[5]);
+        oa[4] = pair_lo(A[2], A[3]); oa[5] = pair_lo(A[6], A[7]); oa[6] = pair_hi(A[2], A[3]); oa[7] = pair_hi(A[6], A[7]);
+        ob[0] = pair_lo(B[0], B[1]); ob[1] = pair_lo(B[4], B[5]); ob[2] = pair_hi(B[0], B[1]); ob[3] = pair_hi(B[4], B[5]);
+        ob[4] = pair_lo(B[2], B[3]); ob[5] = pair_lo(B[6], B[7]); ob[6] = pair_hi(B[2], B[3]); ob[7] = pair_hi(B[6], B[7]);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 va = make_uint4(0, 0, 0, 0), vb = va;
+        if (dlo) va = ldg128(xs + 32 * t + 8 * q);
+        if (dhi) vb = ldg128(xs + 32 * (t + 4) + 8 * q);
+        if constexpr (F == kFmtQ8) {  // pairs (e0,e2) (e1,e3) (e4,e6) (e5,e7) of these 8 elements
+          xa[j][4 * q + 0] = pair_lo(va.x, va.y); xa[j][4 * q + 1] = pair_hi(va.x, va.y);
+          xa[j][4 * q + 2] = pair_lo(va.z, va.w); xa[j][4 * q + 3] = pair_hi(va.z, va.w);
+          xb[j][4 * q + 0] = pair_lo(vb.x, vb.y); xb[j][4 * q + 1] = pair_hi(vb.x, vb.y);
+          xb[j][4 * q + 2] = pair_lo(vb.z, vb.w); xb[j][4 * q + 3] = pair_hi(vb.z, vb.w);
+        } else {  // IQ2: natural pairs (e0,e1) ... (e6,e7)
+          xa[j][4 * q + 0] = va.x; xa[j][4 * q + 1] = va.y; xa[j][4 * q + 2] = va.z; xa[j][4 * q + 3] = va.w;
+          xb[j][4 * q + 0] = vb.x; xb[j][4 * q + 1] = vb.y; xb[j][4 * q + 2] = vb.z; xb[j][4 * q + 3] = vb.w;
+        }
+      }
+    }
+    if constexpr (F == kFmtQ8) {
+      float sa = 0.f, sb = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        sa += bf16_lo(xa[j][i]) + bf16_hi(xa[j][i]);
+        sb += bf16_lo(xb[j][i]) + bf16_hi(xb[j][i]);
+      }
+      // group c's sum is on lane (g = c, t = c & 3): sa for c < 4, sb for c >= 4
+      const float mine = dlo ? sa : (dhi ? sb : 0.f);
+      const int c0 = 2 * t, c1 = 2 * t + 1;
+      xoff[j][0] = 2304.0f * __shfl_sync(0xffffffffu, mine, c0 * 4 + (c0 & 3));
+      xoff[j][1] = 2304.0f * __shfl_sync(0xffffffffu, mine, c1 * 4 + (c1 & 3));
+    } else {
+      xoff[j][0] = xoff[j][1] = 0.f;
+    }
+  }
+  float post = 1.0f;
+  if constexpr (F == kFmtFP4) post = 65536.0f * __ldg(a.gscale);
+  const uint32_t lut_lane = static_cast<uint32_t>(lane & 7) * 16u;
+  const uint16_t* fp4lut = reinterpret_cast<const uint16_t*>(smem);
+  const int q0 = (lane & ~3) | ((2 * t) & 3), q1 = (lane & ~3) | ((2 * t + 1) & 3);
+  const int sel_sh = t >= 2 ? 4 : 0;
+
+  uint32_t it = 0;
+  for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x, ++it) {
+    const int s = static_cast<int>(it % a.stages);
+    mbar_wait(&full[s], (it / a.stages) & 1, kSiteFullWait);
+    const uint8_t* st = stages + s * a.stage_bytes;
+    const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
+    float acc0 = 0.f, acc1 = 0.f;  // rows g, g+8
+#pragma unroll
+    for (int j = 0; j < kSPW; ++j) {
+      const int sl = warp * kSPW + j;
+      const uint32_t so = static_cast<uint32_t>(sl) * SliceFmt<F>::kSliceBytes;
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      if constexpr (F == kFmtIQ2) {
+        const bool al = (sl & 1) != 0;  // odd super-block: records 4-byte aligned
+        uint2 rc[4];
+        rc[0] = lds8(st, r0 + so + 2u + 8u * t, al);
+        rc[1] = lds8(st, r0 + so + 34u + 8u * t, al);
+        rc[2] = lds8(st, r1 + so + 2u + 8u * t, al);
+        rc[3] = lds8(st, r1 + so + 34u + 8u * t, al);
+        const uint32_t dbits = ld_u16(st, r0 + so) | (ld_u16(st, r1 + so) << 16);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint4 m[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) m[r] = *reinterpret_cast<const uint4*>(smem + lut_lane + (((rc[r].x >> (8 * e)) & 0xFFu) << 7));
+          uint32_t A[4][4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint32_t si = (rc[r].y >> (7 * e)) & 0x7Fu;
+            const uint32_t sb = si + (__popc(si) << 7);  // bits above bit 7 never reach bits 15 / 31 below
+            A[r][0] = m[r].x ^ ((sb * 0x40008000u) & 0x80008000u);
+            A[r][1] = m[r].y ^ ((sb * 0x10002000u) & 0x80008000u);
+            A[r][2] = m[r].z ^ ((sb * 0x04000800u) & 0x80008000u);
+            A[r][3] = m[r].w ^ ((sb * 0x01000200u) & 0x80008000u);
+          }
+#pragma unroll
+          for (int wd = 0; wd < 4; ++wd) {
+            const int i = 4 * e + wd;
+            mma_bf16_16816(c[i & 1], A[0][wd], A[2][wd], A[1][wd], A[3][wd], xa[j][i], xb[j][i], c[i & 1]);
+          }
+        }
+        const uint32_t mine = (rc[0].y >> 28) | ((rc[1].y >> 28) << 4) | ((rc[2].y >> 28) << 8) | ((rc[3].y >> 28) << 12);
+        const uint32_t p0 = __shfl_sync(0xffffffffu, mine, q0) >> sel_sh, p1 = __shfl_sync(0xffffffffu, mine, q1) >> sel_sh;
+        const float d0s = fp16_bits_to_f32(dbits & 0xFFFFu) * 0.25f, d1s = fp16_bits_to_f32(dbits >> 16) * 0.25f;
+        // 0.5 + s exactly: float(2^23 + s) - (2^23 - 0.5)
+        acc0 = fmaf(d0s * (__uint_as_float((p0 & 15u) | 0x4B000000u) - 8388607.5f), c[0][0] + c[1][0], acc0);
+        acc0 = fmaf(d0s * (__uint_as_float((p1 & 15u) | 0x4B000000u) - 8388607.5f), c[0][1] + c[1][1], acc0);
+        acc1 = fmaf(d1s * (__uint_as_float(((p0 >> 8) & 15u) | 0x4B000000u) - 8388607.5f), c[0][2] + c[1][2], acc1);
+        acc1 = fmaf(d1s * (__uint_as_float(((p1 >> 8) & 15u) | 0x4B000000u) - 8388607.5f), c[0][3] + c[1][3], acc1);
+      } else if constexpr (F == kFmtQ8) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {  // payload words 4*half .. 4*half+3 of each block
+          uint32_t q[4][4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint32_t off = (r < 2 ? r0 : r1) + so + 34u * static_cast<uint32_t>(t + 4 * (r & 1)) + 2u + 16u * half;
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(st + (off & ~3u));
+            const uint32_t sh = (off & 2u) * 8u;
+            const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+            q[r][0] = __funnelshift_r(w0, w1, sh);
+            q[r][1] = __funnelshift_r(w1, w2, sh);
+            q[r][2] = __funnelshift_r(w2, w3, sh);
+            q[r][3] = __funnelshift_r(w3, w4, sh);
+          }
+#pragma unroll
+          for (int wq = 0; wq < 4; ++wq) {
+            const int w = 4 * half + wq;  // payload word index: elements 4w..4w+3
+            uint32_t A[4][4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const uint32_t v = q[r][wq];
+              A[r][0] = lop_xm(v, 0x000F000Fu, 0x43004300u);                   // (e0, e2) low nibbles: 128 + lo
+              A[r][1] = lop_xm(v >> 4, 0x000F000Fu, 0x45084508u);              // (e0, e2) high: 2048 + 16 (hi ^ 8)
+              A[r][2] = lop_xm(v >> 8, 0x000F000Fu, 0x43004300u);              // (e1, e3) low
+              A[r][3] = lop_xm(v >> 12, 0x000F000Fu, 0x45084508u);             // (e1, e3) high
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int bi = 2 * w + (k >> 1);
+              mma_bf16_16816(c[k & 1], A[0][k], A[2][k], A[1][k], A[3][k], xa[j][bi], xb[j][bi], c[k & 1]);
+            }
+          }
+        }
+        // scales of the lane's C columns: blocks 2t, 2t+1 of rows g, g+8
+        const float d00 = fp16_bits_to_f32(ld_u16(st, r0 + so + 34u * (2 * t)));
+        const float d01 = fp16_bits_to_f32(ld_u16(st, r0 + so + 34u * (2 * t + 1)));
+        const float d10 = fp16_bits_to_f32(ld_u16(st, r1 + so + 34u * (2 * t)));
+        const float d11 = fp16_bits_to_f32(ld_u16(st, r1 + so + 34u * (2 * t + 1)));
+        acc0 = fmaf(d00, (c[0][0] + c[1][0]) - xoff[j][0], acc0);
+        acc0 = fmaf(d01, (c[0][1] + c[1][1]) - xoff[j][1], acc0);
+        acc1 = fmaf(d10, (c[0][2] + c[1][2]) - xoff[j][0], acc1);
+        acc1 = fmaf(d11, (c[0][3] + c[1][3]) - xoff[j][1], acc1);
+      } else {  // NVFP4
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          // records: group t = block 2h sub-block t, group t+4 = block 2h+1 sub-block t
+          uint2 nb[4];
+          uint32_t S[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint32_t bo = (r < 2 ? r0 : r1) + so + 36u * static_cast<uint32_t>(2 * h + (r & 1));
+            const uint32_t* w = reinterpret_cast<const uint32_t*>(st + bo + 4u + 8u * t);
+            nb[r] = make_uint2(w[0], w[1]);
+            const uint32_t sv = fp4lut[st[bo + t]];
+            S[r] = sv | (sv << 16);
+          }
+#pragma unroll
+          for (int ui = 0; ui < 2; ++ui) {
+            uint32_t A[4][4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const uint32_t v = ui ? nb[r].y : nb[r].x;
+              const uint32_t v8 = v >> 8;
+              // (b0, b2) low nibbles, (b0, b2) high, (b1, b3) low, (b1, b3) high -> E2M1 * 2^-126 patterns
+              A[r][0] = hmul2_bits(((v & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S[r]);
+              A[r][1] = hmul2_bits(((v & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S[r]);
+              A[r][2] = hmul2_bits(((v8 & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S[r]);
+              A[r][3] = hmul2_bits(((v8 & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S[r]);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int bi = 8 * h + 4 * ui + k;
+              mma_bf16_16816(c[k & 1], A[0][k], A[2][k], A[1][k], A[3][k], xa[j][bi], xb[j][bi], c[k & 1]);
+            }
+          }
+        }
+        acc0 += (c[0][0] + c[1][0]) + (c[0][1] + c[1][1]);
+        acc1 += (c[0][2] + c[1][2]) + (c[0][3] + c[1][3]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp no longer reads the stage
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    // double-buffered partials: buffer (it & 1) is read by warp 0 after this tile's barrier and
+    // rewritten only after the barrier of the tile after next, which warp 0 reaches once done.
+    float* rb = red + (it & 1) * kW * 16;
+    if (t == 0) {
+      rb[warp * 16 + g] = acc0;
+      rb[warp * 16 + g + 8] = acc1;
+    }
+    named_bar_sync(1, kW * 32);
+    if (threadIdx.x < 16) {
+      float v = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kW; ++w2) v += rb[w2 * 16 + threadIdx.x];
+      const int row = tile * 16 + threadIdx.x;
+      if (row < a.N) a.y[row] = __float2bfloat16(v * post);
+    }
+  }
+}
+
+}  // namespace gguf_b200

@@ -182,16 +182,22 @@ def test_invalid_row_count_raises(cuda):
         ops.Q4Gemv(x, w)
 
 
-@pytest.mark.parametrize("N,K", [(1, 2048), (37, 2048), (200, 4096), (14336, 4096), (77, 8192)])
-def test_iq2_single_row_fast_path(cuda, N, K):
-    """The R=1 IQ2_XXS kernel (block-diagonal super-block MMA) against the oracle and the generic engine."""
-    x, w, extra = I.gemv_case("iq2_xxs", 1, N, K, seed=N + K)
-    y_fast = run_gemv("iq2_xxs", x, w, extra, cuda)
+@pytest.mark.parametrize("op", ["q8_0", "iq2_xxs", "nvfp4"])
+@pytest.mark.parametrize("N,K,xscale", [(1, 2048, 1.0), (37, 2048, 1.0), (200, 4096, 1.0), (4096, 4096, 1.0),
+                                        (61, 5120, 1.0), (300, 4096, 3000.0), (50, 8192, 1.0)])
+def test_single_row_fast_path(cuda, op, N, K, xscale):
+    """The R=1 slice kernels (block-diagonal MMA columns, x resident in registers) against the oracle
+    and against the generic engine; xscale=3000 exercises outlier activations (Q8's offset trick)."""
+    if op == "nvfp4" and K % 64 or op == "iq2_xxs" and K % 256:
+        pytest.skip("shape")
+    _, w, extra = I.gemv_case(op, 1, N, K, seed=N + K)
+    x = I.bf16_normal(I.rng(N * K), (1, K), xscale)
+    y_fast = run_gemv(op, x, w, extra, cuda)
     rows = np.arange(N) if N <= 512 else np.sort(I.rng(3).choice(N, size=512, replace=False))
-    assert rel(y_fast[:, rows], oracle_y("iq2_xxs", x, w, extra, rows)) < TOL
+    assert rel(y_fast[:, rows], oracle_y(op, x, w, extra, rows)) < TOL
     ops.set_fast_paths(False)
     try:
-        y_gen = run_gemv("iq2_xxs", x, w, extra, cuda)
+        y_gen = run_gemv(op, x, w, extra, cuda)
     finally:
         ops.set_fast_paths(True)
     assert rel(y_fast, y_gen) < 2e-3
