@@ -14,7 +14,7 @@ N=14336 -- as weight-stream GB/s (algorithmic bytes = the weight tensor, 15,138,
   (all inside the captured step).
 * roofline = achieved GB/s of the GEMV kernel vs the measured HBM copy bandwidth in
   MEASURED_PEAKS.json; traffic (DRAM bytes per launch) comes from the committed ncu summary
-  profiles/traffic.json when present.
+  profiles/dram_traffic.json when present.
 * cpu_baseline = the oracle port of the reference's CPU path (gguf-py dequantise + fp32 matmul)
   on a bounded row sample, all host threads.
 * configs = every BASELINE config at 1 GPU (skipped with --quick or N > 1).
@@ -409,7 +409,7 @@ def peaks():
 
 def traffic_per_launch():
     try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+        with open(os.path.join(ROOT, "profiles", "dram_traffic.json")) as f:
             t = json.load(f)
         return t.get("C1_R1", {}).get("dram_bytes_per_launch")
     except Exception:  # noqa: BLE001
