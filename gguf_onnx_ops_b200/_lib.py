@@ -32,6 +32,7 @@ SIGNATURES = {
     "gguf_nvfp4_gemv": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_moe_route": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),
     "gguf_moe_verify_iq2_xxs": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "gguf_moe_verify_iq2_xxs_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "gguf_dequantize": (_I32, [_I32, _P, _P, _I64, _I64, _P]),
     "gguf_device_status": (_I32, [ctypes.POINTER(ctypes.c_int)]),
     "gguf_set_pdl": (None, [_I32]),

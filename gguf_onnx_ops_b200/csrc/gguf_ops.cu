@@ -435,6 +435,65 @@ extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const 
   return GGUF_OK;
 }
 
+// ---- MoeVerify with library-owned scratch (no device allocation by the caller or the library) ----
+// Some callers cannot allocate device memory around this op: a host binding without a CUDA
+// allocator (a cgo / JNI / FFI caller that only holds the model's weight and activation buffers), a
+// runtime whose allocator must not be entered on the decode path, or a graph that exposes only
+// `out`.  For them, h, part and meta live in one file-scope device array of this library, sized for
+// R * topk <= 128 pairs and I <= 4096.  The array is not zeroed and needs no zeroing: every call
+// writes all of h, part and meta that it later reads; the only state that must start at zero (the
+// per-expert completion counters kept in the first bytes of `out`) is cleared on the stream by each
+// call.  The array is shared by all calls on a device, so calls whose executions overlap (on
+// different streams, or from threads that do not order their streams) race on it.
+constexpr int64_t kNoAllocMaxPairs = 128, kNoAllocMaxInter = 4096, kNoAllocH = 1024;
+constexpr size_t kNoAllocHBytes = static_cast<size_t>(kNoAllocMaxPairs * kNoAllocMaxInter) * 2;  // bf16 h
+constexpr size_t kNoAllocPartBytes = static_cast<size_t>(kNoAllocMaxPairs * kNoAllocH) * 4;      // f32 part
+constexpr size_t kNoAllocMetaBytes = ((1 + 9 * kNoAllocMaxPairs) * 4 + 255) & ~size_t(255);     // i32 meta
+static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[kNoAllocHBytes + kNoAllocPartBytes + kNoAllocMetaBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_noalloc_ptr[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+// Address of this device's copy of the scratch array, looked up once per device with that device
+// current (cudaGetSymbolAddress, which may load the module on first use).
+int noalloc_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
+  if (dev < 0 || dev >= kMaxDevices) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (no-alloc): device ordinal out of range");
+  void* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+      e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail("MoeVerify (no-alloc) scratch address", e);
+      g_noalloc_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *ptr = p;
+  return GGUF_OK;
+}
+}  // namespace
+
+int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                                    const void* fc2_w, void* out, int64_t R, int64_t E, int64_t I, int64_t topk,
+                                    void* stream) {
+  t_last_error.clear();
+  if (R < 1 || topk < 1 || R * topk > kNoAllocMaxPairs || I > kNoAllocMaxInter)
+    return fail(GGUF_ERR_INVALID_ARGUMENT,
+                "MoeVerify (no-alloc): needs rows*topk <= 128 and I <= 4096 (the size of the library-owned scratch)");
+  void* base = nullptr;
+  const int rc = noalloc_scratch(&base);
+  if (rc != GGUF_OK) return rc;
+  uint8_t* b = static_cast<uint8_t*>(base);
+  return gguf_moe_verify_iq2_xxs(z, idx, weights, fc1_w, fc2_w, out, b, reinterpret_cast<float*>(b + kNoAllocHBytes),
+                                 reinterpret_cast<int32_t*>(b + kNoAllocHBytes + kNoAllocPartBytes), R, E, I, topk,
+                                 stream);
+}
+
 int gguf_dequantize(int type, const void* w, float* out, int64_t rows, int64_t K, void* stream) {
   t_last_error.clear();
   if (!w || !out || rows < 0 || K <= 0) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize: bad arguments");

@@ -97,6 +97,23 @@ GGUF_OPS_API int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, cons
                                          int64_t E, int64_t I, int64_t topk, void* stream);
 
 /*
+ * MoeVerify, iq2=3, for callers that cannot allocate device memory (no counterpart in the
+ * reference): the same computation and `out` as gguf_moe_verify_iq2_xxs, with h, part and meta held
+ * in a device array owned by this library instead of caller tensors.  For a host binding without a
+ * CUDA allocator, or a decode loop that must not enter an allocator.
+ * Limits: rows*topk <= 128 and I <= 4096 (larger sizes return GGUF_ERR_INVALID_ARGUMENT); the other
+ * contract terms of gguf_moe_verify_iq2_xxs apply.
+ * The first call on each device looks the array up (cudaGetSymbolAddress, with that device current)
+ * and should come before any stream capture.  The array is shared by every call on a device: calls
+ * whose executions may overlap (different streams, unordered threads) race on it and must be ordered
+ * by the caller.  Nothing in the array needs to start at zero; the per-call counters are cleared on
+ * the stream by each call.
+ */
+GGUF_OPS_API int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* idx, const float* weights,
+                                                 const void* fc1_w, const void* fc2_w, void* out, int64_t R, int64_t E,
+                                                 int64_t I, int64_t topk, void* stream);
+
+/*
  * Dequantise raw GGUF rows to f32 with the same device decoders the GEMVs use (debug / parity
  * entry point; no counterpart op in the reference).  type = GGUF_TYPE_*; w [rows, row_bytes(K)];
  * out f32 [rows, K].  Results are bit-identical to gguf-py 0.19.0 dequantize.
