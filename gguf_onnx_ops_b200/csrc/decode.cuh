@@ -149,4 +149,25 @@ __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
+// IQ2_XXS codebook (bf16x2) replicated 8x into shared memory: entry e, copy c at e*128 + c*16, so
+// the 8 lanes of each quarter-warp read distinct bank groups whatever entries they pick.  Called by
+// threads 0..kThreads-1; each issues all of its (L2-resident) loads before its first store, so the
+// fill costs one L2 round trip instead of one per iteration.
+template <int kThreads>
+__device__ __forceinline__ void fill_iq2_lut_bf16(uint8_t* smem, int tid) {
+  constexpr int kN = 256 * 8, kIt = (kN + kThreads - 1) / kThreads;
+  const uint4* src = reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[0][0]);
+  uint4 v[kIt];
+#pragma unroll
+  for (int j = 0; j < kIt; ++j) {
+    const int i = tid + j * kThreads;
+    v[j] = i < kN ? __ldg(src + (i >> 3)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int j = 0; j < kIt; ++j) {
+    const int i = tid + j * kThreads;
+    if (i < kN) reinterpret_cast<uint4*>(smem)[i] = v[j];
+  }
+}
+
 }  // namespace gguf_b200

@@ -158,11 +158,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineAr
     fence_mbar_init();
   }
   if constexpr (F == kFmtIQ2) {
-    // codebook replicated 8x: entry e, copy c at e*128 + c*16 -> the 8 lanes of each quarter-warp
-    // read distinct bank groups whatever entries they pick.
-    uint4* lut = reinterpret_cast<uint4*>(smem);
-    const uint4* src = reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[0][0]);
-    for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) lut[i] = src[i >> 3];
+    fill_iq2_lut_bf16<(KW + 1) * 32>(smem, threadIdx.x);
   } else if constexpr (F == kFmtFP4) {
     uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
     for (int i = threadIdx.x; i < 256; i += blockDim.x) sl[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));

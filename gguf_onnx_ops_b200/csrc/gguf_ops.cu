@@ -16,6 +16,8 @@
 #include "../../include/gguf_ops.h"
 #include "engine.cuh"
 #include "slice_r1.cuh"
+#include "slice_iq2_i8.cuh"
+#include "iq2_rowblock.cuh"
 #include "moe_fused.cuh"
 #include "small_kernels.cuh"
 
@@ -211,10 +213,81 @@ int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
   return GGUF_OK;
 }
 
+// IQ2_XXS R = 1 on the integer tensor cores (slice_iq2_i8.cuh); same staging plan as run_slice_r1.
+template <int kW>
+int run_slice_iq2_i8(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
+  SliceArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.x = static_cast<const bf16*>(x);
+  a.y = static_cast<bf16*>(y);
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 256 * 66;
+  a.tiles = (N + 15) / 16;
+  a.stride = a.row_bytes;  // whole-tile copies: rows contiguous in the stage
+  a.stage_bytes = ((16 * a.row_bytes + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
+  const int red_per_stage = kW * 16 * 4 + 4;  // reduction slot + counter
+  a.stages = std::min(8, (kSmemBudgetMax - kI8Lut - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "K too large for the single-row staging plan");
+  a.off_stage = kI8Lut;
+  a.off_red = kI8Lut + a.stages * a.stage_bytes;
+  a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = slice_iq2_i8_kernel<kW>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("single-row GEMV launch", e);
+  return GGUF_OK;
+}
+
+// IQ2_XXS R = 1, 16-row blocks owned by warp pairs (iq2_rowblock.cuh).  Returns -1 when the shape
+// does not fit its plan (K % 512, one stage of every pair in shared memory).
+int run_iq2_rowblock(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
+  if (K % 512 != 0) return -1;
+  RowBlockArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.x = static_cast<const bf16*>(x);
+  a.y = static_cast<bf16*>(y);
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 256 * 66;
+  a.blocks = (N + 15) / 16;
+  a.stage_bytes = ((16 * a.row_bytes + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
+  const int slices = K / 256;
+  const int xbytes = slices * 512 + slices * 8 * 8 + 64;
+  a.off_x = kI8Lut;
+  a.off_stage = (a.off_x + xbytes + 127) & ~127;
+  a.off_red = a.off_stage + kRbPairs * a.stage_bytes;
+  a.off_bar = a.off_red + kRbPairs * 16 * 4;
+  const size_t smem = a.off_bar + kRbPairs * 8;
+  if (smem > static_cast<size_t>(kSmemBudgetMax)) return -1;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = iq2_rowblock_kernel;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(sms), dim3(kRbWarps * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("single-row GEMV launch", e);
+  return GGUF_OK;
+}
+
 // Dispatches R = 1 to the slice kernel when K and the row size allow it; returns -1 otherwise.
 template <int F>
 int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s) {
-  if (!g_fast.load() || (K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes) % 16 != 0) return -1;
+  const int fast = g_fast.load();
+  if (!fast || (K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes) % 16 != 0) return -1;
+  if (F == kFmtIQ2 && fast == 3) return run_iq2_rowblock(x, w, y, N, K, s);
+  if (F == kFmtIQ2 && fast == 1) {
+    switch (K) {
+      case 2048: return run_slice_iq2_i8<8>(x, w, y, N, K, s);
+      case 4096: return run_slice_iq2_i8<16>(x, w, y, N, K, s);
+      case 5120: return run_slice_iq2_i8<20>(x, w, y, N, K, s);
+      default: return -1;
+    }
+  }
   switch (K) {
     case 2048: return run_slice_r1<F, 8, 1>(x, w, gscale, y, N, K, s);
     case 4096: return run_slice_r1<F, 16, 1>(x, w, gscale, y, N, K, s);
@@ -244,7 +317,7 @@ const char* gguf_last_error(void) { return t_last_error.c_str(); }
 
 void gguf_set_pdl(int enable) { g_pdl.store(enable ? 1 : 0); }
 
-void gguf_set_fast_paths(int enable) { g_fast.store(enable ? 1 : 0); }
+void gguf_set_fast_paths(int enable) { g_fast.store(enable < 0 ? 0 : (enable > 3 ? 1 : enable)); }
 
 int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K, void* stream) {
   t_last_error.clear();

@@ -54,11 +54,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) moe_fused_kernel(const MoeFu
     }
     fence_mbar_init();
   }
-  {
-    uint4* lut = reinterpret_cast<uint4*>(smem);
-    const uint4* src = reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[0][0]);
-    for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) lut[i] = src[i >> 3];
-  }
+  fill_iq2_lut_bf16<(KW + 1) * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
   moe_group(a.idx, a.P, a.E, a.topk, s_grp);  // ends with __syncthreads
   const int* s_uexp = s_grp + 3 * kMaxPairs;

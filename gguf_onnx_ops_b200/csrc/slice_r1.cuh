@@ -133,9 +133,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
   // ---------------- consumers ----------------
   // format tables, built while the first tiles are in flight
   if constexpr (F == kFmtIQ2) {  // codebook replicated 8x: conflict-free 16-byte lookups
-    uint4* lut = reinterpret_cast<uint4*>(smem);
-    const uint4* src = reinterpret_cast<const uint4*>(&g_iq2_mag_bf16[0][0]);
-    for (int i = threadIdx.x; i < 256 * 8; i += kW * 32) lut[i] = src[i >> 3];
+    fill_iq2_lut_bf16<kW * 32>(smem, threadIdx.x);
   } else if constexpr (F == kFmtFP4) {
     uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
     for (int i = threadIdx.x; i < 256; i += kW * 32) sl[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));

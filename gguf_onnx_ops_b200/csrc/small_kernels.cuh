@@ -14,7 +14,8 @@ namespace gguf_b200 {
 // warp w of CTA c selects the top-k of row (cluster row base + c*warps + w): iterative arg-max of
 // score + bias with ties to the lower expert index (src/bolt_ops.cu:459-510).
 // ---------------------------------------------------------------------------------------------
-constexpr int kRouteCtas = 8, kRouteRows = 8, kRouteWarps = 8;
+constexpr int kRouteCtas = 8, kRouteRows = 8, kRouteWarps = 16;
+constexpr int kRoutePre = 4;  // 256-element chunks of a warp's first gate row fetched before the dependency wait
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
@@ -29,16 +30,30 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
   const int row0 = cluster * kRouteRows;
   const int nrows = min(kRouteRows, R - row0);
   const int e_lo = (rank * E) / kRouteCtas, e_hi = ((rank + 1) * E) / kRouteCtas;
+  const int e_first = e_lo + warp;
+  // The gate weights do not depend on the previous kernel: this warp's first row (up to
+  // kRoutePre * 256 elements) is in flight before the dependency wait.
+  float4 pw[2 * kRoutePre];
+#pragma unroll
+  for (int c = 0; c < kRoutePre; ++c) {
+    const int k = c * 256 + lane * 8;
+    if (e_first < e_hi && k < K) {
+      const float* wr = gw + static_cast<int64_t>(e_first) * K + k;
+      pw[2 * c] = __ldg(reinterpret_cast<const float4*>(wr));
+      pw[2 * c + 1] = __ldg(reinterpret_cast<const float4*>(wr + 4));
+    } else {
+      pw[2 * c] = pw[2 * c + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   pdl_wait();
   pdl_launch_dependents();
-  for (int e = e_lo + warp; e < e_hi; e += kRouteWarps) {
+  for (int e = e_first; e < e_hi; e += kRouteWarps) {
     const float* wr = gw + static_cast<int64_t>(e) * K;
     float acc[kRouteRows];
 #pragma unroll
     for (int r = 0; r < kRouteRows; ++r) acc[r] = 0.f;
-    for (int k = lane * 8; k < K; k += 256) {
-      const float4 w0 = __ldg(reinterpret_cast<const float4*>(wr + k));
-      const float4 w1 = __ldg(reinterpret_cast<const float4*>(wr + k + 4));
+    // one 8-element chunk at k (this lane's elements k..k+7), accumulated in increasing k
+    auto chunk = [&](const float4 w0, const float4 w1, int k) {
       const float wb[8] = {round_bf16(w0.x), round_bf16(w0.y), round_bf16(w0.z), round_bf16(w0.w),
                            round_bf16(w1.x), round_bf16(w1.y), round_bf16(w1.z), round_bf16(w1.w)};
 #pragma unroll
@@ -53,7 +68,41 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
           }
         }
       }
+    };
+    int k0 = lane * 8;
+    if (e == e_first) {
+      // rows outer, chunks inner: acc[r] still accumulates in increasing k
+      float wb[kRoutePre][8];
+#pragma unroll
+      for (int c = 0; c < kRoutePre; ++c) {
+        const float4 w0 = pw[2 * c], w1 = pw[2 * c + 1];
+        wb[c][0] = round_bf16(w0.x); wb[c][1] = round_bf16(w0.y); wb[c][2] = round_bf16(w0.z); wb[c][3] = round_bf16(w0.w);
+        wb[c][4] = round_bf16(w1.x); wb[c][5] = round_bf16(w1.y); wb[c][6] = round_bf16(w1.z); wb[c][7] = round_bf16(w1.w);
+      }
+#pragma unroll
+      for (int r = 0; r < kRouteRows; ++r) {
+        if (r >= nrows) break;
+        uint4 xv[kRoutePre];
+#pragma unroll
+        for (int c = 0; c < kRoutePre; ++c)
+          xv[c] = c * 256 + lane * 8 < K ? ldg128(x + static_cast<int64_t>(row0 + r) * K + c * 256 + lane * 8)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int c = 0; c < kRoutePre; ++c) {
+          if (c * 256 + lane * 8 >= K) break;
+          const uint32_t xw[4] = {xv[c].x, xv[c].y, xv[c].z, xv[c].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[r] = fmaf(bf16_lo(xw[i]), wb[c][2 * i], acc[r]);
+            acc[r] = fmaf(bf16_hi(xw[i]), wb[c][2 * i + 1], acc[r]);
+          }
+        }
+      }
+      k0 += kRoutePre * 256;
     }
+#pragma unroll 2
+    for (int k = k0; k < K; k += 256)
+      chunk(__ldg(reinterpret_cast<const float4*>(wr + k)), __ldg(reinterpret_cast<const float4*>(wr + k + 4)), k);
 #pragma unroll
     for (int r = 0; r < kRouteRows; ++r) {
       float v = acc[r];

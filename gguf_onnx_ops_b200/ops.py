@@ -187,9 +187,12 @@ def set_pdl(enable: bool) -> None:
     load().gguf_set_pdl(1 if enable else 0)
 
 
-def set_fast_paths(enable: bool) -> None:
-    """Enable / disable the shape-specialised kernels (the generic engine handles every shape)."""
-    load().gguf_set_fast_paths(1 if enable else 0)
+def set_fast_paths(enable) -> None:
+    """Enable / disable the shape-specialised kernels (the generic engine handles every shape).
+
+    ``True`` / 1 = on (default), ``False`` / 0 = generic engine only, 2 = on, with the bf16 instead of
+    the integer tensor-core kernel for single-row IQ2_XXS (a cross-check of the two decoders)."""
+    load().gguf_set_fast_paths(int(enable) if not isinstance(enable, bool) else (1 if enable else 0))
 
 
 def device_status():

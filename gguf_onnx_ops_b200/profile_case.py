@@ -27,6 +27,7 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--copies", type=int, default=3)
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--fast-mode", type=int, default=1, help="gguf_set_fast_paths value (0 = generic engine)")
     a = ap.parse_args()
 
     import bench  # device weight generators with the BASELINE distributions
@@ -35,6 +36,7 @@ def main():
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     ops.set_pdl(not a.no_pdl)
+    ops.set_fast_paths(a.fast_mode)
     if a.op in ("moe", "route"):
         E, H, I, topk = 128, 1024, 1792, 6
         w1 = bench.gen_weights("iq2_xxs", E * I, H, seed=2, dev=dev).reshape(E, I, -1)

@@ -198,7 +198,38 @@ def test_single_row_fast_path(cuda, op, N, K, xscale):
     ops.set_fast_paths(False)
     try:
         y_gen = run_gemv(op, x, w, extra, cuda)
+        if op == "iq2_xxs":  # the other single-row kernels (modes 2, 3) against the default (mode 1)
+            for mode in (2, 3):
+                ops.set_fast_paths(mode)
+                y_alt = run_gemv(op, x, w, extra, cuda)
+                assert rel(y_fast, y_alt) < 2e-3, mode
     finally:
         ops.set_fast_paths(True)
     assert rel(y_fast, y_gen) < 2e-3
+    assert_device_ok()
+
+
+@pytest.mark.parametrize("case", ["wide_range", "zero_groups", "subnormal", "outlier_per_group"])
+def test_iq2_single_row_activation_ranges(cuda, case):
+    """Single-row IQ2_XXS carries each 32-element group of x as a 2-limb fixed-point integer scaled by
+    the group maximum: exact within 2^7 of the maximum, 2^-14 of the maximum below.  Activations with
+    a wide dynamic range inside groups, all-zero groups and subnormal groups stay within the op
+    tolerance of the fp64 oracle."""
+    N, K = 512, 4096
+    _, w, extra = I.gemv_case("iq2_xxs", 1, N, K, seed=11)
+    g = I.rng(99)
+    xf = g.standard_normal(K).astype(np.float32)
+    if case == "wide_range":
+        xf *= np.exp2(g.integers(-24, 12, K)).astype(np.float32)
+    elif case == "zero_groups":
+        xf.reshape(-1, 32)[::3] = 0.0
+    elif case == "subnormal":
+        xf.reshape(-1, 32)[::2] *= np.float32(2.0 ** -130)
+    else:
+        xf.reshape(-1, 32)[:, 5] *= 3000.0
+    x = O.bf16_bits(xf).reshape(1, K)
+    y = run_gemv("iq2_xxs", x, w, extra, cuda)
+    ref = oracle_y("iq2_xxs", x, w, extra, np.arange(N))
+    assert np.isfinite(y).all()
+    assert rel(y, ref) < TOL
     assert_device_ok()
