@@ -31,6 +31,12 @@ constexpr int kModeDense = 0, kModeMoe1 = 1, kModeMoe2 = 2;
 constexpr int kMaxPairs = 128;
 
 struct EngineArgs {
+  // Segmented staging through a 2-D tensor map over the weight bytes viewed as u64 elements
+  // [all rows, row_bytes / 8]: one copy request moves a 16-row x `stride`-byte box (the segment
+  // plus up to 16 bytes of the next one, which give the padded row pitch), instead of 16 row copies
+  // -- the copy engine's throughput per SM is bounded by requests in flight, not bytes.
+  CUtensorMap tmap;
+  int use_tmap;
   // weights
   const uint8_t* w;  // 16-byte aligned
   int K;             // reduction length
@@ -141,7 +147,7 @@ __device__ __forceinline__ void iq2_group_mma(const uint8_t* smem, const uint8_t
 }
 
 template <int F, int NT, int KW, int MODE>
-__global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineArgs a) {
+__global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_constant__ EngineArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   uint64_t* empty = full + a.stages;
@@ -224,12 +230,16 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const EngineAr
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&full[s], bulk);
             if (bulk) bulk_g2s(dst, src, bulk, &full[s]);
+          } else if (a.use_tmap) {
+            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(16 * a.stride));
+            const int row0 = static_cast<int>((src - a.w) / a.row_bytes);
+            tma_load_2d(dst, &a.tmap, sp * (a.seg_bytes / 8), row0, &full[s]);
           } else {
             mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.seg_bytes));
           }
         }
         __syncwarp();
-        if (!a.contiguous && lane < rv)
+        if (!a.contiguous && !a.use_tmap && lane < rv)
           bulk_g2s(dst + lane * a.stride, src + static_cast<int64_t>(sp) * a.seg_bytes + static_cast<int64_t>(lane) * a.row_bytes,
                    a.seg_bytes, &full[s]);
       }

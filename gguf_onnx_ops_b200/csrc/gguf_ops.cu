@@ -4,6 +4,8 @@
 // the reference ops in src/bolt_ops.cu), pick the staging plan of the engine, and enqueue the
 // kernels on the caller's stream with cudaLaunchKernelEx (programmatic dependent launch
 // attribute on by default).  No allocation, no synchronisation.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -155,6 +157,37 @@ int make_plan(EngineArgs& a, int K, int row_bytes, int NT, bool moe, size_t* sme
 
 bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 
+// cuTensorMapEncodeTiled from the driver (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Segmented engine staging through a 2-D tensor map (see EngineArgs::tmap): rows_total rows of
+// row_bytes (a multiple of 16) starting at a.w, boxes of 16 rows x a.stride bytes.  Leaves the
+// per-row copies in place when the plan or the driver does not allow it.
+void attach_tensor_map(EngineArgs& a, int64_t rows_total) {
+  a.use_tmap = 0;
+  if (a.contiguous || a.stride > 2048 || a.stride % 16 || a.row_bytes % 16 || a.seg_bytes % 16) return;
+  auto enc = tensor_map_encoder();
+  if (!enc) return;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.row_bytes / 8), static_cast<cuuint64_t>(rows_total)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(a.row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(a.stride / 8), 16u};
+  cuuint32_t estride[2] = {1u, 1u};
+  const CUresult r = enc(&a.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(a.w), dims, gstride, box,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) a.use_tmap = 1;
+}
+
 template <int F, int NT>
 int run_dense(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
   EngineArgs a = {};
@@ -164,6 +197,7 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
   a.w = static_cast<const uint8_t*>(w);
   a.rows = N;
   a.tiles = (N + 15) / 16;
+  attach_tensor_map(a, N);
   a.x = static_cast<const bf16*>(x);
   a.R = R;
   a.y = y;
@@ -462,6 +496,7 @@ extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const 
     a.w = static_cast<const uint8_t*>(fc1_w);
     a.rows = static_cast<int>(I);
     a.tiles = static_cast<int>((I + 15) / 16);
+    attach_tensor_map(a, E * I);
     a.x = static_cast<const bf16*>(z);
     a.R = static_cast<int>(R);
     a.y = h;
@@ -486,6 +521,7 @@ extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const 
     a.w = static_cast<const uint8_t*>(fc2_w);
     a.rows = H;
     a.tiles = H / 16;
+    attach_tensor_map(a, E * H);
     a.x = static_cast<const bf16*>(h);
     a.R = static_cast<int>(R);
     a.y = part;
