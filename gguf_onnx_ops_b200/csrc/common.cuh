@@ -1,5 +1,5 @@
 // Common device helpers for the GGUF decode kernels (sm_100a): PTX wrappers for mbarriers, bulk
-// async copies (TMA engine, no multicast), programmatic dependent launch, mma.sync, bounded waits
+// async copies (TMA engine, this CTA only), programmatic dependent launch, mma.sync, bounded waits
 // and the device-side error word.
 #pragma once
 
@@ -23,6 +23,7 @@ enum DeviceErrorSite : int {
   kSiteFullWait = 1,     // consumer waited too long for a weight stage
   kSiteEmptyWait = 2,    // producer waited too long for a free stage
   kSiteDrainWait = 3,    // producer waited too long for its last copies at exit
+  kSitePeerWait = 5,     // a sharded op waited too long for a peer GPU's completion flag
 };
 
 // A wait on an mbarrier that has not completed after this many nanoseconds is treated as a fault:
@@ -94,7 +95,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-// 2-D tiled tensor copy global -> shared (this CTA, no multicast): the box at element coordinates
+// 2-D tiled tensor copy global -> shared (this CTA only): the box at element coordinates
 // (x inner, y outer) of `map`; out-of-range elements are zero-filled and still counted in bytes.
 // x * element size must be a multiple of 16 bytes; dst 128-byte aligned.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -138,5 +139,62 @@ __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(_
 __device__ __forceinline__ uint4 ldg128(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ uint2 ldg64(const void* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
 __device__ __forceinline__ uint32_t ldg32(const void* p) { return __ldg(reinterpret_cast<const uint32_t*>(p)); }
+
+// ---------------------------------------------------------------------------------------------
+// Sharded outputs over peer memory (row-split GEMV with its all-gather fused into the epilogue)
+// ---------------------------------------------------------------------------------------------
+constexpr int kMaxPeers = 8;
+
+// Output of one shard of a row-split GEMV: every value is stored into the full-size y of every
+// GPU of the group (peer pointers from CUDA IPC, NVLink stores), then a flag protocol makes the
+// launch complete only when every peer's shard has landed in this GPU's y.
+struct PeerOut {
+  bf16* y[kMaxPeers];          // y of GPU p: [R, ld] bf16 (this shard's rows start at row0)
+  uint32_t* flags[kMaxPeers];  // flag array of GPU p: [kMaxPeers], slot q = last epoch GPU q finished
+  uint32_t* state;             // this GPU: [0] = completed epochs, [1] = CTAs of the running launch finished
+  int npeer, rank, ld, row0;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// y[col, row] of this shard (row local to the shard) into every GPU's output.
+__device__ __forceinline__ void peer_store(const PeerOut& po, int col, int row, bf16 v) {
+  const int64_t off = static_cast<int64_t>(col) * po.ld + po.row0 + row;
+#pragma unroll 1
+  for (int p = 0; p < po.npeer; ++p) po.y[p][off] = v;
+}
+
+// Called by one thread per CTA after the CTA's last peer_store (and a barrier over the threads that
+// stored).  The last CTA of the launch publishes this GPU's epoch to every peer and waits, bounded,
+// for every peer's; the launch therefore ends only once the whole y is present on this GPU.  Must
+// run after griddepcontrol.wait (the previous launch of the op updates state[0] last).
+__device__ __forceinline__ void peer_complete(const PeerOut& po) {
+  __threadfence_system();
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(po.state) + 1u;
+  const uint32_t done = atomicAdd(po.state + 1, 1u) + 1u;
+  if (done != gridDim.x) return;  // not the last CTA of this launch
+  __threadfence_system();
+  po.state[1] = 0u;  // the next launch counts from zero (it reaches this point only after griddepcontrol.wait)
+  for (int p = 0; p < po.npeer; ++p) st_release_sys(po.flags[p] + po.rank, epoch);
+  const uint32_t* mine = po.flags[po.rank];
+  const uint64_t t0 = global_timer_ns();
+  for (int p = 0; p < po.npeer; ++p) {
+    while (static_cast<int32_t>(ld_acquire_sys(mine + p) - epoch) < 0) {
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(kSitePeerWait);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  *reinterpret_cast<volatile uint32_t*>(po.state) = epoch;
+}
 
 }  // namespace gguf_b200

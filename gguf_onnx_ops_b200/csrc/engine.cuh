@@ -62,6 +62,7 @@ struct EngineArgs {
   const int32_t* idx;  // [R, topk]
   int topk, P, E;
   int32_t* meta;       // moe1: written by CTA 0
+  PeerOut po;          // dense, npeer > 0: row-split shard stored into every GPU of the group
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
@@ -365,7 +366,8 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
       const int row = tile * 16 + rl;
       if (row >= a.rows || col >= a.R) continue;
       if constexpr (MODE == kModeDense) {
-        reinterpret_cast<bf16*>(a.y)[static_cast<int64_t>(col) * a.rows + row] = __float2bfloat16(v * post);
+        if (a.po.npeer) peer_store(a.po, col, row, __float2bfloat16(v * post));
+        else reinterpret_cast<bf16*>(a.y)[static_cast<int64_t>(col) * a.rows + row] = __float2bfloat16(v * post);
       } else {
         const int p = s_pair[u * 8 + col];
         if (p < 0) continue;
@@ -379,6 +381,9 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
       }
     }
     named_bar_sync(1, KW * 32);
+  }
+  if constexpr (MODE == kModeDense) {
+    if (a.po.npeer && threadIdx.x == 0) peer_complete(a.po);  // stores are behind the last barrier
   }
 }
 

@@ -189,8 +189,10 @@ void attach_tensor_map(EngineArgs& a, int64_t rows_total) {
 }
 
 template <int F, int NT>
-int run_dense(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
+int run_dense(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s,
+              const PeerOut* po = nullptr) {
   EngineArgs a = {};
+  if (po) a.po = *po;
   size_t smem = 0;
   int rc = make_plan<F>(a, K, K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes, NT, false, &smem);
   if (rc) return rc;
@@ -216,8 +218,10 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
 
 // One activation row: slice kernel (slice_r1.cuh), K = 256 * kW * kSPW, rows 16-byte multiples.
 template <int F, int kW, int kSPW>
-int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s) {
+int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s,
+                 const PeerOut* po = nullptr) {
   SliceArgs a = {};
+  if (po) a.po = *po;
   a.w = static_cast<const uint8_t*>(w);
   a.x = static_cast<const bf16*>(x);
   a.gscale = gscale;
@@ -328,6 +332,23 @@ int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
     case 5120: return run_slice_r1<F, 20, 1>(x, w, gscale, y, N, K, s);
     default: return -1;
   }
+}
+
+// Row-split shard: the bf16 slice kernel for R = 1 (K in its instantiated set), else the engine.
+template <int F>
+int run_rowsplit(const void* x, const void* w, const float* gscale, int R, int rows, int K, cudaStream_t s,
+                 const PeerOut& po) {
+  const bool slice_ok = R == 1 && (K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes) % 16 == 0;
+  if (slice_ok) {
+    switch (K) {
+      case 2048: return run_slice_r1<F, 8, 1>(x, w, gscale, nullptr, rows, K, s, &po);
+      case 4096: return run_slice_r1<F, 16, 1>(x, w, gscale, nullptr, rows, K, s, &po);
+      case 5120: return run_slice_r1<F, 20, 1>(x, w, gscale, nullptr, rows, K, s, &po);
+      default: break;
+    }
+  }
+  return R <= 8 ? run_dense<F, 1>(x, w, gscale, nullptr, R, rows, K, s, &po)
+                : run_dense<F, 2>(x, w, gscale, nullptr, R, rows, K, s, &po);
 }
 
 std::string dims(int64_t R, int64_t N, int64_t K) {
@@ -601,6 +622,88 @@ int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* idx, const flo
   return gguf_moe_verify_iq2_xxs(z, idx, weights, fc1_w, fc2_w, out, b, reinterpret_cast<float*>(b + kNoAllocHBytes),
                                  reinterpret_cast<int32_t*>(b + kNoAllocHBytes + kNoAllocPartBytes), R, E, I, topk,
                                  stream);
+}
+
+int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float* gscale, const GgufPeerOut* out,
+                       int64_t R, int64_t rows, int64_t K, void* stream) {
+  t_last_error.clear();
+  if (!x || !w_shard || !out) return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: null pointer");
+  if (out->world < 1 || out->world > kMaxPeers || out->rank < 0 || out->rank >= out->world)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 1 <= world <= 8 and 0 <= rank < world");
+  if (!out->state || rows < 1 || out->row0 < 0 || out->row0 + rows > out->n_total || !int_range(out->n_total))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 0 <= row0, row0 + rows <= n_total and a state array");
+  for (int p = 0; p < out->world; ++p)
+    if (!out->y[p] || !out->flags[p]) return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: null peer buffer");
+  if (R < 1 || R > 16 || K <= 0 || !int_range(K) || !aligned(w_shard, 16) || !aligned(x, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 1..16 rows and 16-byte aligned x and w");
+  PeerOut po = {};
+  for (int p = 0; p < out->world; ++p) {
+    po.y[p] = static_cast<bf16*>(out->y[p]);
+    po.flags[p] = out->flags[p];
+  }
+  po.state = out->state;
+  po.npeer = out->world;
+  po.rank = out->rank;
+  po.ld = static_cast<int>(out->n_total);
+  po.row0 = static_cast<int>(out->row0);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (type) {
+    case GGUF_TYPE_Q8_0:
+      if (K % 64) break;
+      return run_rowsplit<kFmtQ8>(x, w_shard, nullptr, (int)R, (int)rows, (int)K, s, po);
+    case GGUF_TYPE_IQ2_XXS:
+      if (K % 256) break;
+      return run_rowsplit<kFmtIQ2>(x, w_shard, nullptr, (int)R, (int)rows, (int)K, s, po);
+    case GGUF_TYPE_NVFP4:
+      if (K % 64 || !gscale) break;
+      return run_rowsplit<kFmtFP4>(x, w_shard, gscale, (int)R, (int)rows, (int)K, s, po);
+    default:
+      return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: unknown GGUF type");
+  }
+  return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: K does not match the format's block size (or gscale missing)");
+}
+
+int gguf_ipc_get_handle(const void* dev_ptr, void* handle64, int64_t* offset) {
+  t_last_error.clear();
+  if (!dev_ptr || !handle64 || !offset) return fail(GGUF_ERR_INVALID_ARGUMENT, "ipc: null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+  if (e != cudaSuccess) return cuda_fail("cudaIpcGetMemHandle", e);
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle64, &h, sizeof(h));
+  // the handle names the whole allocation; the peer opens its base, so report where dev_ptr lies
+  static PFN_cuMemGetAddressRange_v3020 range = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  }();
+  if (!range) return fail(GGUF_ERR_CUDA, "ipc: cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(GGUF_ERR_CUDA, "ipc: cuMemGetAddressRange failed");
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return GGUF_OK;
+}
+
+int gguf_ipc_open(const void* handle64, void** dev_ptr) {
+  t_last_error.clear();
+  if (!handle64 || !dev_ptr) return fail(GGUF_ERR_INVALID_ARGUMENT, "ipc: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail("cudaIpcOpenMemHandle", e);
+  return GGUF_OK;
+}
+
+int gguf_ipc_close(void* dev_ptr) {
+  t_last_error.clear();
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) return cuda_fail("cudaIpcCloseMemHandle", e);
+  return GGUF_OK;
 }
 
 int gguf_dequantize(int type, const void* w, float* out, int64_t rows, int64_t K, void* stream) {

@@ -43,6 +43,7 @@ struct SliceArgs {
   int N, K, row_bytes, tiles;
   int stride, stage_bytes, stages;
   int off_stage, off_red, off_bar;
+  PeerOut po;  // npeer > 0: row-split shard, y stored into every GPU of the group (slice_r1_kernel)
 };
 
 template <int F>
@@ -355,8 +356,15 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
 #pragma unroll
       for (int w2 = 0; w2 < kW; ++w2) v += rb[w2 * 16 + threadIdx.x];
       const int row = tile * 16 + threadIdx.x;
-      if (row < a.N) a.y[row] = __float2bfloat16(v * post);
+      if (row < a.N) {
+        if (a.po.npeer) peer_store(a.po, 0, row, __float2bfloat16(v * post));
+        else a.y[row] = __float2bfloat16(v * post);
+      }
     }
+  }
+  if (a.po.npeer) {  // all-gather completion: every consumer's stores are behind the barrier
+    named_bar_sync(1, kW * 32);
+    if (threadIdx.x == 0) peer_complete(a.po);
   }
 }
 

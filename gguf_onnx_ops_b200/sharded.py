@@ -1,0 +1,126 @@
+"""Multi-GPU sharding of the GGUF decode path (one process per GPU).
+
+The reference runs on one GPU; the two sharded patterns here are the row-split GEMV of a large
+output (the Q8 LM head) and -- through the same peer-memory machinery -- its building blocks.
+torch.distributed is the plumbing only: it exchanges CUDA IPC handles once at set-up.  The data
+path is a single kernel per call that computes this GPU's rows and stores them straight into the
+output of every GPU of the group over NVLink, then waits (bounded) for the peers' flags.
+
+    shard = shard_rows(n_total, world, rank)          # (row0, rows) of this rank
+    op = RowSplitGemv(GGUF_TYPE_Q8_0, w_full[row0:row0 + rows], n_total, row0, K, r_max=16)
+    y = op(x)                                          # [R, n_total] bf16, complete on every GPU
+
+Every rank must construct the op and call it the same number of times in the same order.  The
+output alternates between two buffers (a peer may start call e+1 while this GPU still reads the y
+of call e); the returned tensor is valid until the call after next.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import check, load
+from .ops import IQ2_XXS_BYTES, NVFP4_BYTES, Q8_0_BYTES
+
+MAX_PEERS = 8
+_FMT = {_lib.GGUF_TYPE_Q8_0: (32, Q8_0_BYTES), _lib.GGUF_TYPE_IQ2_XXS: (256, IQ2_XXS_BYTES),
+        _lib.GGUF_TYPE_NVFP4: (64, NVFP4_BYTES)}
+
+
+def shard_rows(n_total: int, world: int, rank: int, align: int = 16) -> tuple[int, int]:
+    """Contiguous, balanced split of n_total output rows; every boundary but the last is a multiple
+    of `align` (the kernels' 16-row tiles)."""
+    if not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    units = -(-n_total // align)
+    lo = (units * rank) // world * align
+    hi = n_total if rank == world - 1 else (units * (rank + 1)) // world * align
+    return min(lo, n_total), max(0, min(hi, n_total) - min(lo, n_total))
+
+
+def exchange(payload, group=None) -> list:
+    """all_gather_object of a picklable payload (the set-up step; works on gloo and NCCL groups)."""
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, payload, group=group)
+    return out
+
+
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    h = (ctypes.c_char * 64)()
+    off = ctypes.c_int64(0)
+    check(load().gguf_ipc_get_handle(ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)))
+    return bytes(h), off.value
+
+
+def ipc_open(handle: bytes, offset: int) -> tuple[int, int]:
+    """(pointer to use, base to close)."""
+    p = ctypes.c_void_p(0)
+    check(load().gguf_ipc_open(ctypes.c_char_p(handle), ctypes.byref(p)))
+    return p.value + offset, p.value
+
+
+class RowSplitGemv:
+    """Row-split GEMV over raw GGUF rows with the all-gather fused into the kernel (see module doc)."""
+
+    def __init__(self, gguf_type: int, w_shard: torch.Tensor, n_total: int, row0: int, K: int, r_max: int = 16,
+                 gscale: torch.Tensor | None = None, group=None):
+        if gguf_type not in _FMT:
+            raise ValueError("unknown GGUF type")
+        blk, nbytes = _FMT[gguf_type]
+        self.type, self.K, self.n_total, self.row0 = gguf_type, K, n_total, row0
+        self.rows = w_shard.shape[0]
+        if w_shard.dtype != torch.uint8 or w_shard.numel() != self.rows * (K // blk) * nbytes:
+            raise ValueError("w_shard must be raw GGUF rows [rows, (K/block)*type_size] (uint8)")
+        self.w, self.gscale, self.group = w_shard.contiguous(), gscale, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > MAX_PEERS:
+            raise ValueError("at most 8 GPUs per group")
+        dev = w_shard.device
+        self.r_max = r_max
+        self.y = [torch.empty(r_max, n_total, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        self.flags = torch.zeros(MAX_PEERS, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        mine = [ipc_handle(self.y[0]), ipc_handle(self.y[1]), ipc_handle(self.flags)]
+        allh = exchange(mine, group)
+        self._opened = []
+        self._po = [_lib.GgufPeerOut(), _lib.GgufPeerOut()]
+        for p, hs in enumerate(allh):
+            ptrs = []
+            for (h, off), own in zip(hs, (self.y[0], self.y[1], self.flags)):
+                if p == self.rank:
+                    ptrs.append(own.data_ptr())
+                else:
+                    ptr, base = ipc_open(h, off)
+                    self._opened.append(base)
+                    ptrs.append(ptr)
+            for b in range(2):
+                self._po[b].y[p] = ptrs[b]
+                self._po[b].flags[p] = ptrs[2]
+        for po in self._po:
+            po.state = self.state.data_ptr()
+            po.world, po.rank = self.world, self.rank
+            po.n_total, po.row0 = n_total, row0
+        self.calls = 0
+
+    def __call__(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        R = x.shape[0]
+        if x.dtype != torch.bfloat16 or x.shape[1] != self.K or not 1 <= R <= self.r_max:
+            raise ValueError("x must be bf16 [R, K] with R <= r_max")
+        b = self.calls & 1
+        s = (stream or torch.cuda.current_stream()).cuda_stream
+        gs = ctypes.c_void_p(self.gscale.data_ptr()) if self.gscale is not None else None
+        check(load().gguf_gemv_rowsplit(self.type, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(self.w.data_ptr()), gs,
+                                        ctypes.byref(self._po[b]), R, self.rows, self.K, ctypes.c_void_p(s)))
+        self.calls += 1
+        return self.y[b][:R]
+
+    def close(self) -> None:
+        for base in self._opened:
+            load().gguf_ipc_close(ctypes.c_void_p(base))
+        self._opened = []

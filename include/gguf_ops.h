@@ -114,6 +114,38 @@ GGUF_OPS_API int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* i
                                                  int64_t I, int64_t topk, void* stream);
 
 /*
+ * Row-split (tensor-parallel) GEMV with the all-gather fused into the kernel (no counterpart in the
+ * reference, which runs on one GPU; SURVEY row-split of the LM-head-sized Q8Gemv).  GPU `rank` of
+ * `world` holds rows [row0, row0 + rows) of W (w_shard, raw GGUF rows) and computes those outputs
+ * for all R activation rows; every value is stored directly into the full y [R, n_total] of every
+ * GPU of the group (peer pointers opened with gguf_ipc_open, NVLink stores), and the launch ends
+ * only when every peer's shard has landed in this GPU's y (epoch flags, bounded waits reported
+ * through gguf_device_status).  All GPUs of the group must issue the same sequence of calls.
+ * Double buffering: a peer that finished call e may start call e+1 while this GPU still reads the
+ * y of call e, so consecutive calls must alternate between two y buffers (flags and state are
+ * shared by the two).
+ */
+typedef struct {
+  void* y[8];           /* y of GPU p (bf16 [R, n_total]); y[rank] = this GPU's own buffer */
+  uint32_t* flags[8];   /* flag array of GPU p: uint32 [8], zero-initialised, shared by all calls */
+  uint32_t* state;      /* this GPU: uint32 [2], zero-initialised, shared by all calls */
+  int world, rank;
+  int64_t n_total, row0;
+} GgufPeerOut;
+
+/* type = GGUF_TYPE_*; gscale for NVFP4 only.  Contract as the single-GPU GEMV of that type, plus
+ * 1 <= world <= 8, 0 <= rank < world, row0 + rows <= n_total. */
+GGUF_OPS_API int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float* gscale,
+                                    const GgufPeerOut* out, int64_t R, int64_t rows, int64_t K, void* stream);
+
+/* CUDA IPC plumbing for the peer pointers: the 64-byte handle of the device allocation holding
+ * dev_ptr and dev_ptr's offset in it; open a peer's handle in this process (returns the allocation
+ * base: add the peer's offset; peer access is enabled lazily); close an opened handle. */
+GGUF_OPS_API int gguf_ipc_get_handle(const void* dev_ptr, void* handle64, int64_t* offset);
+GGUF_OPS_API int gguf_ipc_open(const void* handle64, void** dev_ptr);
+GGUF_OPS_API int gguf_ipc_close(void* dev_ptr);
+
+/*
  * Dequantise raw GGUF rows to f32 with the same device decoders the GEMVs use (debug / parity
  * entry point; no counterpart op in the reference).  type = GGUF_TYPE_*; w [rows, row_bytes(K)];
  * out f32 [rows, K].  Results are bit-identical to gguf-py 0.19.0 dequantize.

@@ -1,0 +1,70 @@
+"""Worker for tests/test_gpu_dist.py: one process per GPU (launched by torch.distributed.run).
+
+Every rank builds the same seeded weights, keeps its row shard, and checks the row-split GEMV with
+the fused peer-store all-gather against the single-GPU op on the full matrix, over several calls
+(both output buffers)."""
+
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from gguf_onnx_ops_b200 import _lib, ops  # noqa: E402
+from gguf_onnx_ops_b200.sharded import RowSplitGemv, shard_rows  # noqa: E402
+from oracle import inputs as I  # noqa: E402
+
+TYPES = {"q8_0": _lib.GGUF_TYPE_Q8_0, "iq2_xxs": _lib.GGUF_TYPE_IQ2_XXS, "nvfp4": _lib.GGUF_TYPE_NVFP4}
+
+
+def single(op, x, w, gs):
+    if op == "q8_0":
+        return ops.Q8Gemv(x, w)
+    if op == "iq2_xxs":
+        return ops.Q4Gemv(x, w)
+    return ops.Nvfp4Gemv(x, w, None, gs)
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dev = torch.device("cuda", rank)
+    failures = []
+    for op, N, K, Rs in (("q8_0", 8192, 4096, (1, 4, 16)), ("iq2_xxs", 4096, 4096, (1, 8)), ("nvfp4", 2048, 5120, (1, 3)),
+                         ("q8_0", 1000, 1024, (2,))):
+        _, w, extra = I.gemv_case(op, 1, N, K, seed=N + K)
+        wt = torch.from_numpy(w).to(dev)
+        gs = torch.from_numpy(extra.get("gscale", np.array([1.0 / 448.0], np.float32))).to(dev)
+        row0, rows = shard_rows(N, world, rank)
+        sharded = RowSplitGemv(TYPES[op], wt[row0:row0 + rows], N, row0, K, r_max=16, gscale=gs)
+        for R in Rs:
+            for it in range(3):
+                x = torch.from_numpy(I.bf16_normal(I.rng(100 * R + it), (R, K)).view(np.int16)).view(torch.bfloat16).to(dev)
+                y = sharded(x)
+                ref = single(op, x, wt, gs)
+                torch.cuda.synchronize()
+                if op == "iq2_xxs" and R == 1:  # single GPU runs the integer kernel, the shard the bf16 one
+                    err = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
+                    ok = err < 2e-3
+                else:
+                    ok = torch.equal(y, ref)
+                if not ok:
+                    failures.append((op, N, K, R, it))
+        sharded.close()
+    rc, site = _lib.device_status()
+    if rc:
+        failures.append(("device status", rc, site))
+    dist.barrier()
+    dist.destroy_process_group()
+    if failures:
+        print(f"rank {rank} FAILED {failures}", flush=True)
+        sys.exit(1)
+    print(f"rank {rank} ok", flush=True)
+
+
+if __name__ == "__main__":
+    main()
