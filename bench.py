@@ -20,7 +20,9 @@ N=14336 -- as weight-stream GB/s (algorithmic bytes = the weight tensor, 15,138,
 * configs = every BASELINE config at 1 GPU (skipped with --quick or N > 1).
 
 N > 1 (torchrun): config 1 does not shard (replicas only): every rank runs the same workload on its
-own GPU; the timing is the max over ranks.
+own GPU; the timing is the max over ranks.  The line then also carries "sharded": the C4 LM head
+(Q8_0, N=131072) row-split over the N GPUs with the all-gather fused into the GEMV kernel, next to
+the same GEMV followed by an NCCL all-gather.
 ``--impl reference`` times the reference's CPU path (oracle port) on the same metric.
 """
 
@@ -276,6 +278,65 @@ def bench_gemv(op, R, N, K, steps, warmup, dev, target_step_ms=8.0, world=1, sam
     return out, (ws, x, ys, gs, wbytes, copies)
 
 
+def bench_rowsplit(R, steps, warmup, dev, world, rank):
+    """C4 LM head (Q8_0, N=131072, K=4096) row-split over the group: per call, each GPU streams its
+    N/world rows and stores its y shard into every GPU's y inside the same kernel (NVLink peer
+    stores + epoch flags).  Baseline: the same per-GPU GEMV into a local shard followed by an NCCL
+    all-gather (both captured in CUDA graphs).  Times are the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from gguf_onnx_ops_b200 import _lib, ops
+    from gguf_onnx_ops_b200.sharded import RowSplitGemv, shard_rows
+
+    N, K = 131072, 4096
+    row0, rows = shard_rows(N, world, rank)
+    wbytes = rows * ROW_BYTES["q8_0"](K)
+    copies = n_copies(wbytes)
+    copies += copies & 1  # an even number of calls per pass keeps the double-buffer parity fixed
+    base = gen_weights("q8_0", rows, K, seed=1 + rank, dev=dev)
+    ws = replicate(base, copies)
+    del base
+    x = torch.randn(R, K, device=dev).bfloat16()
+    op = RowSplitGemv(_lib.GGUF_TYPE_Q8_0, ws[0], N, row0, K, r_max=R)
+
+    def fused_pass():
+        for w in ws:
+            op(x, w=w)
+
+    g = capture(fused_pass)
+    ms = max_over_ranks(time_graph(g, steps, warmup, world), world)
+    del g
+    fused_us = ms * 1e3 / (steps * copies)
+    y_local = torch.empty(R, rows, dtype=torch.bfloat16, device=dev)
+    y_all = torch.empty(world * R * rows, dtype=torch.bfloat16, device=dev)
+    nccl_us, nccl_err = None, None
+    if R == 1 and N % world == 0:
+        dist.all_gather_into_tensor(y_all, y_local.view(-1))  # warm the communicator outside capture
+        torch.cuda.synchronize()
+
+        def nccl_pass():
+            for w in ws:
+                ops.q8_0_gemv_into(x, w, y_local, R, rows, K)
+                dist.all_gather_into_tensor(y_all, y_local.view(-1))
+
+        try:
+            g2 = capture(nccl_pass)
+            ms2 = max_over_ranks(time_graph(g2, steps, warmup, world), world)
+            del g2  # graphs holding NCCL calls are released before the process group
+            nccl_us = ms2 * 1e3 / (steps * copies)
+        except Exception as e:  # noqa: BLE001 -- the baseline is optional; report why it is missing
+            nccl_us = None
+            nccl_err = f"{type(e).__name__}: {str(e)[:160]}"
+    torch.cuda.synchronize()
+    rc, site = _lib.device_status()
+    op.close()
+    total = N * ROW_BYTES["q8_0"](K)
+    return dict(world=world, R=R, fused_us_per_call=fused_us, fused_gbs=total / (fused_us * 1e-6) / 1e9,
+                nccl_us_per_call=nccl_us, nccl_gbs=None if nccl_us is None else total / (nccl_us * 1e-6) / 1e9,
+                rows_per_gpu=rows, copies=copies, device_status=rc, **({"nccl_error": nccl_err} if nccl_err else {}))
+
+
 def bench_e2e_gemv(op, R, N, K, steps, warmup, dev, state):
     """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host."""
     import torch
@@ -490,6 +551,9 @@ def main():
                 cfgs[f"C3_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()}
                 torch.cuda.empty_cache()
             line["configs"] = cfgs
+    if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather
+        line["sharded"] = {f"C4_R{R}": bench_rowsplit(R, max(5, args.steps // 2), args.warmup, dev, world, rank)
+                           for R in (1, 4)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

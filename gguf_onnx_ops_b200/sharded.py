@@ -108,14 +108,18 @@ class RowSplitGemv:
             po.n_total, po.row0 = n_total, row0
         self.calls = 0
 
-    def __call__(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, w: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """y = x @ W^T over the whole group; `w` optionally replaces the shard (same shape and type)."""
         R = x.shape[0]
         if x.dtype != torch.bfloat16 or x.shape[1] != self.K or not 1 <= R <= self.r_max:
             raise ValueError("x must be bf16 [R, K] with R <= r_max")
+        w = self.w if w is None else w
+        if w.shape != self.w.shape or w.dtype != torch.uint8 or not w.is_contiguous():
+            raise ValueError("w must have the shard's shape")
         b = self.calls & 1
         s = (stream or torch.cuda.current_stream()).cuda_stream
         gs = ctypes.c_void_p(self.gscale.data_ptr()) if self.gscale is not None else None
-        check(load().gguf_gemv_rowsplit(self.type, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(self.w.data_ptr()), gs,
+        check(load().gguf_gemv_rowsplit(self.type, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()), gs,
                                         ctypes.byref(self._po[b]), R, self.rows, self.K, ctypes.c_void_p(s)))
         self.calls += 1
         return self.y[b][:R]
