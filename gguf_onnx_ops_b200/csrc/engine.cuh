@@ -112,6 +112,34 @@ __device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int 
   __syncthreads();
 }
 
+// One IQ2_XXS k-group (32-element sub-block) of a staged 16-row tile for lane (g, t) against one
+// 8-column B fragment already in registers (xv = the lane's 8 activations k0 + 8t .. k0 + 8t + 7 of
+// column g): rows g and g+8, grid entry t of each record.
+__device__ __forceinline__ void iq2_group_mma_x(const uint8_t* smem, const uint8_t* st, uint32_t r0, uint32_t r1, int grp,
+                                                int t, uint32_t lut_lane, const uint4 xv, float (&acc)[4]) {
+  const uint32_t sbo = static_cast<uint32_t>(grp >> 3) * 66u;
+  const uint32_t rec = sbo + 2u + static_cast<uint32_t>(grp & 7) * 8u;
+  const uint2 q0 = ld_u64_a2(st, r0 + rec);
+  const uint2 q1 = ld_u64_a2(st, r1 + rec);
+  const float d0 = fp16_bits_to_f32(ld_u16(st, r0 + sbo));
+  const float d1 = fp16_bits_to_f32(ld_u16(st, r1 + sbo));
+  const uint32_t gi0 = (q0.x >> (8 * t)) & 0xFFu, gi1 = (q1.x >> (8 * t)) & 0xFFu;
+  const uint4 m0 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi0 << 7));
+  const uint4 m1 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi1 << 7));
+  uint32_t A0[4], A1[4];
+  iq2_apply_signs(m0, q0.y, 7u * t, A0);
+  iq2_apply_signs(m1, q1.y, 7u * t, A1);
+  const float db0 = iq2_db(d0, q0.y), db1 = iq2_db(d1, q1.y);
+  const float z[4] = {0.f, 0.f, 0.f, 0.f};
+  float D[4];
+  mma_bf16_16816(D, A0[0], A1[0], A0[1], A1[1], xv.x, xv.y, z);
+  mma_bf16_16816(D, A0[2], A1[2], A0[3], A1[3], xv.z, xv.w, D);
+  acc[0] = fmaf(db0, D[0], acc[0]);
+  acc[1] = fmaf(db0, D[1], acc[1]);
+  acc[2] = fmaf(db1, D[2], acc[2]);
+  acc[3] = fmaf(db1, D[3], acc[3]);
+}
+
 // One IQ2_XXS k-group (32-element sub-block) of a staged 16-row tile for lane (g, t): rows g and
 // g+8 (byte offsets r0, r1 in the stage), grid entry t of each record, B fragments read from
 // xr[nt] + k0 + 8t.  kCoherent: the activation rows were written earlier in the same kernel, so

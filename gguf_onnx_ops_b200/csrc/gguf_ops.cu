@@ -465,23 +465,24 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   a.T1 = I / 16;
   a.T2 = H / 16;
   a.stage_bytes = ((16 * std::max(a.rb1, a.rb2) + 16) + 127) & ~127;
-  const int lut = 256 * 8 * 16, red = kKW * 128 * 4, grp = (5 * kMaxPairs + kMaxPairs * 8 + 8) * 4;
-  a.stages = std::min(8, (kSmemBudgetMax - lut - red - grp - 256) / a.stage_bytes);
-  if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
+  const int lut = 256 * 8 * 16, red = kMoeTeams * 2 * kMoeTeamWarps * 128 * 4,
+            grp = (5 * kMaxPairs + kMaxPairs * 8 + 8) * 4;
   a.off_stage = lut;
-  a.off_red = lut + a.stages * a.stage_bytes;
+  a.off_red = lut + kMoeTeams * 2 * a.stage_bytes;
   a.off_bar = a.off_red + red;
-  a.off_grp = a.off_bar + 2 * a.stages * 8;
+  a.off_grp = a.off_bar + kMoeTeams * 4 * 8;
   const size_t smem = a.off_grp + grp;
+  if (smem > static_cast<size_t>(kSmemBudgetMax))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(P) * sizeof(int), s);
   if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
   static std::atomic<uint64_t> done{0};
-  auto kern = moe_fused_kernel<kKW>;
+  auto kern = moe_fused_kernel;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
   // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
-  e = launch(kern, dim3(sms), dim3(kThreads), smem, s, a);
+  e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   e = launch(moe_finalize_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, s, static_cast<const float*>(part), weights,
              idx, topk, H, E, static_cast<bf16*>(out));
