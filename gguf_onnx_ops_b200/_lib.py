@@ -34,6 +34,7 @@ SIGNATURES = {
     "gguf_moe_verify_iq2_xxs": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "gguf_moe_verify_iq2_xxs_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "gguf_gemv_rowsplit": (_I32, [_I32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "gguf_moe_verify_iq2_xxs_ep": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "gguf_ipc_get_handle": (_I32, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
     "gguf_ipc_open": (_I32, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "gguf_ipc_close": (_I32, [_P]),
@@ -49,6 +50,13 @@ class GgufPeerOut(ctypes.Structure):
 
     _fields_ = [("y", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8), ("state", ctypes.c_void_p),
                 ("world", ctypes.c_int), ("rank", ctypes.c_int), ("n_total", ctypes.c_int64), ("row0", ctypes.c_int64)]
+
+
+class GgufPeerReduce(ctypes.Structure):
+    """Mirror of GgufPeerReduce (include/gguf_ops.h)."""
+
+    _fields_ = [("slots", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8), ("state", ctypes.c_void_p),
+                ("world", ctypes.c_int), ("rank", ctypes.c_int), ("r_max", ctypes.c_int64)]
 
 
 class GgufOpsError(RuntimeError):

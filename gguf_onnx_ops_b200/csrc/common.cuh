@@ -197,4 +197,35 @@ __device__ __forceinline__ void peer_complete(const PeerOut& po) {
   *reinterpret_cast<volatile uint32_t*>(po.state) = epoch;
 }
 
+// Sum across GPUs of an f32 [R, H] partial (expert-parallel MoeVerify): every GPU stores its
+// partial into slot `rank` of every GPU's reduction buffer [2 parities][world][r_max * H] (the
+// parity of the call's epoch: a peer may run one call ahead), publishes its epoch, waits for every
+// peer's, and sums the slots in rank order.
+struct PeerReduce {
+  float* slots[kMaxPeers];     // reduction buffer of GPU p
+  uint32_t* flags[kMaxPeers];  // flag array of GPU p: [kMaxPeers]
+  uint32_t* state;             // this GPU: [0] = completed epochs
+  int npeer, rank;
+  int slot_elems;              // r_max * H
+};
+
+// Thread 0 of the (single) reducing CTA, after the CTA's stores into the peers' slots: publish and
+// wait (bounded).  Returns the epoch of this call.
+__device__ __forceinline__ uint32_t peer_reduce_sync(const PeerReduce& pr, uint32_t epoch) {
+  __threadfence_system();
+  for (int p = 0; p < pr.npeer; ++p) st_release_sys(pr.flags[p] + pr.rank, epoch);
+  const uint32_t* mine = pr.flags[pr.rank];
+  const uint64_t t0 = global_timer_ns();
+  for (int p = 0; p < pr.npeer; ++p) {
+    while (static_cast<int32_t>(ld_acquire_sys(mine + p) - epoch) < 0) {
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_device_error(kSitePeerWait);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  return epoch;
+}
+
 }  // namespace gguf_b200

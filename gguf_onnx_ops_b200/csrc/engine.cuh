@@ -71,8 +71,10 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 
 // Unique-expert grouping of idx (first-occurrence order, as src/bolt_ops.cu:1233-1261):
 // s_uexp[u] = expert id of group u, s_pair[u*8 + row] = pair index (row*topk + k) or -1.
-// Pairs with an expert id outside [0, E) are ignored.  Returns U (in shared memory).
-__device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int topk, int* s_idx) {
+// Expert ids are taken relative to `offset` (the first expert this GPU holds under expert
+// parallelism; 0 otherwise); pairs whose relative id is outside [0, E) are ignored.  Returns U (in
+// shared memory).
+__device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int topk, int* s_idx, int offset = 0) {
   int* s_first = s_idx + kMaxPairs;
   int* s_rank = s_first + kMaxPairs;
   int* s_uexp = s_rank + kMaxPairs;
@@ -80,7 +82,7 @@ __device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int 
   int* s_U = s_pair + kMaxPairs * 8;
   const int tid = threadIdx.x, nth = blockDim.x;
   for (int i = tid; i < kMaxPairs * 8; i += nth) s_pair[i] = -1;
-  if (tid < P) s_idx[tid] = idx[tid];
+  if (tid < P) s_idx[tid] = idx[tid] - offset;
   __syncthreads();
   if (tid < P) {
     const int my = s_idx[tid];

@@ -442,7 +442,8 @@ namespace {
 // MoeVerify iq2=3 as: zero the phase counters (first 4P bytes of out), one fused persistent kernel
 // (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.
 int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w, void* out,
-                  void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s) {
+                  void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s,
+                  const PeerReduce* ep = nullptr, int expert_offset = 0) {
   constexpr int H = 1024;
   const int P = R * topk;
   MoeFusedArgs a = {};
@@ -454,6 +455,7 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   a.part = part;
   a.meta = meta;
   a.done = static_cast<int*>(out);
+  a.expert_offset = expert_offset;
   a.R = R;
   a.topk = topk;
   a.P = P;
@@ -484,6 +486,12 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
   e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+  if (ep) {
+    e = launch(moe_finalize_ep_kernel, dim3(1), dim3(kEpThreads), 0, s, static_cast<const float*>(part), weights, idx, topk,
+               H, E, expert_offset, R, static_cast<bf16*>(out), *ep);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify expert-parallel finalize launch", e);
+    return GGUF_OK;
+  }
   e = launch(moe_finalize_kernel, dim3(static_cast<unsigned>(R)), dim3(256), 0, s, static_cast<const float*>(part), weights,
              idx, topk, H, E, static_cast<bf16*>(out));
   if (e != cudaSuccess) return cuda_fail("MoeVerify finalize launch", e);
@@ -662,6 +670,38 @@ int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float
       return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: unknown GGUF type");
   }
   return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: K does not match the format's block size (or gscale missing)");
+}
+
+int gguf_moe_verify_iq2_xxs_ep(const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                               const void* fc2_w, void* out, void* h, float* part, int32_t* meta, const GgufPeerReduce* red,
+                               int64_t R, int64_t E_local, int64_t expert_offset, int64_t I, int64_t topk, void* stream) {
+  t_last_error.clear();
+  if (!z || !idx || !weights || !fc1_w || !fc2_w || !out || !h || !part || !meta || !red)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (expert parallel): null tensor pointer");
+  const int64_t P = R * topk;
+  if (R < 1 || R > 8 || topk < 1 || P > 128)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (expert parallel): rows must be in [1,8] and rows*topk <= 128");
+  if (I <= 0 || I % 256 != 0 || I > (1 << 20) || E_local < 1 || E_local > (1 << 20) || expert_offset < 0 ||
+      expert_offset > (1 << 20))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (expert parallel): inter size alignment mismatch or bad expert range");
+  if (red->world < 1 || red->world > kMaxPeers || red->rank < 0 || red->rank >= red->world || !red->state ||
+      R > red->r_max || red->r_max > 8)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (expert parallel): needs 1 <= world <= 8, 0 <= rank < world, R <= r_max <= 8");
+  for (int p = 0; p < red->world; ++p)
+    if (!red->slots[p] || !red->flags[p]) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (expert parallel): null peer buffer");
+  if (!aligned(fc1_w, 16) || !aligned(fc2_w, 16) || !aligned(z, 16) || !aligned(h, 16) || !aligned(part, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (expert parallel): tensors must be 16-byte aligned");
+  PeerReduce pr = {};
+  for (int p = 0; p < red->world; ++p) {
+    pr.slots[p] = red->slots[p];
+    pr.flags[p] = red->flags[p];
+  }
+  pr.state = red->state;
+  pr.npeer = red->world;
+  pr.rank = red->rank;
+  pr.slot_elems = static_cast<int>(red->r_max * 1024);
+  return run_moe_fused(z, idx, weights, fc1_w, fc2_w, out, h, part, meta, (int)R, (int)E_local, (int)I, (int)topk,
+                       static_cast<cudaStream_t>(stream), &pr, (int)expert_offset);
 }
 
 int gguf_ipc_get_handle(const void* dev_ptr, void* handle64, int64_t* offset) {

@@ -40,6 +40,7 @@ struct MoeFusedArgs {
   int rb1, rb2;       // row bytes of W1 / W2
   int T1, T2;         // 16-row tiles per expert: I/16, H/16
   int stage_bytes;    // one 16-row tile of either matrix (+ pad)
+  int expert_offset;  // expert parallelism: global id of local expert 0 (idx holds global ids)
   int off_stage, off_red, off_bar, off_grp;
 };
 
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
   }
   fill_iq2_lut_bf16<kMoeWarps * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
-  moe_group(a.idx, a.P, a.E, a.topk, s_grp);  // ends with __syncthreads
+  moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
   const int* s_uexp = s_grp + 3 * kMaxPairs;
   const int* s_pair = s_uexp + kMaxPairs;
   const int U = s_pair[kMaxPairs * 8];
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
     for (int i = threadIdx.x; i < 1 + 9 * a.P; i += blockDim.x) {
       int v;
       if (i == 0) v = U;
-      else if (i <= a.P) v = (i - 1 < U) ? s_uexp[i - 1] : -1;
+      else if (i <= a.P) v = (i - 1 < U) ? s_uexp[i - 1] + a.expert_offset : -1;
       else v = s_pair[i - 1 - a.P];
       a.meta[i] = v;
     }

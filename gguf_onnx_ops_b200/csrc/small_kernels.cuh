@@ -271,4 +271,62 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Expert-parallel MoeVerify finalize (one CTA): this GPU's weighted partial sum over its own pairs
+// (pairs whose expert lies in [offset, offset + E_local)), summed across the group through peer
+// memory in rank order, rounded once to bf16.
+// ---------------------------------------------------------------------------------------------
+constexpr int kEpThreads = 1024;
+
+__global__ void __launch_bounds__(kEpThreads) moe_finalize_ep_kernel(const float* __restrict__ part, const float* __restrict__ w,
+                                                                   const int32_t* __restrict__ idx, int topk, int H,
+                                                                   int E_local, int offset, int R, bf16* __restrict__ out,
+                                                                   const PeerReduce pr) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile uint32_t*>(pr.state) + 1u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
+  const int64_t par = static_cast<int64_t>(epoch & 1u) * pr.npeer;
+  const int n4 = R * (H / 4);
+  for (int i = threadIdx.x; i < n4; i += kEpThreads) {
+    const int t = i / (H / 4), v = i % (H / 4);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < topk; ++k) {
+      const int p = t * topk + k;
+      const int e = __ldg(idx + p) - offset;
+      if (e < 0 || e >= E_local) continue;
+      const float wk = __ldg(w + p);
+      const float4 pv = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(p) * H) + v);
+      a.x += wk * pv.x;
+      a.y += wk * pv.y;
+      a.z += wk * pv.z;
+      a.w += wk * pv.w;
+    }
+    const int64_t off = (par + pr.rank) * pr.slot_elems + static_cast<int64_t>(t) * H;
+    for (int q = 0; q < pr.npeer; ++q) reinterpret_cast<float4*>(pr.slots[q] + off)[v] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) peer_reduce_sync(pr, epoch);
+  __syncthreads();
+  const float* mine = pr.slots[pr.rank];
+  for (int i = threadIdx.x; i < n4; i += kEpThreads) {
+    const int t = i / (H / 4), v = i % (H / 4);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < pr.npeer; ++q) {
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(mine + (par + q) * pr.slot_elems + static_cast<int64_t>(t) * H) + v);
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(a.x, a.y);
+    o.y = pack_bf16x2(a.z, a.w);
+    reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * H)[v] = o;
+  }
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(pr.state) = epoch;
+}
+
 }  // namespace gguf_b200

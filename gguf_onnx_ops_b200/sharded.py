@@ -128,3 +128,74 @@ class RowSplitGemv:
         for base in self._opened:
             load().gguf_ipc_close(ctypes.c_void_p(base))
         self._opened = []
+
+
+def shard_experts(n_experts: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous, balanced split of the experts: (first expert, count) of this rank."""
+    if not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    lo, hi = (n_experts * rank) // world, (n_experts * (rank + 1)) // world
+    return lo, hi - lo
+
+
+class ExpertParallelMoE:
+    """MoeVerify iq2=3 with the experts split across the group (one process per GPU).
+
+    Every rank holds experts [offset, offset + E_local) and processes the pairs routed to them; the
+    f32 partial outputs are summed across the group inside the finalize kernel through peer memory
+    (see gguf_moe_verify_iq2_xxs_ep).  idx holds global expert ids (the router is replicated).
+    """
+
+    H = 1024
+
+    def __init__(self, fc1_local: torch.Tensor, fc2_local: torch.Tensor, expert_offset: int, topk: int, r_max: int = 8,
+                 group=None):
+        self.E, self.I = fc1_local.shape[0], fc1_local.shape[1]
+        if fc2_local.shape[0] != self.E or fc1_local.dtype != torch.uint8 or fc2_local.dtype != torch.uint8:
+            raise ValueError("fc1 / fc2 must be raw IQ2_XXS expert tensors of the same experts")
+        if not 1 <= r_max <= 8 or r_max * topk > 128:
+            raise ValueError("r_max must be in [1, 8] with r_max * topk <= 128")
+        self.w1, self.w2, self.offset, self.topk, self.r_max = fc1_local, fc2_local, expert_offset, topk, r_max
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        dev = fc1_local.device
+        P = r_max * topk
+        self.red = torch.zeros(2, self.world, r_max * self.H, dtype=torch.float32, device=dev)
+        self.flags = torch.zeros(MAX_PEERS, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.h = torch.empty(P, self.I, dtype=torch.bfloat16, device=dev)
+        self.part = torch.empty(P, self.H, dtype=torch.float32, device=dev)
+        self.meta = torch.empty(1 + 9 * P, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        allh = exchange([ipc_handle(self.red), ipc_handle(self.flags)], group)
+        self._opened = []
+        self._pr = _lib.GgufPeerReduce()
+        for p, ((hr, offr), (hf, offf)) in enumerate(allh):
+            if p == self.rank:
+                self._pr.slots[p], self._pr.flags[p] = self.red.data_ptr(), self.flags.data_ptr()
+                continue
+            pr_, br = ipc_open(hr, offr)
+            pf, bf = ipc_open(hf, offf)
+            self._opened += [br, bf]
+            self._pr.slots[p], self._pr.flags[p] = pr_, pf
+        self._pr.state = self.state.data_ptr()
+        self._pr.world, self._pr.rank, self._pr.r_max = self.world, self.rank, r_max
+
+    def __call__(self, z: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None = None,
+                 stream=None) -> torch.Tensor:
+        R = z.shape[0]
+        if z.dtype != torch.bfloat16 or z.shape[1] != self.H or not 1 <= R <= self.r_max:
+            raise ValueError("z must be bf16 [R, 1024] with R <= r_max")
+        if idx.dtype != torch.int32 or weights.dtype != torch.float32 or idx.shape != (R, self.topk):
+            raise ValueError("idx int32 [R, topk] and weights f32 [R, topk] expected")
+        out = torch.empty(R, self.H, dtype=torch.bfloat16, device=z.device) if out is None else out
+        s = (stream or torch.cuda.current_stream()).cuda_stream
+        p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        check(load().gguf_moe_verify_iq2_xxs_ep(p(z), p(idx), p(weights), p(self.w1), p(self.w2), p(out), p(self.h),
+                                                p(self.part), p(self.meta), ctypes.byref(self._pr), R, self.E, self.offset,
+                                                self.I, self.topk, ctypes.c_void_p(s)))
+        return out
+
+    def close(self) -> None:
+        for base in self._opened:
+            load().gguf_ipc_close(ctypes.c_void_p(base))
+        self._opened = []

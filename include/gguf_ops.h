@@ -138,6 +138,28 @@ typedef struct {
 GGUF_OPS_API int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float* gscale,
                                     const GgufPeerOut* out, int64_t R, int64_t rows, int64_t K, void* stream);
 
+/*
+ * Expert-parallel MoeVerify iq2=3 (no counterpart in the reference; SURVEY expert split of
+ * MoeVerify): GPU `rank` holds experts [expert_offset, expert_offset + E_local) (fc1_w / fc2_w are
+ * those experts' tensors) and processes the pairs routed to them; idx holds global expert ids (the
+ * router is replicated).  The f32 [R, 1024] partial outputs are summed across the group through peer
+ * memory (every GPU stores its partial into its slot of every GPU's buffer, epoch flags, bounded
+ * waits), in rank order, and rounded once to bf16 into out.  h / part / meta hold this GPU's pairs
+ * only (meta with global expert ids).  All GPUs must issue the same sequence of calls.
+ */
+typedef struct {
+  float* slots[8];      /* reduction buffer of GPU p: f32 [2][world][r_max * 1024] */
+  uint32_t* flags[8];   /* flag array of GPU p: uint32 [8], zero-initialised */
+  uint32_t* state;      /* this GPU: uint32 [1], zero-initialised */
+  int world, rank;
+  int64_t r_max;
+} GgufPeerReduce;
+
+GGUF_OPS_API int gguf_moe_verify_iq2_xxs_ep(const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                                            const void* fc2_w, void* out, void* h, float* part, int32_t* meta,
+                                            const GgufPeerReduce* red, int64_t R, int64_t E_local,
+                                            int64_t expert_offset, int64_t I, int64_t topk, void* stream);
+
 /* CUDA IPC plumbing for the peer pointers: the 64-byte handle of the device allocation holding
  * dev_ptr and dev_ptr's offset in it; open a peer's handle in this process (returns the allocation
  * base: add the peer's offset; peer access is enabled lazily); close an opened handle. */

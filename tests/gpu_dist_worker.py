@@ -17,6 +17,8 @@ from gguf_onnx_ops_b200 import _lib, ops  # noqa: E402
 from gguf_onnx_ops_b200.sharded import RowSplitGemv, shard_rows  # noqa: E402
 from oracle import inputs as I  # noqa: E402
 
+I_ = I
+
 TYPES = {"q8_0": _lib.GGUF_TYPE_Q8_0, "iq2_xxs": _lib.GGUF_TYPE_IQ2_XXS, "nvfp4": _lib.GGUF_TYPE_NVFP4}
 
 
@@ -55,6 +57,27 @@ def main():
                 if not ok:
                     failures.append((op, N, K, R, it))
         sharded.close()
+    # expert-parallel MoeVerify against the single-GPU op on all experts
+    E, H, Iw, topk = 16, 1024, 512, 6
+    from gguf_onnx_ops_b200.sharded import ExpertParallelMoE, shard_experts
+    g = I_.rng(42)
+    w1 = torch.from_numpy(I_.iq2_xxs_weights(g, (E, Iw), H)).to(dev)
+    w2 = torch.from_numpy(I_.iq2_xxs_weights(g, (E, H), Iw)).to(dev)
+    e0, el = shard_experts(E, world, rank)
+    ep = ExpertParallelMoE(w1[e0:e0 + el].contiguous(), w2[e0:e0 + el].contiguous(), e0, topk, r_max=8)
+    for R in (1, 3, 8, 1):
+        for it in range(2):
+            gg = I_.rng(1000 * R + it)
+            z = torch.from_numpy(I_.bf16_normal(gg, (R, H)).view(np.int16)).view(torch.bfloat16).to(dev)
+            idx = torch.from_numpy(np.stack([gg.choice(E, topk, replace=False) for _ in range(R)]).astype(np.int32)).to(dev)
+            wt = torch.from_numpy(gg.random((R, topk)).astype(np.float32)).to(dev)
+            out = ep(z, idx, wt)
+            ref = ops.MoeVerify(z, idx, wt, w1, None, w2, None, topk=topk)[0]
+            torch.cuda.synchronize()
+            err = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
+            if not err < 5e-3:
+                failures.append(("moe_ep", R, it, err))
+    ep.close()
     rc, site = _lib.device_status()
     if rc:
         failures.append(("device status", rc, site))
