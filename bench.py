@@ -337,6 +337,45 @@ def bench_rowsplit(R, steps, warmup, dev, world, rank):
                 rows_per_gpu=rows, copies=copies, device_status=rc, **({"nccl_error": nccl_err} if nccl_err else {}))
 
 
+def bench_moe_ep(R, steps, warmup, dev, world, rank):
+    """C3 MoeVerify with the 128 experts split over the group (expert parallelism, partial outputs
+    summed through peer memory inside the finalize kernel); idx from one router call (replicated).
+    Time per call = max over ranks."""
+    import torch
+
+    from gguf_onnx_ops_b200 import _lib, ops
+    from gguf_onnx_ops_b200.sharded import ExpertParallelMoE, shard_experts
+
+    E, H, I, topk = 128, 1024, 1792, 6
+    e0, el = shard_experts(E, world, rank)
+    w1 = gen_weights("iq2_xxs", el * I, H, seed=2 + rank, dev=dev).reshape(el, I, -1)
+    w2 = gen_weights("iq2_xxs", el * H, I, seed=40 + rank, dev=dev).reshape(el, H, -1)
+    torch.manual_seed(R)  # the same routing on every rank
+    gw = torch.randn(E, H, device=dev) * 0.02
+    bias = torch.randn(E, device=dev) * 0.01
+    x = torch.randn(R, H, device=dev).bfloat16()
+    z = torch.randn(R, H, device=dev).bfloat16()
+    idx, wt, _ = ops.MoeRouteGGUF(x, gw, bias, topk, 1.0)
+    op = ExpertParallelMoE(w1, w2, e0, topk, r_max=8)
+    out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+
+    def one():
+        for _ in range(8):
+            op(z, idx, wt, out=out)
+
+    g = capture(one)
+    ms = max_over_ranks(time_graph(g, steps, warmup, world), world)
+    del g
+    torch.cuda.synchronize()
+    rc, _ = _lib.device_status()
+    op.close()
+    us = ms * 1e3 / (steps * 8)
+    U = len(torch.unique(idx))
+    wbytes = U * (I * (H // 256) * 66 + H * (I // 256) * 66)
+    return dict(world=world, R=R, us_per_call=us, gbs=wbytes / (us * 1e-6) / 1e9, unique_experts=U,
+                experts_per_gpu=el, device_status=rc, note="L2-resident weights (one expert copy per GPU)")
+
+
 def bench_e2e_gemv(op, R, N, K, steps, warmup, dev, state):
     """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host."""
     import torch
@@ -554,6 +593,9 @@ def main():
     if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather
         line["sharded"] = {f"C4_R{R}": bench_rowsplit(R, max(5, args.steps // 2), args.warmup, dev, world, rank)
                            for R in (1, 4)}
+        for R in (1, 8):
+            line["sharded"][f"C3_R{R}_expert_parallel"] = bench_moe_ep(R, max(5, args.steps // 2), args.warmup, dev,
+                                                                        world, rank)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
