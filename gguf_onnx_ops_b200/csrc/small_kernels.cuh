@@ -21,6 +21,69 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
 
+// float -> unsigned key with the same order
+__device__ __forceinline__ uint32_t ordered_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Top-k of one row by one warp: lane l holds experts l, l + 32, ... (kPer of them).  Each pick is an
+// arg-max of score + bias over the warp with ties to the lower expert index (src/bolt_ops.cu:459-510):
+// one warp max of the ordered keys, then one warp min of the indices holding that key.
+template <int kPer>
+__device__ __forceinline__ void route_select(const float* __restrict__ sr, int row, int E, int topk, float scale,
+                                             const float* __restrict__ bias, int32_t* __restrict__ idx_out,
+                                             float* __restrict__ w_out) {
+  const int lane = threadIdx.x & 31;
+  float sc[kPer];
+  uint32_t key[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    sc[i] = e < E ? __ldcg(sr + e) : 0.f;
+    const float v = e < E ? sc[i] + __ldg(bias + e) : 0.f;
+    key[i] = (e < E && v == v) ? ordered_key(v) : 0u;  // 0: below every real key (absent or NaN: never picked)
+  }
+  int my_idx = -1;
+  float my_sc = 0.f, sum = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    uint32_t bk = 0u;
+    int bi = 0x7FFFFFFF;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (key[i] > bk) {  // ascending expert order within the lane: the first maximum wins
+        bk = key[i];
+        bi = lane + 32 * i;
+      }
+    const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+    const int wi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(bk == wk ? bi : 0x7FFFFFFF)));
+    float s = 0.f;
+    if (wk != 0u) {
+      const int owner = wi & 31, slot = wi >> 5;
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (i == slot) mine = sc[i];
+      s = __shfl_sync(0xffffffffu, mine, owner);
+      if (lane == owner) {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+          if (i == slot) key[i] = 0u;
+      }
+    }
+    if (lane == j) {
+      my_idx = wk != 0u ? wi : -1;
+      my_sc = s;
+    }
+    sum += s;
+  }
+  const float denom = sum + 1e-20f;
+  if (lane < topk) {
+    idx_out[static_cast<int64_t>(row) * topk + lane] = my_idx;
+    w_out[static_cast<int64_t>(row) * topk + lane] = my_sc / denom * scale;
+  }
+}
+
 __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps * 32)
     route_kernel(const bf16* __restrict__ x, const float* __restrict__ gw, const float* __restrict__ bias, int R, int K,
                  int E, int topk, float scale, int32_t* __restrict__ idx_out, float* __restrict__ w_out,
@@ -116,58 +179,9 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
   if (r >= nrows) return;
   const int row = row0 + r;
   const float* sr = scores + static_cast<int64_t>(row) * E;
-  float val[16], sc[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int e = lane + 32 * i;
-    if (e < E) {
-      sc[i] = __ldcg(sr + e);
-      val[i] = sc[i] + __ldg(bias + e);
-    } else {
-      sc[i] = 0.f;
-      val[i] = -INFINITY;
-    }
-  }
-  int my_idx = -1;
-  float my_sc = 0.f, sum = 0.f;
-  for (int j = 0; j < topk; ++j) {
-    float bv = -INFINITY, bs = 0.f;
-    int bi = -1;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (val[i] > bv) {  // ascending expert order within the lane: first max wins
-        bv = val[i];
-        bs = sc[i];
-        bi = lane + 32 * i;
-      }
-    float wv = bv;
-    int wi = bi;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, wv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
-      if (oi >= 0 && (wi < 0 || ov > wv || (ov == wv && oi < wi))) {
-        wv = ov;
-        wi = oi;
-      }
-    }
-    const float s = wi >= 0 ? __shfl_sync(0xffffffffu, bs, wi & 31) : 0.f;
-    if (wi >= 0 && (wi & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (i == (wi >> 5)) val[i] = -INFINITY;
-    }
-    if (lane == j) {
-      my_idx = wi;
-      my_sc = s;
-    }
-    sum += s;
-  }
-  const float denom = sum + 1e-20f;
-  if (lane < topk) {
-    idx_out[static_cast<int64_t>(row) * topk + lane] = my_idx;
-    w_out[static_cast<int64_t>(row) * topk + lane] = my_sc / denom * scale;
-  }
+  if (E <= 128) route_select<4>(sr, row, E, topk, scale, bias, idx_out, w_out);
+  else if (E <= 256) route_select<8>(sr, row, E, topk, scale, bias, idx_out, w_out);
+  else route_select<16>(sr, row, E, topk, scale, bias, idx_out, w_out);
 }
 
 // ---------------------------------------------------------------------------------------------
