@@ -481,11 +481,27 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(P) * sizeof(int), s);
   if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
   static std::atomic<uint64_t> done{0};
-  auto kern = moe_fused_kernel;
-  if ((rc = ensure_smem(kern, smem, done))) return rc;
-  // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
-  e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
-  if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+  if (R == 1 && g_fast.load() == 1) {
+    // one row: the integer single-row decode; tables at offset 0 and a smaller reduction buffer
+    MoeFusedArgs b = a;
+    b.off_stage = kI8Lut;
+    b.off_red = b.off_stage + kMoeTeams * 2 * a.stage_bytes;
+    b.off_bar = b.off_red + kMoeTeams * 2 * kMoeTeamWarps * 16 * 4;
+    b.off_grp = b.off_bar + kMoeTeams * 4 * 8;
+    const size_t smem1 = b.off_grp + grp;
+    if (smem1 > static_cast<size_t>(kSmemBudgetMax))
+      return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
+    static std::atomic<uint64_t> done1{0};
+    if ((rc = ensure_smem(moe_r1_i8_kernel, smem1, done1))) return rc;
+    e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeWarps * 32), smem1, s, b);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+  } else {
+    auto kern = moe_fused_kernel;
+    if ((rc = ensure_smem(kern, smem, done))) return rc;
+    // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
+    e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+  }
   if (ep) {
     e = launch(moe_finalize_ep_kernel, dim3(1), dim3(kEpThreads), 0, s, static_cast<const float*>(part), weights, idx, topk,
                H, E, expert_offset, R, static_cast<bf16*>(out), *ep);

@@ -24,6 +24,7 @@
 #pragma once
 
 #include "engine.cuh"
+#include "slice_iq2_i8.cuh"
 
 namespace gguf_b200 {
 
@@ -196,6 +197,167 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
         } else {
           a.part[static_cast<int64_t>(p) * a.H + tile * 16 + rl] = vb;
         }
+      }
+    }
+    if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);
+    if (phase == 1) {  // publish: this tile of h is written (every team thread is past its store)
+      named_bar_sync(bar_id, bar_n);
+      if (leader) {
+        __threadfence();
+        atomicAdd(a.done + u, 1);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// The same MoE for one activation row (R = 1, the decode step) on the integer tensor cores: every
+// unique expert has exactly one pair, so the single-row decode of slice_iq2_i8.cuh applies (exact
+// u8 weights 64 + s*m, the row as two 8-bit limbs per 32-element group, block-diagonal MMA
+// columns).  Phase 1 (K = 1024 = 4 slices): warp w of a team decodes slice w of its item with the
+// fragments of z converted once per launch.  Phase 2 (K = I): warp w decodes slices w, w + 4, ...
+// converting the pair's h slice (read through L2) right before each.  Work split, staging, phase
+// order and outputs are those of moe_fused_kernel.  Tables (48 KB) sit at shared offset 0.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_r1_i8_kernel(const MoeFusedArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int team = warp / kMoeTeamWarps, tw = warp % kMoeTeamWarps;
+  const bool leader = tw == 0 && lane == 0;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
+  uint64_t* empty = full + 2;
+  uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
+  float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 16;  // [2][warps][16]
+  int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
+
+  if (leader) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kMoeTeamWarps);
+    }
+    fence_mbar_init();
+  }
+  i8_fill_tables<kMoeWarps * 32>(smem, threadIdx.x);
+  pdl_wait();  // idx (router) and z come from earlier kernels
+  moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
+  const int* s_uexp = s_grp + 3 * kMaxPairs;
+  const int* s_pair = s_uexp + kMaxPairs;
+  const int U = s_pair[kMaxPairs * 8];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < 1 + 9 * a.P; i += blockDim.x) {
+      int v;
+      if (i == 0) v = U;
+      else if (i <= a.P) v = (i - 1 < U) ? s_uexp[i - 1] + a.expert_offset : -1;
+      else v = s_pair[i - 1 - a.P];
+      a.meta[i] = v;
+    }
+  pdl_launch_dependents();
+
+  const int n1 = U * a.T1, n2 = U * a.T2, nitems = n1 + n2;
+  const int teams = kMoeTeams * static_cast<int>(gridDim.x);
+  const int first = team * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
+  auto item_of = [&](int q, int& phase, int& u, int& tile) {
+    if (q < n1) {
+      phase = 1;
+      u = q / a.T1;
+      tile = q % a.T1;
+    } else {
+      phase = 2;
+      u = (q - n1) / a.T2;
+      tile = (q - n1) % a.T2;
+    }
+  };
+  auto fetch = [&](int q, uint32_t k) {
+    int phase, u, tile;
+    item_of(q, phase, u, tile);
+    const int s = static_cast<int>(k & 1u);
+    if (k >= 2u) mbar_wait(&empty[s], ((k >> 1) - 1u) & 1u, kSiteEmptyWait);
+    const int e = s_uexp[u];
+    const uint8_t* src = phase == 1 ? a.w1 + (static_cast<int64_t>(e) * a.I + tile * 16) * a.rb1
+                                    : a.w2 + (static_cast<int64_t>(e) * a.H + tile * 16) * a.rb2;
+    const uint32_t bytes = 16u * static_cast<uint32_t>(phase == 1 ? a.rb1 : a.rb2);
+    mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_g2s(stage0 + s * a.stage_bytes, src, bytes, &full[s]);
+  };
+  if (leader) {
+    if (first < nitems) fetch(first, 0u);
+    if (first + teams < nitems) fetch(first + teams, 1u);
+  }
+
+  const int g = lane >> 2, t = lane & 3;
+  // z fragments of this warp's phase-1 slice (the single row's z, slice tw of H = 1024)
+  I8XFrag zf;
+  i8_x_frag(ldg128(a.z + tw * 256 + 8 * lane), zf);
+  const int bar_id = 1 + team, bar_n = kMoeTeamWarps * 32;
+  const int slices2 = a.I / 256;
+  uint32_t k = 0;
+  for (int q = first; q < nitems; q += teams, ++k) {
+    int phase, u, tile;
+    item_of(q, phase, u, tile);
+    const int p = s_pair[u * 8];  // the pair of row 0 (R = 1)
+    if (phase == 2) {  // every phase-1 tile of expert u must be in h
+      if (leader) {
+        const uint64_t t0 = global_timer_ns();
+        int v;
+        for (;;) {
+          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(a.done + u) : "memory");
+          if (v >= a.T1) break;
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(kMoeDoneWaitSite);
+            break;
+          }
+          __nanosleep(128);
+        }
+      }
+      named_bar_sync(bar_id, bar_n);
+    }
+    const int s = static_cast<int>(k & 1u);
+    mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
+    const uint8_t* st = stage0 + s * a.stage_bytes;
+    float acc0 = 0.f, acc1 = 0.f;
+    if (phase == 1) {
+      const uint32_t r0 = static_cast<uint32_t>(g * a.rb1), r1 = static_cast<uint32_t>((g + 8) * a.rb1);
+      uint2 rc[4];
+      uint32_t dbits;
+      i8_records_any(st, r0, r1, static_cast<uint32_t>(tw) * 66u, rc, dbits);
+      i8_slice(smem, rc, dbits, zf, acc0, acc1);
+    } else {
+      const uint32_t r0 = static_cast<uint32_t>(g * a.rb2), r1 = static_cast<uint32_t>((g + 8) * a.rb2);
+      const bf16* hp = a.h + static_cast<int64_t>(p) * a.I;
+      for (int sl = tw; sl < slices2; sl += kMoeTeamWarps) {
+        I8XFrag hf;
+        i8_x_frag(__ldcg(reinterpret_cast<const uint4*>(hp + sl * 256 + 8 * lane)), hf);
+        uint2 rc[4];
+        uint32_t dbits;
+        i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
+        float b0, b1;
+        i8_slice(smem, rc, dbits, hf, b0, b1);
+        acc0 += b0;
+        acc1 += b1;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    // team reduction of the 16 rows; slot (k & 1) is rewritten two items later, after a barrier
+    float* rb = red + s * kMoeTeamWarps * 16;
+    if (t == 0) {
+      rb[tw * 16 + g] = acc0;
+      rb[tw * 16 + g + 8] = acc1;
+    }
+    named_bar_sync(bar_id, bar_n);
+    const int ti = tw * 32 + lane;
+    if (ti < 16 && p >= 0) {
+      const float v = (rb[ti] + rb[16 + ti]) + (rb[32 + ti] + rb[48 + ti]);
+      const float vb = round_bf16(v);
+      if (phase == 1) {
+        const float r = fmaxf(vb, 0.f);
+        a.h[static_cast<int64_t>(p) * a.I + tile * 16 + ti] = __float2bfloat16(r * r);
+      } else {
+        a.part[static_cast<int64_t>(p) * a.H + tile * 16 + ti] = vb;
       }
     }
     if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);

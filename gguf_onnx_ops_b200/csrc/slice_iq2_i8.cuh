@@ -78,6 +78,163 @@ __device__ __forceinline__ int bf16_to_fixed(int neg, int sig, int ex, int emax)
   return neg ? -v : v;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Building blocks shared by the single-row GEMV and the single-row MoE kernel
+// ---------------------------------------------------------------------------------------------
+// B fragments of one 256-element activation slice (block-diagonal; see the header comment).
+struct I8XFrag {
+  uint32_t bh0[8], bl0[8], bh1[8], bl1[8];
+  float xs0, xs1;    // 2^(E - 14) of the lane's C columns (groups 2t, 2t+1)
+  int xoff0, xoff1;  // 64 * sum(x_int) of those columns
+};
+
+// Converts the 8 activations xv (elements 8l..8l+7 of the slice, l = lane) into the warp's
+// fragments: lane l handles group l >> 2; the group's scale and sum are reduced over the quad.
+__device__ __forceinline__ void i8_x_frag(const uint4 xv, I8XFrag& f) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const bool dlo = (g == t), dhi = (g == t + 4);
+  const uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+  // largest |x| of the group: bf16 magnitudes order like their bit patterns
+  uint32_t mb = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mb = max(mb, max(wv[i] & 0x7FFFu, (wv[i] >> 16) & 0x7FFFu));
+  mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+  mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+  const int emax = max(1, static_cast<int>(mb >> 7));  // effective biased exponent of the maximum
+  uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+  int xsum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int neg, sig, ex;
+    bf16_parts(i & 1 ? (wv[i >> 1] >> 16) : (wv[i >> 1] & 0xFFFFu), neg, sig, ex);
+    const int xi = bf16_to_fixed(neg, sig, ex, emax);
+    xsum += xi;
+    hw[i >> 2] |= (static_cast<uint32_t>(xi >> 8) & 0xFFu) << (8 * (i & 3));
+    lw[i >> 2] |= (static_cast<uint32_t>(xi) & 0xFFu) << (8 * (i & 3));
+  }
+  xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+  xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+  // owner of group c: lane (g = c, t = c) for c < 4, lane (g = c, t = c - 4) for c >= 4.  Step j of
+  // group c = elements 4j..4j+3 = word (j & 1) of lane 4c + (j >> 1).
+  const int c = dlo ? t : (dhi ? t + 4 : 0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int src = 4 * c + (j >> 1);
+    const uint32_t h = __shfl_sync(0xffffffffu, hw[j & 1], src);
+    const uint32_t l = __shfl_sync(0xffffffffu, lw[j & 1], src);
+    f.bh0[j] = dlo ? h : 0u;
+    f.bl0[j] = dlo ? l : 0u;
+    f.bh1[j] = dhi ? h : 0u;
+    f.bl1[j] = dhi ? l : 0u;
+  }
+  const int e0 = __shfl_sync(0xffffffffu, emax, 4 * (2 * t)), e1 = __shfl_sync(0xffffffffu, emax, 4 * (2 * t + 1));
+  f.xoff0 = 64 * __shfl_sync(0xffffffffu, xsum, 4 * (2 * t));
+  f.xoff1 = 64 * __shfl_sync(0xffffffffu, xsum, 4 * (2 * t + 1));
+  f.xs0 = ldexpf(1.0f, e0 - 141);  // 2^(E - 14), E = emax - 127
+  f.xs1 = ldexpf(1.0f, e1 - 141);
+}
+
+// The records of one slice for lane (g, t): grid bytes + sign/scale words of rows g, g+8 x groups
+// t, t+4 (rc[0..3] = [g, t], [g, t+4], [g+8, t], [g+8, t+4]) and the two super-block scales.
+// r0 / r1: byte offsets of rows g / g+8 in the stage; so: the slice's byte offset in a row (its
+// records are 4-byte aligned iff `al`).
+__device__ __forceinline__ void i8_records(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t so, bool al,
+                                           uint2 (&rc)[4], uint32_t& dbits) {
+  const uint32_t t = threadIdx.x & 3;
+  rc[0] = lds8(st, r0 + so + 2u + 8u * t, al);
+  rc[1] = lds8(st, r0 + so + 34u + 8u * t, al);
+  rc[2] = lds8(st, r1 + so + 2u + 8u * t, al);
+  rc[3] = lds8(st, r1 + so + 34u + 8u * t, al);
+  dbits = ld_u16(st, r0 + so) | (ld_u16(st, r1 + so) << 16);
+}
+// The same for rows whose byte offsets may differ in alignment from lane to lane (odd row sizes):
+// every 8-byte record is read as three aligned words and funnel-shifted (a shift of 0 when aligned).
+__device__ __forceinline__ uint2 lds8_any(const uint8_t* base, uint32_t off) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(base + (off & ~3u));
+  const uint32_t sh = (off & 2u) * 8u, w0 = w[0], w1 = w[1], w2 = w[2];
+  return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+__device__ __forceinline__ void i8_records_any(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t so, uint2 (&rc)[4],
+                                               uint32_t& dbits) {
+  const uint32_t t = threadIdx.x & 3;
+  rc[0] = lds8_any(st, r0 + so + 2u + 8u * t);
+  rc[1] = lds8_any(st, r0 + so + 34u + 8u * t);
+  rc[2] = lds8_any(st, r1 + so + 2u + 8u * t);
+  rc[3] = lds8_any(st, r1 + so + 34u + 8u * t);
+  dbits = ld_u16(st, r0 + so) | (ld_u16(st, r1 + so) << 16);
+}
+
+// One 16-row x 256-column slice: decode (tables at shared offset 0), 16 MMAs, fp32 epilogue.  Gives
+// the lane's partial sums of rows g (acc0) and g+8 (acc1) over its C columns; the caller reduces
+// them over the quad (shuffles by 1 and 2).
+__device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[4], uint32_t dbits, const I8XFrag& f,
+                                         float& acc0, float& acc1) {
+  const int lane = threadIdx.x & 31, t = lane & 3;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
+  const int q0 = (lane & ~3) | ((2 * t) & 3), q1 = (lane & ~3) | ((2 * t + 1) & 3);
+  const int sel_sh = t >= 2 ? 4 : 0;
+  int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t A[4][2];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      // table offsets: (grid byte e) * 128 and (sign field e) * 128, one shift + one LOP3 each
+      const uint32_t gx = e == 0 ? (rc[r].x << 7) : (rc[r].x >> (8 * e - 7));
+      const uint32_t sy = e == 0 ? (rc[r].y << 7) : (e == 1 ? rc[r].y : (rc[r].y >> (7 * e - 7)));
+      const uint2 X = *reinterpret_cast<const uint2*>(smem + ((gx & 0x7F80u) | lane_off));
+      const uint2 M = *reinterpret_cast<const uint2*>(smem + kI8MagLut + ((sy & 0x3F80u) | lane_off));
+      A[r][0] = X.x - 2u * (X.x & M.x);  // 64 + s*m per byte, no borrow between bytes
+      A[r][1] = X.y - 2u * (X.y & M.y);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = 2 * e + h;
+      imma_u8s8(ch, A[0][h], A[2][h], A[1][h], A[3][h], f.bh0[j], f.bh1[j]);
+      imma_u8u8(cl, A[0][h], A[2][h], A[1][h], A[3][h], f.bl0[j], f.bl1[j]);
+    }
+  }
+  // exact s32 dot products of the lane's four (row, group) cells: sum(A x) - 64 sum(x)
+  const float f0 = static_cast<float>(ch[0] * 256 + cl[0] - f.xoff0);
+  const float f1 = static_cast<float>(ch[1] * 256 + cl[1] - f.xoff1);
+  const float f2 = static_cast<float>(ch[2] * 256 + cl[2] - f.xoff0);
+  const float f3 = static_cast<float>(ch[3] * 256 + cl[3] - f.xoff1);
+  const uint32_t mine = (rc[0].y >> 28) | ((rc[1].y >> 28) << 4) | ((rc[2].y >> 28) << 8) | ((rc[3].y >> 28) << 12);
+  const uint32_t p0 = __shfl_sync(0xffffffffu, mine, q0) >> sel_sh, p1 = __shfl_sync(0xffffffffu, mine, q1) >> sel_sh;
+  const float d0s = fp16_bits_to_f32(dbits & 0xFFFFu) * 0.25f, d1s = fp16_bits_to_f32(dbits >> 16) * 0.25f;
+  // 0.5 + s exactly: float(2^23 + s) - (2^23 - 0.5)
+  const float h00 = __uint_as_float((p0 & 15u) | 0x4B000000u) - 8388607.5f;
+  const float h01 = __uint_as_float((p1 & 15u) | 0x4B000000u) - 8388607.5f;
+  const float h10 = __uint_as_float(((p0 >> 8) & 15u) | 0x4B000000u) - 8388607.5f;
+  const float h11 = __uint_as_float(((p1 >> 8) & 15u) | 0x4B000000u) - 8388607.5f;
+  acc0 = (f0 * (f.xs0 * h00) + f1 * (f.xs1 * h01)) * d0s;
+  acc1 = (f2 * (f.xs0 * h10) + f3 * (f.xs1 * h11)) * d1s;
+}
+
+// 16 replicas of each 8-byte table entry at shared offset 0 (64 + magnitudes, then the sign masks),
+// two replicas per 16-byte store; called by threads 0..kThreads-1, each issuing all of its loads
+// before its first store (one L2 round trip).
+template <int kThreads>
+__device__ __forceinline__ void i8_fill_tables(uint8_t* smem, int tid) {
+  constexpr int kStores = (256 + 128) * 8, kIters = (kStores + kThreads - 1) / kThreads;
+  uint2 v[kIters];
+#pragma unroll
+  for (int j = 0; j < kIters; ++j) {
+    const int i = tid + j * kThreads, ent = i >> 3;
+    v[j] = i >= kStores ? make_uint2(0u, 0u)
+                        : (ent < 256 ? __ldg(reinterpret_cast<const uint2*>(&g_iq2_mag_u8[ent][0]))
+                                     : __ldg(reinterpret_cast<const uint2*>(&g_iq2_sign_mask[ent - 256][0])));
+    // magnitudes -> 64 + m (m < 64), sign masks -> 0x3F per negative byte
+    const uint32_t op = ent < 256 ? 0x40404040u : 0u, and_ = ent < 256 ? 0xFFFFFFFFu : 0x3F3F3F3Fu;
+    v[j] = make_uint2((v[j].x & and_) | op, (v[j].y & and_) | op);
+  }
+#pragma unroll
+  for (int j = 0; j < kIters; ++j) {
+    const int i = tid + j * kThreads;
+    if (i < kStores) *reinterpret_cast<uint4*>(smem + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(v[j].x, v[j].y, v[j].x, v[j].y);
+  }
+}
+
 // Stage = one 16-row tile (one bulk copy, see `fill`).  There is no dedicated producer warp (a 17th
 // warp would cap every thread at 96 registers) and no CTA-wide barrier per tile: each warp writes
 // its 16 partial row sums into the stage's reduction slot and increments the stage's counter
@@ -127,97 +284,19 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
       if (tile < a.tiles) fill(j, tile);
     }
 
-  // ---------------- consumers: tables, built while the first tiles are in flight ----------------
-  // tables: 16 replicas of each 8-byte entry, written two replicas (16 bytes) per store; all of a
-  // thread's loads are issued before its first store (one L2 round trip)
-  {
-    constexpr int kStores = (256 + 128) * 8, kIters = (kStores + kW * 32 - 1) / (kW * 32);
-    uint2 v[kIters];
-#pragma unroll
-    for (int j = 0; j < kIters; ++j) {
-      const int i = threadIdx.x + j * kW * 32, ent = i >> 3;
-      v[j] = i >= kStores ? make_uint2(0u, 0u)
-                          : (ent < 256 ? __ldg(reinterpret_cast<const uint2*>(&g_iq2_mag_u8[ent][0]))
-                                       : __ldg(reinterpret_cast<const uint2*>(&g_iq2_sign_mask[ent - 256][0])));
-      // magnitudes -> 64 + m (m < 64), sign masks -> 0x3F per negative byte
-      const uint32_t op = ent < 256 ? 0x40404040u : 0u, and_ = ent < 256 ? 0xFFFFFFFFu : 0x3F3F3F3Fu;
-      v[j] = make_uint2((v[j].x & and_) | op, (v[j].y & and_) | op);
-    }
-#pragma unroll
-    for (int j = 0; j < kIters; ++j) {
-      const int i = threadIdx.x + j * kW * 32;
-      if (i < kStores) *reinterpret_cast<uint4*>(smem + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(v[j].x, v[j].y, v[j].x, v[j].y);
-    }
-  }
+  // ---------------- tables, built while the first tiles are in flight ----------------
+  i8_fill_tables<kW * 32>(smem, threadIdx.x);
   __syncthreads();
 
   const int g = lane >> 2, t = lane & 3;
-  const bool dlo = (g == t), dhi = (g == t + 4);
   pdl_wait();  // x is produced by the previous kernel
 
-  // ---- x limbs of this warp's slice: lane l converts elements 8l..8l+7 (group l >> 2) ----
-  uint32_t bh0[8], bl0[8], bh1[8], bl1[8];
-  float xs0, xs1;  // 2^(E - 14) of the lane's C columns (groups 2t, 2t+1)
-  int xoff0, xoff1;
-  {
-    const bf16* xs = a.x + warp * 256;
-    const uint4 v = ldg128(xs + 8 * lane);
-    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-    // largest |x| of the group: bf16 magnitudes order like their bit patterns
-    uint32_t mb = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) mb = max(mb, max(wv[i] & 0x7FFFu, (wv[i] >> 16) & 0x7FFFu));
-    mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
-    mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
-    const int emax = max(1, static_cast<int>(mb >> 7));  // effective biased exponent of the maximum
-    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-    int xsum = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      int neg, sig, ex;
-      bf16_parts(i & 1 ? (wv[i >> 1] >> 16) : (wv[i >> 1] & 0xFFFFu), neg, sig, ex);
-      const int xi = bf16_to_fixed(neg, sig, ex, emax);
-      xsum += xi;
-      hw[i >> 2] |= (static_cast<uint32_t>(xi >> 8) & 0xFFu) << (8 * (i & 3));
-      lw[i >> 2] |= (static_cast<uint32_t>(xi) & 0xFFu) << (8 * (i & 3));
-    }
-    xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
-    xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
-    // owner of group c: lane (g = c, t = c) for c < 4, lane (g = c, t = c - 4) for c >= 4.  Step j of
-    // group c = elements 4j..4j+3 = word (j & 1) of lane 4c + (j >> 1).
-    const int c = dlo ? t : (dhi ? t + 4 : 0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int src = 4 * c + (j >> 1);
-      const uint32_t h = __shfl_sync(0xffffffffu, hw[j & 1], src);
-      const uint32_t l = __shfl_sync(0xffffffffu, lw[j & 1], src);
-      bh0[j] = dlo ? h : 0u;
-      bl0[j] = dlo ? l : 0u;
-      bh1[j] = dhi ? h : 0u;
-      bl1[j] = dhi ? l : 0u;
-    }
-    const int e0 = __shfl_sync(0xffffffffu, emax, 4 * (2 * t)), e1 = __shfl_sync(0xffffffffu, emax, 4 * (2 * t + 1));
-    xoff0 = 64 * __shfl_sync(0xffffffffu, xsum, 4 * (2 * t));  // 64 * sum(x_int) of the lane's C columns
-    xoff1 = 64 * __shfl_sync(0xffffffffu, xsum, 4 * (2 * t + 1));
-    xs0 = ldexpf(1.0f, e0 - 141);  // 2^(E - 14), E = emax - 127
-    xs1 = ldexpf(1.0f, e1 - 141);
-  }
-  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
-  const int q0 = (lane & ~3) | ((2 * t) & 3), q1 = (lane & ~3) | ((2 * t + 1) & 3);
-  const int sel_sh = t >= 2 ? 4 : 0;
+  // ---- x fragments of this warp's slice: lane l converts elements 8l..8l+7 (group l >> 2) ----
+  I8XFrag xf;
+  i8_x_frag(ldg128(a.x + warp * 256 + 8 * lane), xf);
   const bool al = (warp & 1) != 0;  // odd super-block: records 4-byte aligned
   const uint32_t so = static_cast<uint32_t>(warp) * 66u;
-
   const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
-  // this warp's records of one stage: grid bytes + sign/scale words of rows g, g+8 x groups t, t+4,
-  // and the two super-block scales
-  auto load_records = [&](const uint8_t* st, uint2 (&rc)[4], uint32_t& dbits) {
-    rc[0] = lds8(st, r0 + so + 2u + 8u * t, al);
-    rc[1] = lds8(st, r0 + so + 34u + 8u * t, al);
-    rc[2] = lds8(st, r1 + so + 2u + 8u * t, al);
-    rc[3] = lds8(st, r1 + so + 34u + 8u * t, al);
-    dbits = ld_u16(st, r0 + so) | (ld_u16(st, r1 + so) << 16);
-  };
   int s = 0;        // stage of this round
   uint32_t ph = 0;  // parity of the stage's current use
   // Records are software-pipelined: a round decodes the records loaded during the previous round
@@ -226,7 +305,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
   uint32_t dbits;
   if (static_cast<int>(blockIdx.x) < a.tiles) {
     mbar_wait(&full[0], 0u, kSiteFullWait);
-    load_records(stages, rc, dbits);
+    i8_records(stages, r0, r1, so, al, rc, dbits);
   }
   for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
     const int sn = s + 1 == a.stages ? 0 : s + 1;
@@ -235,48 +314,11 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
     uint32_t dbitsn = 0;
     if (tile + static_cast<int>(gridDim.x) < a.tiles) {
       mbar_wait(&full[sn], phn, kSiteFullWait);
-      load_records(stages + sn * a.stage_bytes, rcn, dbitsn);
+      i8_records(stages + sn * a.stage_bytes, r0, r1, so, al, rcn, dbitsn);
     }
 
-    int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      uint32_t A[4][2];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        // table offsets: (grid byte e) * 128 and (sign field e) * 128, one shift + one LOP3 each
-        const uint32_t gx = e == 0 ? (rc[r].x << 7) : (rc[r].x >> (8 * e - 7));
-        const uint32_t sy = e == 0 ? (rc[r].y << 7) : (e == 1 ? rc[r].y : (rc[r].y >> (7 * e - 7)));
-        const uint2 X = *reinterpret_cast<const uint2*>(smem + ((gx & 0x7F80u) | lane_off));
-        const uint2 M = *reinterpret_cast<const uint2*>(smem + kI8MagLut + ((sy & 0x3F80u) | lane_off));
-        A[r][0] = X.x - 2u * (X.x & M.x);  // 64 + s*m per byte, no borrow between bytes
-        A[r][1] = X.y - 2u * (X.y & M.y);
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int j = 2 * e + h;
-        imma_u8s8(ch, A[0][h], A[2][h], A[1][h], A[3][h], bh0[j], bh1[j]);
-        imma_u8u8(cl, A[0][h], A[2][h], A[1][h], A[3][h], bl0[j], bl1[j]);
-      }
-    }
-    // exact s32 dot products of the lane's four (row, group) cells: sum(A x) - 64 sum(x)
-    float f[4];
-    f[0] = static_cast<float>(ch[0] * 256 + cl[0] - xoff0);
-    f[1] = static_cast<float>(ch[1] * 256 + cl[1] - xoff1);
-    f[2] = static_cast<float>(ch[2] * 256 + cl[2] - xoff0);
-    f[3] = static_cast<float>(ch[3] * 256 + cl[3] - xoff1);
-    const uint32_t mine = (rc[0].y >> 28) | ((rc[1].y >> 28) << 4) | ((rc[2].y >> 28) << 8) | ((rc[3].y >> 28) << 12);
-    const uint32_t p0 = __shfl_sync(0xffffffffu, mine, q0) >> sel_sh, p1 = __shfl_sync(0xffffffffu, mine, q1) >> sel_sh;
-    const float d0s = fp16_bits_to_f32(dbits & 0xFFFFu) * 0.25f, d1s = fp16_bits_to_f32(dbits >> 16) * 0.25f;
-    // 0.5 + s exactly: float(2^23 + s) - (2^23 - 0.5)
-    const float h00 = __uint_as_float((p0 & 15u) | 0x4B000000u) - 8388607.5f;
-    const float h01 = __uint_as_float((p1 & 15u) | 0x4B000000u) - 8388607.5f;
-    const float h10 = __uint_as_float(((p0 >> 8) & 15u) | 0x4B000000u) - 8388607.5f;
-    const float h11 = __uint_as_float(((p1 >> 8) & 15u) | 0x4B000000u) - 8388607.5f;
-    float acc0 = f[0] * (xs0 * h00) + f[1] * (xs1 * h01);
-    float acc1 = f[2] * (xs0 * h10) + f[3] * (xs1 * h11);
-    acc0 *= d0s;
-    acc1 *= d1s;
+    float acc0, acc1;
+    i8_slice(smem, rc, dbits, xf, acc0, acc1);
 
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
