@@ -376,6 +376,33 @@ def bench_moe_ep(R, steps, warmup, dev, world, rank):
                 experts_per_gpu=el, device_status=rc, note="L2-resident weights (one expert copy per GPU)")
 
 
+def bench_embed(R, steps, warmup, dev, V=131072, K=4096):
+    """Q8Embed gather of R token rows from a [V, K] Q8_0 table (C4's LM-head shape as the embedding).
+    Algorithmic bytes per call: R x (row bytes read + bf16 row written + 8-byte id)."""
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    row_bytes = K // 32 * 34
+    w = gen_weights("q8_0", V, K, seed=3, dev=dev)
+    g = torch.Generator(device="cpu").manual_seed(R)
+    copies = 8  # distinct id sets per pass so consecutive calls read different rows
+    ids = [torch.randint(0, V, (R,), generator=g).to(dev) for _ in range(copies)]
+    outs = [torch.empty(R, K, dtype=torch.bfloat16, device=dev) for _ in range(copies)]
+
+    def one_pass():
+        for i, o in zip(ids, outs):
+            ops.q8_0_embed_into(w, i, o, V, row_bytes, R)
+
+    gr = capture(one_pass)
+    ms = time_graph(gr, steps, warmup)
+    us = ms * 1e3 / (steps * copies)
+    algo = R * (row_bytes + 2 * K + 8)
+    del gr, w
+    return {"us_per_call": round(us, 4), "gbs": round(algo / (us * 1e-6) / 1e9, 2), "algorithmic_bytes": algo,
+            "table": f"[{V}, {row_bytes}] u8 (Q8_0, K={K})"}
+
+
 def bench_e2e_gemv(op, R, N, K, steps, warmup, dev, state):
     """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host."""
     import torch
@@ -590,6 +617,9 @@ def main():
                 cfgs[f"C3_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()}
                 torch.cuda.empty_cache()
             line["configs"] = cfgs
+            line["next_rows"] = {f"Q8Embed_R{R}": bench_embed(R, max(5, args.steps // 2), args.warmup, dev)
+                                 for R in (1, 8, 4096)}
+            torch.cuda.empty_cache()
     if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather
         line["sharded"] = {f"C4_R{R}": bench_rowsplit(R, max(5, args.steps // 2), args.warmup, dev, world, rank)
                            for R in (1, 4)}

@@ -763,6 +763,29 @@ int gguf_ipc_close(void* dev_ptr) {
   return GGUF_OK;
 }
 
+int gguf_q8_0_embed(const void* w, const int64_t* ids, void* out, int64_t vocab, int64_t row_bytes, int64_t R,
+                    void* stream) {
+  t_last_error.clear();
+  if (vocab <= 0) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Embed: invalid weight shape");
+  if (row_bytes <= 0 || row_bytes % 34 != 0 || row_bytes / 34 > (1 << 24))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Embed: row_bytes must be a positive multiple of 34");
+  if (R < 0) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Embed: negative number of ids");
+  if (R == 0) return GGUF_OK;
+  if (!w || !ids || !out) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Embed: null tensor pointer");
+  if (!aligned(w, 2) || !aligned(ids, 8) || !aligned(out, 8))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Embed: w must be 2-byte, ids and out 8-byte aligned");
+  const int nb = static_cast<int>(row_bytes / 34);
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  const int64_t warps = R * ((nb + 3) / 4);
+  const int64_t ctas = std::min<int64_t>((warps + kEmbedWarps - 1) / kEmbedWarps, static_cast<int64_t>(sms) * 8);
+  const cudaError_t e = launch(q8_embed_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kEmbedWarps * 32), 0,
+                               static_cast<cudaStream_t>(stream), static_cast<const uint8_t*>(w), ids, vocab, nb, R,
+                               static_cast<bf16*>(out));
+  if (e != cudaSuccess) return cuda_fail("Q8Embed launch", e);
+  return GGUF_OK;
+}
+
 int gguf_dequantize(int type, const void* w, float* out, int64_t rows, int64_t K, void* stream) {
   t_last_error.clear();
   if (!w || !out || rows < 0 || K <= 0) return fail(GGUF_ERR_INVALID_ARGUMENT, "dequantize: bad arguments");

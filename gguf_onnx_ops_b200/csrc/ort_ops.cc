@@ -170,6 +170,22 @@ void moe_verify(Ort::KernelContext& c, const Attrs& a) {
                                 meta.GetTensorMutableData<int32_t>(), R, E, I, a.topk, stream(c)));
 }
 
+void q8_embed(Ort::KernelContext& c, const Attrs&) {
+  auto w = c.GetInput(0);
+  auto ids = c.GetInput(1);
+  const auto ws = shape(w);
+  const int64_t vocab = ws.empty() ? 0 : ws[0];
+  if (vocab <= 0 || count(w) % vocab != 0) throw std::invalid_argument("Q8Embed: invalid weight shape");
+  const int64_t row_bytes = count(w) / vocab;
+  if (row_bytes <= 0 || row_bytes % 34 != 0)
+    throw std::invalid_argument("Q8Embed: row_bytes must be a positive multiple of 34");
+  auto os = shape(ids);
+  os.push_back(row_bytes / 34 * 32);
+  auto out = c.GetOutput(0, os);
+  check(gguf_q8_0_embed(w.GetTensorRawData(), ids.GetTensorData<int64_t>(), out.GetTensorMutableRawData(), vocab,
+                        row_bytes, count(ids), stream(c)));
+}
+
 // Names, signatures and optional inputs of the reference's 15 ops (src/bolt_ops.cu:1886-2061).
 const std::vector<OpDesc>& op_table() {
   static const std::vector<OpDesc> t = {
@@ -186,7 +202,7 @@ const std::vector<OpDesc>& op_table() {
       {"Nvfp4Gemv", {kBF, kU8, kU8, kF32}, {kBF}, {2}, fp4_gemv},
       {"Q8Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q8_gemv},
       {"Q4Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q4_gemv},
-      {"Q8Embed", {kU8, kI64}, {kBF}, {}, nullptr},
+      {"Q8Embed", {kU8, kI64}, {kBF}, {}, q8_embed},
       {"RmsNorm", {kBF, kF32}, {kBF}, {}, nullptr},
       {"SkipRmsNorm", {kBF, kBF, kF32}, {kBF, kBF}, {}, nullptr},
   };

@@ -343,4 +343,45 @@ __global__ void __launch_bounds__(kEpThreads) moe_finalize_ep_kernel(const float
   if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(pr.state) = epoch;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Q8Embed (src/bolt_ops.cu:1645-1690): out[r, k] = bf16(fp32(d) * q[k]) of row ids[r] of a GGUF Q8_0
+// table [vocab, nb * 34]; ids outside [0, vocab) read row 0.  A warp handles 4 blocks (128
+// elements) of one token: lane -> block lane / 8, elements 4 (lane % 8) .. + 3; the 8-byte outputs
+// of a warp are contiguous (512 bytes).
+// ---------------------------------------------------------------------------------------------
+constexpr int kEmbedWarps = 8;
+
+__global__ void __launch_bounds__(kEmbedWarps * 32) q8_embed_kernel(const uint8_t* __restrict__ w,
+                                                                    const int64_t* __restrict__ ids, int64_t vocab,
+                                                                    int nb, int64_t R, bf16* __restrict__ out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t quads = (static_cast<int64_t>(nb) + 3) / 4;  // 4-block groups per token
+  const int64_t total = R * quads;
+  for (int64_t wi = static_cast<int64_t>(blockIdx.x) * kEmbedWarps + (threadIdx.x >> 5); wi < total;
+       wi += static_cast<int64_t>(gridDim.x) * kEmbedWarps) {
+    const int64_t r = wi / quads;
+    const int b = static_cast<int>(wi % quads) * 4 + (lane >> 3);
+    if (b >= nb) continue;
+    int64_t tok = __ldg(ids + r);
+    if (tok < 0 || tok >= vocab) tok = 0;
+    const uint8_t* blk = w + (tok * nb + b) * 34;
+    const int j = lane & 7;
+    const float d = fp16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(blk)));
+    // q bytes 4j..4j+3 start 2-byte aligned: two 16-bit loads
+    const uint32_t qlo = __ldg(reinterpret_cast<const uint16_t*>(blk + 2 + 4 * j));
+    const uint32_t qhi = __ldg(reinterpret_cast<const uint16_t*>(blk + 4 + 4 * j));
+    const uint32_t q = qlo | (qhi << 16);
+    const float v0 = d * static_cast<float>(static_cast<int8_t>(q & 0xFFu));
+    const float v1 = d * static_cast<float>(static_cast<int8_t>((q >> 8) & 0xFFu));
+    const float v2 = d * static_cast<float>(static_cast<int8_t>((q >> 16) & 0xFFu));
+    const float v3 = d * static_cast<float>(static_cast<int8_t>(q >> 24));
+    uint2 o;
+    o.x = pack_bf16x2(v0, v1);
+    o.y = pack_bf16x2(v2, v3);
+    *reinterpret_cast<uint2*>(out + (r * nb + b) * 32 + 4 * j) = o;
+  }
+}
+
 }  // namespace gguf_b200

@@ -6,6 +6,7 @@ the outputs with the reference's shapes (as ``KernelContext::GetOutput`` would) 
 C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
 
     Q8Gemv(x, w, scales=None, gguf=1)                  -> y        src/bolt_ops.cu:1592-1643, :2018-2027
+    Q8Embed(w, input_ids)                              -> out      src/bolt_ops.cu:1645-1690, :2038-2044
     Q4Gemv(x, w, scales=None, iq2=3)                   -> y        src/bolt_ops.cu:1592-1643, :2028-2037
     Nvfp4Gemv(x, w, w_scale, gscale, gguf=1)           -> y        src/bolt_ops.cu:1411-1469, :2004-2016
     MoeRouteGGUF(x, gate_w, bias, topk, scale)         -> idx, weights, scores    src/bolt_ops.cu:512-546
@@ -111,6 +112,30 @@ def Nvfp4Gemv(x: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor | None, gs
     y = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
     nvfp4_gemv_into(x, w, gscale, y, R, N, K)
     return y
+
+
+# ------------------------------------------------------------------------------------------------
+# Embedding
+# ------------------------------------------------------------------------------------------------
+def q8_0_embed_into(w, ids, out, vocab: int, row_bytes: int, R: int, stream=None) -> None:
+    check(load().gguf_q8_0_embed(_ptr(w), _ptr(ids), _ptr(out), vocab, row_bytes, R, _stream(stream)))
+
+
+def Q8Embed(w: torch.Tensor, input_ids: torch.Tensor) -> torch.Tensor:
+    """Gather + dequantise rows of a raw GGUF Q8_0 table w [vocab, (K/32)*34] -> bf16 [..., K]
+    (src/bolt_ops.cu:1645-1690, :2038-2044); out-of-range ids read row 0."""
+    _need(w, "w", torch.uint8, "Q8Embed")
+    _need(input_ids, "input_ids", torch.int64, "Q8Embed")
+    vocab = w.shape[0]
+    if vocab <= 0 or w.numel() % vocab != 0:
+        raise ValueError("Q8Embed: invalid weight shape")
+    row_bytes = w.numel() // vocab
+    if row_bytes <= 0 or row_bytes % Q8_0_BYTES != 0:
+        raise ValueError("Q8Embed: row_bytes must be a positive multiple of 34")
+    K = row_bytes // Q8_0_BYTES * 32
+    out = torch.empty(*input_ids.shape, K, dtype=torch.bfloat16, device=w.device)
+    q8_0_embed_into(w, input_ids, out, vocab, row_bytes, input_ids.numel())
+    return out
 
 
 # ------------------------------------------------------------------------------------------------

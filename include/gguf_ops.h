@@ -71,6 +71,15 @@ GGUF_OPS_API int gguf_nvfp4_gemv(const void* x, const void* w, const float* gsca
                                  int64_t K, void* stream);
 
 /*
+ * Q8Embed:  out[..., k] = bf16(fp32(d) * q[k]) of the rows input_ids[...] of a GGUF Q8_0 embedding
+ * table w [vocab, row_bytes] (row_bytes = (K/32)*34); ids outside [0, vocab) read row 0.
+ * ids: int64 [R] (any shape, flattened); out: bf16 [R, K].  R = 0 is a no-op.
+ * Replaces Q8EmbedState::ComputeV2 (src/bolt_ops.cu:1662-1688).
+ */
+GGUF_OPS_API int gguf_q8_0_embed(const void* w, const int64_t* ids, void* out, int64_t vocab, int64_t row_bytes,
+                                 int64_t R, void* stream);
+
+/*
  * MoeRouteGGUF:  scores[R,E] = sigmoid(x[R,K] @ bf16(gate_w)^T);  idx[R,topk] = top-k of scores + bias
  * (descending, ties to the lower expert index);  weights = s_sel / (sum s_sel + 1e-20) * scale.
  * x bf16 [R,K]; gate_w f32 [E,K]; bias f32 [E] -> idx i32 [R,topk], weights f32 [R,topk], scores f32 [R,E].

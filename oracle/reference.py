@@ -7,6 +7,8 @@
 * ``route_ref`` -- sigmoid router with bf16-rounded gate weights (``src/bolt_ops.cu:399-404``),
   bias-corrected top-k with ties to the lower index (``src/bolt_ops.cu:489``), weights
   ``s / (sum s + 1e-20) * scale`` (``src/bolt_ops.cu:505-508``); logits in fp64.
+* ``embed_ref`` -- Q8Embed: rows ``ids`` of a Q8_0 table dequantised and rounded to bf16, ids
+  outside [0, vocab) reading row 0 (``src/bolt_ops.cu:1645-1660``, ``:1674-1687``).
 * ``rel_l2``    -- the reference's metric ``||a-b|| / ||b||`` (``tests/test_bolt_ops.py:62-64``).
 """
 
@@ -59,6 +61,21 @@ def moe_ref(z, idx: np.ndarray, w: np.ndarray, d1: np.ndarray, d2: np.ndarray):
             h_all[t * k + j] = h
             p_all[t * k + j] = p
     return out, h_all, p_all
+
+
+def embed_ref(w_raw: np.ndarray, ids) -> np.ndarray:
+    """w_raw: uint8 [vocab, row_bytes] Q8_0 table; ids: int64 of any shape -> fp32 [..., K] holding
+    bf16 values.  Element value = fp32(fp16 d) * int8 q, one rounding to bf16."""
+    from .quants import dequant_q8_0
+
+    w_raw = np.asarray(w_raw, dtype=np.uint8)
+    ids = np.asarray(ids, dtype=np.int64)
+    vocab = w_raw.shape[0]
+    flat = ids.reshape(-1)
+    rows = np.where((flat < 0) | (flat >= vocab), 0, flat)
+    K = w_raw.shape[1] // 34 * 32
+    deq = dequant_q8_0(w_raw[rows]) if rows.size else np.zeros((0, K), np.float32)
+    return bf16_round(deq.astype(np.float32)).reshape(*ids.shape, K)
 
 
 def route_ref(x, gate_w: np.ndarray, bias: np.ndarray, topk: int, scale: float, tie_eps: float = 1e-6):

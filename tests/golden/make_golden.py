@@ -10,6 +10,8 @@ Every expected value here comes from the reference's own CPU path, not from the 
   gguf-py dequantised experts (kept in fp32: the repo's kernels consume the exact weights);
 * router outputs: the harness's torch router (tests/test_bolt_ops.py:116-119) on bf16-rounded gate
   weights, as MoeRouteGGUF specifies (src/bolt_ops.cu:441-448);
+* Q8Embed output: the harness's torch expression (tests/test_bolt_ops.py:310-311) with ids outside
+  [0, vocab) replaced by row 0, the op's rule (src/bolt_ops.cu:1680);
 * the IQ2_XXS codebook: parsed from the reference's src/iq2xxs_grid.h (kIq2xxsGrid, line 6, and
   kIq2xxsGridBf16, line 75).
 
@@ -17,7 +19,7 @@ Inputs use the reference test builders (iq2_native_blocks, the Q8 block builder,
 builder of tests/test_bolt_ops.py:210-215, :290-294, :274-275) with numpy RNG, plus the BASELINE
 config distributions at reduced sizes.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference /root/reference] [--only embed]
 """
 
 from __future__ import annotations
@@ -35,7 +37,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from oracle import inputs as I  # noqa: E402  (input builders only; expected values come from gguf/torch)
-from tests.golden.cases import GEMV_CASES, moe_inputs, route_inputs, sha  # noqa: E402
+from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, route_inputs, sha  # noqa: E402
 
 
 def gguf_deq(raw: np.ndarray, qt) -> np.ndarray:
@@ -58,10 +60,28 @@ def parse_reference_grid(ref: str):
     return grid64, gridbf
 
 
+def make_embed():
+    blk, ids = embed_inputs()
+    V = blk.shape[0]
+    nb = blk.shape[1] // 34
+    t = torch.from_numpy(blk).reshape(V, nb, 34)
+    d = t[:, :, :2].contiguous().view(torch.float16).reshape(V, nb)
+    table = (d.float().unsqueeze(-1) * t[:, :, 2:].contiguous().view(torch.int8).float()).reshape(V, -1).bfloat16()
+    tid = torch.from_numpy(ids)
+    tid = torch.where((tid >= 0) & (tid < V), tid, torch.zeros_like(tid))
+    out = table[tid]
+    np.savez_compressed(os.path.join(HERE, "embed.npz"), out_bf16=out.view(torch.int16).numpy().view(np.uint16),
+                        sha=np.array(sha(blk, ids)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["embed"], default=None)
     args = ap.parse_args()
+    if args.only == "embed":
+        make_embed()
+        return
     from gguf import GGMLQuantizationType as Q
 
     # 1. IQ2_XXS codebook of the reference
@@ -126,6 +146,7 @@ def main():
             h = (torch.relu(h) ** 2).bfloat16().float()
             ref[t] += float(wts[t, j]) * (h @ d2[e].T).bfloat16().float()
     np.savez_compressed(os.path.join(HERE, "moe.npz"), out=ref.numpy(), sha=np.array(sha(z, idx, wts, b1, b2)))
+    make_embed()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

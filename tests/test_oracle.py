@@ -7,7 +7,7 @@ import torch
 
 import oracle as O
 from oracle import inputs as I
-from tests.golden.cases import GEMV_CASES, moe_inputs, route_inputs, sha
+from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, route_inputs, sha
 from tests.util import rel
 
 
@@ -109,6 +109,23 @@ def test_moe_ref_matches_golden(golden):
     out, h, part = O.moe_ref(z, idx, w, d1, d2)
     # fp64 vs torch fp32 sums may flip an occasional bf16 rounding of h / part
     assert rel(out, d["out"]) < 2e-3
+
+
+def test_embed_ref_matches_golden(golden):
+    d = golden("embed.npz")
+    blk, ids = embed_inputs()
+    assert sha(blk, ids) == str(d["sha"]), "input builder drifted"
+    out = O.embed_ref(blk, ids)
+    assert out.shape == (2, 9, 1024)
+    assert np.array_equal(O.bf16_bits(out), d["out_bf16"])
+    # ids outside [0, vocab) read row 0 (src/bolt_ops.cu:1680)
+    assert np.array_equal(out[0, 3], out[1, 0]) and np.array_equal(out[1, 8], O.embed_ref(blk, np.array([0]))[0])
+
+
+def test_embed_ref_empty_ids():
+    blk, _ = embed_inputs()
+    assert O.embed_ref(blk, np.zeros((0,), np.int64)).shape == (0, 1024)
+    assert O.embed_ref(blk, np.zeros((3, 0), np.int64)).shape == (3, 0, 1024)
 
 
 def test_bf16_round_matches_torch():
