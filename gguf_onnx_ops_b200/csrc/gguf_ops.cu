@@ -777,11 +777,16 @@ int gguf_q8_0_embed(const void* w, const int64_t* ids, void* out, int64_t vocab,
   const int nb = static_cast<int>(row_bytes / 34);
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
-  const int64_t warps = R * ((nb + 3) / 4);
+  // Decode-sized gathers (a few rows) keep the scalar kernel: its load -> store chain is the shortest.
+  const int64_t units = R * (nb / 8);
+  const bool vec = nb % 8 == 0 && aligned(w, 16) && aligned(out, 16) && units > 512;
+  const int U = units > 4096 ? 4 : 1;
+  const int64_t warps = vec ? (units + U - 1) / U : R * ((nb + 3) / 4);
   const int64_t ctas = std::min<int64_t>((warps + kEmbedWarps - 1) / kEmbedWarps, static_cast<int64_t>(sms) * 8);
-  const cudaError_t e = launch(q8_embed_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kEmbedWarps * 32), 0,
-                               static_cast<cudaStream_t>(stream), static_cast<const uint8_t*>(w), ids, vocab, nb, R,
-                               static_cast<bf16*>(out));
+  const auto kern = !vec ? q8_embed_kernel : U == 4 ? q8_embed_vec_kernel<4> : q8_embed_vec_kernel<1>;
+  const cudaError_t e = launch(kern, dim3(static_cast<unsigned>(ctas)),
+                               dim3(kEmbedWarps * 32), 0, static_cast<cudaStream_t>(stream),
+                               static_cast<const uint8_t*>(w), ids, vocab, nb, R, static_cast<bf16*>(out));
   if (e != cudaSuccess) return cuda_fail("Q8Embed launch", e);
   return GGUF_OK;
 }

@@ -384,4 +384,65 @@ __global__ void __launch_bounds__(kEmbedWarps * 32) q8_embed_kernel(const uint8_
   }
 }
 
+// Vector form for rows whose block count is a multiple of 8 (row_bytes a multiple of 272 = 17 x 16 B)
+// and 16-byte aligned tensors.  Unit = one token x 8 blocks: 272 bytes in (17 lanes x 16 B), 256
+// elements out (32 lanes x 16 B).  A warp loads kEmbedU units before decoding any (bytes in flight per
+// SM = warps x kEmbedU x 272), stages them in its own shared slice and writes 512 contiguous bytes per
+// unit.  Lane l decodes block l / 4, elements 8 (l % 4) .. + 7.  Few units (decode) take kEmbedU = 1
+// so that every unit has its own warp.
+template <int kEmbedU>
+__global__ void __launch_bounds__(kEmbedWarps * 32) q8_embed_vec_kernel(const uint8_t* __restrict__ w,
+                                                                        const int64_t* __restrict__ ids,
+                                                                        int64_t vocab, int nb, int64_t R,
+                                                                        bf16* __restrict__ out) {
+  __shared__ __align__(16) uint8_t stage[kEmbedWarps][kEmbedU][272];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gpr = nb >> 3;  // 8-block groups per row
+  const int64_t units = R * gpr;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kEmbedWarps * kEmbedU;
+  const int64_t row_bytes = static_cast<int64_t>(nb) * 34;
+  for (int64_t u0 = (static_cast<int64_t>(blockIdx.x) * kEmbedWarps + warp) * kEmbedU; u0 < units; u0 += stride) {
+    int64_t r = u0 / gpr;
+    int g = static_cast<int>(u0 - r * gpr);
+    uint4 v[kEmbedU];
+#pragma unroll
+    for (int i = 0; i < kEmbedU; ++i) {
+      v[i] = make_uint4(0u, 0u, 0u, 0u);
+      if (u0 + i < units && lane < 17) {
+        int64_t tok = __ldg(ids + r);
+        if (tok < 0 || tok >= vocab) tok = 0;
+        v[i] = __ldg(reinterpret_cast<const uint4*>(w + tok * row_bytes + g * 272) + lane);
+      }
+      if (++g == gpr) g = 0, ++r;
+    }
+#pragma unroll
+    for (int i = 0; i < kEmbedU; ++i)
+      if (lane < 17) *reinterpret_cast<uint4*>(&stage[warp][i][lane * 16]) = v[i];
+    __syncwarp();
+    const int b = lane >> 2, j = lane & 3;
+#pragma unroll
+    for (int i = 0; i < kEmbedU; ++i) {
+      if (u0 + i >= units) break;
+      const uint8_t* sb = &stage[warp][i][34 * b];
+      const float d = fp16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sb));
+      const uint16_t* q16 = reinterpret_cast<const uint16_t*>(sb + 2 + 8 * j);
+      const uint32_t qa = q16[0] | (static_cast<uint32_t>(q16[1]) << 16);
+      const uint32_t qb = q16[2] | (static_cast<uint32_t>(q16[3]) << 16);
+      uint4 o;
+      o.x = pack_bf16x2(d * static_cast<float>(static_cast<int8_t>(qa & 0xFFu)),
+                        d * static_cast<float>(static_cast<int8_t>((qa >> 8) & 0xFFu)));
+      o.y = pack_bf16x2(d * static_cast<float>(static_cast<int8_t>((qa >> 16) & 0xFFu)),
+                        d * static_cast<float>(static_cast<int8_t>(qa >> 24)));
+      o.z = pack_bf16x2(d * static_cast<float>(static_cast<int8_t>(qb & 0xFFu)),
+                        d * static_cast<float>(static_cast<int8_t>((qb >> 8) & 0xFFu)));
+      o.w = pack_bf16x2(d * static_cast<float>(static_cast<int8_t>((qb >> 16) & 0xFFu)),
+                        d * static_cast<float>(static_cast<int8_t>(qb >> 24)));
+      *reinterpret_cast<uint4*>(out + (u0 + i) * 256 + lane * 8) = o;
+    }
+    __syncwarp();
+  }
+}
+
 }  // namespace gguf_b200

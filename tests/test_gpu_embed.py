@@ -29,6 +29,8 @@ def test_embed_golden_bit_exact(cuda, golden):
                                        (1000, 2048, (3, 77)),
                                        (37, 96, (5,)),           # K not a multiple of 128: partial 4-block group
                                        (7, 32, (2, 3, 4)),
+                                       (300, 2080, (2, 50)),     # 65 blocks per row: scalar kernel
+                                       (2000, 768, (4001,)),     # 3 units per row, 4 per warp, ragged tail
                                        (32000, 4096, (4, 2048))])
 def test_embed_random_bit_exact(cuda, V, K, shape):
     g = I.rng(V * 31 + K)
