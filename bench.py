@@ -403,6 +403,48 @@ def bench_embed(R, steps, warmup, dev, V=131072, K=4096):
             "table": f"[{V}, {row_bytes}] u8 (Q8_0, K={K})"}
 
 
+def bench_gguf_load(dev, rows=131072, K=4096, reps=3):
+    """GGUF loader: a page-cache resident synthetic file holding one Q8_0 [rows, K] tensor (C4's LM
+    head, 557 MB) copied into HBM by gguf_file_upload; GB/s = tensor bytes / wall time of the
+    (host-synchronous) call, median of reps."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    from gguf import GGMLQuantizationType as Q
+    from gguf import GGUFWriter
+
+    from gguf_onnx_ops_b200.gguf_file import GGUFFile
+
+    row_bytes = K // 32 * 34
+    tmpdir = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    with tempfile.TemporaryDirectory(dir=tmpdir) as d:
+        path = os.path.join(d, "lm_head.gguf")
+        data = np.random.default_rng(0).integers(0, 256, size=(rows, row_bytes), dtype=np.uint8)
+        w = GGUFWriter(path, "bench")
+        w.add_tensor("output.weight", data, raw_dtype=Q.Q8_0)
+        w.write_header_to_file()
+        w.write_kv_data_to_file()
+        w.write_tensors_to_file()
+        w.close()
+        del data
+        with GGUFFile(path) as f:
+            out = torch.empty(rows, row_bytes, dtype=torch.uint8, device=dev)
+            f.load("output.weight", out=out)  # warm-up: page cache, staging buffers
+            times = []
+            for _ in range(reps):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                f.load("output.weight", out=out)
+                times.append(time.perf_counter() - t0)
+            nbytes = f["output.weight"].nbytes
+            del out
+    t = statistics.median(times)
+    return {"gbs": round(nbytes / t / 1e9, 2), "ms": round(t * 1e3, 2), "bytes": nbytes,
+            "source": "page-cache resident file (tmpfs when available)"}
+
+
 def bench_e2e_gemv(op, R, N, K, steps, warmup, dev, state):
     """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host."""
     import torch
@@ -620,6 +662,7 @@ def main():
             line["next_rows"] = {f"Q8Embed_R{R}": bench_embed(R, max(5, args.steps // 2), args.warmup, dev)
                                  for R in (1, 8, 4096)}
             torch.cuda.empty_cache()
+            line["next_rows"]["GGUF_load_C4_lm_head"] = bench_gguf_load(dev)
     if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather
         line["sharded"] = {f"C4_R{R}": bench_rowsplit(R, max(5, args.steps // 2), args.warmup, dev, world, rank)
                            for R in (1, 4)}

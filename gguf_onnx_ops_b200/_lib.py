@@ -17,6 +17,7 @@ GGUF_ERR_INVALID_ARGUMENT = 1
 GGUF_ERR_CUDA = 2
 GGUF_ERR_NOT_IMPLEMENTED = 3
 GGUF_ERR_DEVICE = 4
+GGUF_ERR_IO = 5
 
 GGUF_TYPE_Q8_0 = 8
 GGUF_TYPE_IQ2_XXS = 16
@@ -43,7 +44,43 @@ SIGNATURES = {
     "gguf_device_status": (_I32, [ctypes.POINTER(ctypes.c_int)]),
     "gguf_set_pdl": (None, [_I32]),
     "gguf_set_fast_paths": (None, [_I32]),
+    # include/gguf_file.h
+    "gguf_file_open": (_I32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "gguf_file_close": (None, [_P]),
+    "gguf_file_header": (_I32, [_P, ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int64),
+                                ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
+    "gguf_file_data": (_P, [_P]),
+    "gguf_file_tensor_count": (_I64, [_P]),
+    "gguf_file_tensor_info": (_I32, [_P, _I64, _P]),
+    "gguf_file_find_tensor": (_I64, [_P, ctypes.c_char_p]),
+    "gguf_file_kv_count": (_I64, [_P]),
+    "gguf_file_kv": (_I32, [_P, _I64, _P]),
+    "gguf_file_find_kv": (_I64, [_P, ctypes.c_char_p]),
+    "gguf_type_size": (_I32, [ctypes.c_int32, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
+    "gguf_file_upload": (_I32, [_P, _P, _I64, _P]),
 }
+
+
+class GgufTensorInfo(ctypes.Structure):
+    """Mirror of GgufTensorInfo (include/gguf_file.h)."""
+
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_int32), ("n_dims", ctypes.c_int32),
+                ("dims", ctypes.c_int64 * 4), ("offset", ctypes.c_int64), ("nbytes", ctypes.c_int64),
+                ("block_elems", ctypes.c_int64), ("block_bytes", ctypes.c_int64), ("row_bytes", ctypes.c_int64)]
+
+
+class GgufKv(ctypes.Structure):
+    """Mirror of GgufKv (include/gguf_file.h)."""
+
+    _fields_ = [("key", ctypes.c_char_p), ("type", ctypes.c_int32), ("elem_type", ctypes.c_int32),
+                ("count", ctypes.c_int64), ("data", ctypes.c_void_p), ("nbytes", ctypes.c_int64)]
+
+
+class GgufUploadItem(ctypes.Structure):
+    """Mirror of GgufUploadItem (include/gguf_file.h)."""
+
+    _fields_ = [("tensor", ctypes.c_int64), ("byte_offset", ctypes.c_int64), ("nbytes", ctypes.c_int64),
+                ("dst", ctypes.c_void_p)]
 
 
 class GgufPeerOut(ctypes.Structure):
@@ -93,6 +130,8 @@ def check(rc: int) -> None:
             raise ValueError(msg)
         if rc == GGUF_ERR_NOT_IMPLEMENTED:
             raise NotImplementedError(msg)
+        if rc == GGUF_ERR_IO:
+            raise OSError(msg)
         raise GgufOpsError(rc, msg)
 
 

@@ -59,6 +59,11 @@ def build(force: bool = False, verbose: bool = False) -> str:
         cmd += ["-Xptxas", "-v"]
     subprocess.run(cmd, check=True)
     objs.append(os.path.join(tmp, "gguf_ops.o"))
+    host_flags = ["-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-pthread", "-Wall", "-I",
+                  os.path.join(ROOT, "include"), "-I", os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")]
+    subprocess.run(["g++", *host_flags, "-c", os.path.join(CSRC, "gguf_file.cc"), "-o", os.path.join(tmp, "gguf_file.o")],
+                   check=True)
+    objs.append(os.path.join(tmp, "gguf_file.o"))
     ort_inc = os.environ.get("ORT_INCLUDE_DIR", "")
     if ort_inc and os.path.exists(os.path.join(ort_inc, "onnxruntime_c_api.h")):
         cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-I", ort_inc, "-I", os.path.join(ROOT, "include"),

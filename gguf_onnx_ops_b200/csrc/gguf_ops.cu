@@ -360,6 +360,11 @@ std::string dims(int64_t R, int64_t N, int64_t K) {
 bool int_range(int64_t v) { return v > 0 && v < (1ll << 31); }
 
 }  // namespace
+
+// Error channel shared with the host-only translation units (gguf_file.cc).
+int set_error(int code, const std::string& msg) { return fail(code, msg); }
+void clear_error() { t_last_error.clear(); }
+
 }  // namespace gguf_b200
 
 using namespace gguf_b200;

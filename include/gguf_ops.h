@@ -32,7 +32,8 @@ enum {
   GGUF_ERR_INVALID_ARGUMENT = 1, /* shape / attribute / alignment contract violated (ORT_INVALID_ARGUMENT / ORT_FAIL) */
   GGUF_ERR_CUDA = 2,             /* a CUDA launch or runtime call failed */
   GGUF_ERR_NOT_IMPLEMENTED = 3,  /* legacy (non-GGUF) layout requested */
-  GGUF_ERR_DEVICE = 4            /* a kernel reported a device-side error (bounded wait expired) */
+  GGUF_ERR_DEVICE = 4,           /* a kernel reported a device-side error (bounded wait expired) */
+  GGUF_ERR_IO = 5                /* a file could not be opened or mapped (gguf_file.h) */
 };
 
 /* GGUF tensor type ids (ggml numbering, docs/GGUF_ONNX_Custom_Ops.md:13-18). */

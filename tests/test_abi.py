@@ -10,18 +10,20 @@ import pytest
 from gguf_onnx_ops_b200 import _lib
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "gguf_ops.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if h.endswith(".h")]
 
 
 def declared():
-    src = open(HEADER).read()
+    src = "".join(open(h).read() for h in HEADERS)
     return re.findall(r"GGUF_OPS_API\s+[\w\s\*]+?\b(gguf_\w+)\s*\(", src)
 
 
 def test_header_declares_the_hot_path():
     names = set(declared())
     for n in ("gguf_q8_0_gemv", "gguf_iq2_xxs_gemv", "gguf_nvfp4_gemv", "gguf_moe_route", "gguf_moe_verify_iq2_xxs",
-              "gguf_dequantize", "gguf_last_error", "gguf_device_status"):
+              "gguf_dequantize", "gguf_last_error", "gguf_device_status", "gguf_q8_0_embed", "gguf_file_open",
+              "gguf_file_upload"):
         assert n in names
 
 
