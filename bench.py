@@ -403,6 +403,33 @@ def bench_embed(R, steps, warmup, dev, V=131072, K=4096):
             "table": f"[{V}, {row_bytes}] u8 (Q8_0, K={K})"}
 
 
+def bench_norm(R, steps, warmup, dev, H=4096, skip=True):
+    """SkipRmsNorm (sum written) or RmsNorm over [R, H] bf16; algorithmic bytes per call:
+    R*H*2 x (x + skip + y + sum, or x + y) + 4H of gamma."""
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    copies = max(1, min(8, (256 << 20) // max(1, R * H * 2 * 4)))  # distinct buffers per pass
+    xs = [torch.randn(R, H, device=dev).bfloat16() for _ in range(copies)]
+    ss = [torch.randn(R, H, device=dev).bfloat16() for _ in range(copies)] if skip else [None] * copies
+    ys = [torch.empty(R, H, dtype=torch.bfloat16, device=dev) for _ in range(copies)]
+    sums = [torch.empty(R, H, dtype=torch.bfloat16, device=dev) for _ in range(copies)] if skip else [None] * copies
+    gamma = torch.rand(H, device=dev) + 0.5
+
+    def one_pass():
+        for x, sk, y, su in zip(xs, ss, ys, sums):
+            ops.rms_norm_into(x, sk, gamma, y, su, R, H, 1e-5)
+
+    g = capture(one_pass)
+    ms = time_graph(g, steps, warmup)
+    us = ms * 1e3 / (steps * copies)
+    algo = R * H * 2 * (4 if skip else 2) + 4 * H
+    del g
+    return {"us_per_call": round(us, 4), "gbs": round(algo / (us * 1e-6) / 1e9, 2), "algorithmic_bytes": algo,
+            "op": "SkipRmsNorm (sum written)" if skip else "RmsNorm", "H": H}
+
+
 def bench_gguf_load(dev, rows=131072, K=4096, reps=3):
     """GGUF loader: a page-cache resident synthetic file holding one Q8_0 [rows, K] tensor (C4's LM
     head, 557 MB) copied into HBM by gguf_file_upload; GB/s = tensor bytes / wall time of the
@@ -661,6 +688,10 @@ def main():
             line["configs"] = cfgs
             line["next_rows"] = {f"Q8Embed_R{R}": bench_embed(R, max(5, args.steps // 2), args.warmup, dev)
                                  for R in (1, 8, 4096)}
+            torch.cuda.empty_cache()
+            for R in (1, 8, 4096):
+                line["next_rows"][f"SkipRmsNorm_R{R}"] = bench_norm(R, max(5, args.steps // 2), args.warmup, dev)
+            line["next_rows"]["RmsNorm_R1"] = bench_norm(1, max(5, args.steps // 2), args.warmup, dev, skip=False)
             torch.cuda.empty_cache()
             line["next_rows"]["GGUF_load_C4_lm_head"] = bench_gguf_load(dev)
     if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather

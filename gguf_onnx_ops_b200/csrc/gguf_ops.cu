@@ -22,6 +22,7 @@
 #include "iq2_rowblock.cuh"
 #include "moe_fused.cuh"
 #include "small_kernels.cuh"
+#include "rms_norm.cuh"
 
 namespace gguf_b200 {
 
@@ -793,6 +794,42 @@ int gguf_q8_0_embed(const void* w, const int64_t* ids, void* out, int64_t vocab,
                                dim3(kEmbedWarps * 32), 0, static_cast<cudaStream_t>(stream),
                                static_cast<const uint8_t*>(w), ids, vocab, nb, R, static_cast<bf16*>(out));
   if (e != cudaSuccess) return cuda_fail("Q8Embed launch", e);
+  return GGUF_OK;
+}
+
+int gguf_rms_norm(const void* x, const void* skip, const float* gamma, void* y, void* sum, int64_t R, int64_t H,
+                  float eps, void* stream) {
+  t_last_error.clear();
+  const char* op = skip ? "SkipRmsNorm" : "RmsNorm";
+  if (H <= 0 || H % 8 != 0 || H > (1 << 24))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": hidden size H must be a positive multiple of 8");
+  if (R < 0) return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": negative number of rows");
+  if (R == 0) return GGUF_OK;
+  if (!x || !gamma || !y) return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": null tensor pointer");
+  if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(y, 16) || (skip && !aligned(skip, 16)) ||
+      (sum && !aligned(sum, 16)))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": tensors must be 16-byte aligned");
+  if (!skip) sum = nullptr;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  const int nc = static_cast<int>((H / 8 + kNormThreads - 1) / kNormThreads);
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(R, static_cast<int64_t>(sms) * 4)));
+  auto* s = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const bf16*>(x);
+  const auto* sb = static_cast<const bf16*>(skip);
+  auto* yb = static_cast<bf16*>(y);
+  auto* ob = static_cast<bf16*>(sum);
+  const int h = static_cast<int>(H);
+  cudaError_t e;
+  auto go = [&](auto kern) { return launch(kern, grid, dim3(kNormThreads), 0, s, xb, sb, gamma, eps, h, R, yb, ob); };
+  if (skip) {
+    e = nc == 1 ? go(rms_norm_kernel<true, 1>) : nc == 2 ? go(rms_norm_kernel<true, 2>)
+      : nc <= 4 ? go(rms_norm_kernel<true, 4>) : go(rms_norm_kernel<true, 0>);
+  } else {
+    e = nc == 1 ? go(rms_norm_kernel<false, 1>) : nc == 2 ? go(rms_norm_kernel<false, 2>)
+      : nc <= 4 ? go(rms_norm_kernel<false, 4>) : go(rms_norm_kernel<false, 0>);
+  }
+  if (e != cudaSuccess) return cuda_fail(skip ? "SkipRmsNorm launch" : "RmsNorm launch", e);
   return GGUF_OK;
 }
 

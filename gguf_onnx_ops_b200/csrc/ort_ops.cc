@@ -36,7 +36,7 @@ struct NotImplemented : std::runtime_error {
 // Attributes of one node, read once at kernel creation.
 struct Attrs {
   int64_t gguf = 0, iq2 = 0, topk = 0;
-  float scale = 1.0f;
+  float scale = 1.0f, epsilon = 1e-5f;
 };
 
 int64_t opt_int(const OrtKernelInfo* info, const char* name, int64_t dflt) {
@@ -65,6 +65,7 @@ struct OpDesc {
   std::vector<ONNXTensorElementDataType> in, out;
   std::vector<int> optional_in;  // indices of optional inputs
   ComputeFn compute;             // nullptr: op outside the GGUF decode path
+  std::vector<int> optional_out = {};  // indices of optional outputs
 };
 
 // ---- helpers over the C++ API ----
@@ -186,6 +187,27 @@ void q8_embed(Ort::KernelContext& c, const Attrs&) {
                         row_bytes, count(ids), stream(c)));
 }
 
+template <bool kSkip>
+void rms_norm(Ort::KernelContext& c, const Attrs& a) {
+  auto x = c.GetInput(0);
+  auto xs = shape(x);
+  if (xs.empty()) throw std::invalid_argument("RmsNorm: input must be at least 1D");
+  const int64_t H = xs.back();
+  if (H <= 0 || H % 8 != 0) throw std::invalid_argument("RmsNorm: hidden size H must be a positive multiple of 8");
+  if (kSkip && count(c.GetInput(1)) != count(x)) throw std::invalid_argument("SkipRmsNorm: skip shape mismatch");
+  auto gamma = c.GetInput(kSkip ? 2 : 1);
+  if (count(gamma) != H) throw std::invalid_argument("RmsNorm: gamma size mismatch");
+  auto y = c.GetOutput(0, xs);
+  void* sum = nullptr;
+  if (kSkip && c.GetOutputCount() > 1) {
+    auto so = c.GetOutput(1, xs);
+    if (so) sum = so.GetTensorMutableRawData();
+  }
+  check(gguf_rms_norm(x.GetTensorRawData(), kSkip ? c.GetInput(1).GetTensorRawData() : nullptr,
+                      gamma.GetTensorData<float>(), y.GetTensorMutableRawData(), sum, count(x) / H, H, a.epsilon,
+                      stream(c)));
+}
+
 // Names, signatures and optional inputs of the reference's 15 ops (src/bolt_ops.cu:1886-2061).
 const std::vector<OpDesc>& op_table() {
   static const std::vector<OpDesc> t = {
@@ -203,8 +225,8 @@ const std::vector<OpDesc>& op_table() {
       {"Q8Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q8_gemv},
       {"Q4Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q4_gemv},
       {"Q8Embed", {kU8, kI64}, {kBF}, {}, q8_embed},
-      {"RmsNorm", {kBF, kF32}, {kBF}, {}, nullptr},
-      {"SkipRmsNorm", {kBF, kBF, kF32}, {kBF, kBF}, {}, nullptr},
+      {"RmsNorm", {kBF, kF32}, {kBF}, {}, rms_norm<false>},
+      {"SkipRmsNorm", {kBF, kBF, kF32}, {kBF, kBF}, {}, rms_norm<true>, {1}},
   };
   return t;
 }
@@ -242,7 +264,11 @@ struct GgufOp : Ort::CustomOpBase<GgufOp, GgufKernel, true> {
       if (static_cast<size_t>(o) == i) return INPUT_OUTPUT_OPTIONAL;
     return INPUT_OUTPUT_REQUIRED;
   }
-  OrtCustomOpInputOutputCharacteristic GetOutputCharacteristic(size_t) const { return INPUT_OUTPUT_REQUIRED; }
+  OrtCustomOpInputOutputCharacteristic GetOutputCharacteristic(size_t i) const {
+    for (int o : d->optional_out)
+      if (static_cast<size_t>(o) == i) return INPUT_OUTPUT_OPTIONAL;
+    return INPUT_OUTPUT_REQUIRED;
+  }
   OrtStatus* CreateKernelV2(const OrtApi& api, const OrtKernelInfo* info, void** kernel) const noexcept {
     try {
       auto* k = new GgufKernel{d, {}};
@@ -250,6 +276,7 @@ struct GgufOp : Ort::CustomOpBase<GgufOp, GgufKernel, true> {
       k->a.iq2 = opt_int(info, "iq2", 0);
       k->a.topk = opt_int(info, "topk", 0);
       k->a.scale = opt_float(info, "scale", 1.0f);
+      k->a.epsilon = opt_float(info, "epsilon", 1e-5f);
       *kernel = k;
       return nullptr;
     } catch (const std::exception& e) {

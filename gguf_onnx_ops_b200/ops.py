@@ -7,6 +7,8 @@ C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
 
     Q8Gemv(x, w, scales=None, gguf=1)                  -> y        src/bolt_ops.cu:1592-1643, :2018-2027
     Q8Embed(w, input_ids)                              -> out      src/bolt_ops.cu:1645-1690, :2038-2044
+    RmsNorm(x, gamma, epsilon)                         -> y        src/bolt_ops.cu:1692-1864, :2045-2051
+    SkipRmsNorm(x, skip, gamma, epsilon)               -> y, sum   src/bolt_ops.cu:1692-1864, :2052-2061
     Q4Gemv(x, w, scales=None, iq2=3)                   -> y        src/bolt_ops.cu:1592-1643, :2028-2037
     Nvfp4Gemv(x, w, w_scale, gscale, gguf=1)           -> y        src/bolt_ops.cu:1411-1469, :2004-2016
     MoeRouteGGUF(x, gate_w, bias, topk, scale)         -> idx, weights, scores    src/bolt_ops.cu:512-546
@@ -136,6 +138,48 @@ def Q8Embed(w: torch.Tensor, input_ids: torch.Tensor) -> torch.Tensor:
     out = torch.empty(*input_ids.shape, K, dtype=torch.bfloat16, device=w.device)
     q8_0_embed_into(w, input_ids, out, vocab, row_bytes, input_ids.numel())
     return out
+
+
+# ------------------------------------------------------------------------------------------------
+# Norms
+# ------------------------------------------------------------------------------------------------
+def rms_norm_into(x, skip, gamma, y, sum_out, R: int, H: int, eps: float, stream=None) -> None:
+    check(load().gguf_rms_norm(_ptr(x), _ptr(skip), _ptr(gamma), _ptr(y), _ptr(sum_out), R, H, eps, _stream(stream)))
+
+
+def _norm_shapes(x, gamma, op):
+    _need(x, "x", torch.bfloat16, op)
+    _need(gamma, "gamma", torch.float32, op)
+    if x.dim() < 1:
+        raise ValueError(f"{op}: input must be at least 1D")
+    H = x.shape[-1]
+    if H <= 0 or H % 8 != 0:
+        raise ValueError(f"{op}: hidden size H must be a positive multiple of 8")
+    if gamma.numel() != H:
+        raise ValueError(f"{op}: gamma size mismatch")
+    return x.numel() // H, H
+
+
+def RmsNorm(x: torch.Tensor, gamma: torch.Tensor, epsilon: float = 1e-5) -> torch.Tensor:
+    """y = bf16(bf16(gamma) * x * rsqrt(mean(x^2) + eps)) over the last dim (src/bolt_ops.cu:1692-1864)."""
+    R, H = _norm_shapes(x, gamma, "RmsNorm")
+    y = torch.empty_like(x)
+    rms_norm_into(x, None, gamma, y, None, R, H, epsilon)
+    return y
+
+
+def SkipRmsNorm(x: torch.Tensor, skip: torch.Tensor, gamma: torch.Tensor, epsilon: float = 1e-5,
+                return_sum: bool = True):
+    """sum = bf16(x + skip); y = RmsNorm(sum).  Returns (y, sum), or (y,) when the optional second
+    output is not requested (src/bolt_ops.cu:1830-1856)."""
+    R, H = _norm_shapes(x, gamma, "SkipRmsNorm")
+    _need(skip, "skip", torch.bfloat16, "SkipRmsNorm")
+    if skip.numel() != x.numel():
+        raise ValueError("SkipRmsNorm: skip shape mismatch")
+    y = torch.empty_like(x)
+    s = torch.empty_like(x) if return_sum else None
+    rms_norm_into(x, skip, gamma, y, s, R, H, epsilon)
+    return (y, s) if return_sum else (y,)
 
 
 # ------------------------------------------------------------------------------------------------

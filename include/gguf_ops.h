@@ -81,6 +81,17 @@ GGUF_OPS_API int gguf_q8_0_embed(const void* w, const int64_t* ids, void* out, i
                                  int64_t R, void* stream);
 
 /*
+ * RmsNorm / SkipRmsNorm:  v = x, or v = bf16(x + skip) when skip != NULL (then also stored to sum
+ * when sum != NULL);  y = bf16(bf16(gamma) * v * rsqrt(mean(v^2) + eps)).
+ * x, skip, y, sum: bf16 [R, H]; gamma: fp32 [H]; H a positive multiple of 8; 16-byte aligned
+ * tensors.  R = 0 is a no-op.  Replaces RmsNormState<HAS_SKIP>::ComputeV2 (src/bolt_ops.cu:1817-1863)
+ * and its kernels (:1695-1815); the mean of squares is summed in a fixed fp32 order of 512 partial
+ * sums that the fused GEMV prologues reproduce.
+ */
+GGUF_OPS_API int gguf_rms_norm(const void* x, const void* skip, const float* gamma, void* y, void* sum, int64_t R,
+                               int64_t H, float eps, void* stream);
+
+/*
  * MoeRouteGGUF:  scores[R,E] = sigmoid(x[R,K] @ bf16(gate_w)^T);  idx[R,topk] = top-k of scores + bias
  * (descending, ties to the lower expert index);  weights = s_sel / (sum s_sel + 1e-20) * scale.
  * x bf16 [R,K]; gate_w f32 [E,K]; bias f32 [E] -> idx i32 [R,topk], weights f32 [R,topk], scores f32 [R,E].

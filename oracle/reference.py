@@ -9,6 +9,8 @@
   ``s / (sum s + 1e-20) * scale`` (``src/bolt_ops.cu:505-508``); logits in fp64.
 * ``embed_ref`` -- Q8Embed: rows ``ids`` of a Q8_0 table dequantised and rounded to bf16, ids
   outside [0, vocab) reading row 0 (``src/bolt_ops.cu:1645-1660``, ``:1674-1687``).
+* ``rms_norm_ref`` -- RmsNorm / SkipRmsNorm: v = x or bf16(x + skip), y = bf16(bf16(gamma) * v *
+  rsqrt(mean(v^2) + eps)) (``src/bolt_ops.cu:1692-1815``); mean in fp64, products in fp32.
 * ``rel_l2``    -- the reference's metric ``||a-b|| / ||b||`` (``tests/test_bolt_ops.py:62-64``).
 """
 
@@ -76,6 +78,19 @@ def embed_ref(w_raw: np.ndarray, ids) -> np.ndarray:
     K = w_raw.shape[1] // 34 * 32
     deq = dequant_q8_0(w_raw[rows]) if rows.size else np.zeros((0, K), np.float32)
     return bf16_round(deq.astype(np.float32)).reshape(*ids.shape, K)
+
+
+def rms_norm_ref(x, gamma: np.ndarray, eps: float, skip=None):
+    """x, skip: [R, H] bf16 bits (uint16); gamma: fp32 [H].  Returns (y fp32 [R, H] holding bf16
+    values, v fp32 [R, H] holding the bf16 values normalised: x, or bf16(x + skip))."""
+    v = _x_f32(x)
+    if skip is not None:
+        v = bf16_round(v + _x_f32(skip))  # fp32 add + bf16 rounding = bf16 rounding of the exact sum
+    ms = (v.astype(np.float64) ** 2).mean(axis=-1, keepdims=True)
+    rs = (1.0 / np.sqrt(ms + np.float64(eps))).astype(np.float32)
+    g = bf16_round(np.asarray(gamma, dtype=np.float32))
+    y = bf16_round((g * v).astype(np.float32) * rs)
+    return y, v
 
 
 def route_ref(x, gate_w: np.ndarray, bias: np.ndarray, topk: int, scale: float, tie_eps: float = 1e-6):

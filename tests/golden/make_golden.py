@@ -12,6 +12,7 @@ Every expected value here comes from the reference's own CPU path, not from the 
   weights, as MoeRouteGGUF specifies (src/bolt_ops.cu:441-448);
 * Q8Embed output: the harness's torch expression (tests/test_bolt_ops.py:310-311) with ids outside
   [0, vocab) replaced by row 0, the op's rule (src/bolt_ops.cu:1680);
+* RmsNorm / SkipRmsNorm outputs: the harness's torch expressions (tests/test_bolt_ops.py:321-337);
 * the IQ2_XXS codebook: parsed from the reference's src/iq2xxs_grid.h (kIq2xxsGrid, line 6, and
   kIq2xxsGridBf16, line 75).
 
@@ -37,7 +38,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from oracle import inputs as I  # noqa: E402  (input builders only; expected values come from gguf/torch)
-from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, route_inputs, sha  # noqa: E402
+from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, norm_inputs, route_inputs, sha  # noqa: E402
 
 
 def gguf_deq(raw: np.ndarray, qt) -> np.ndarray:
@@ -74,13 +75,28 @@ def make_embed():
                         sha=np.array(sha(blk, ids)))
 
 
+def make_norm():
+    cases = {}
+    for name in ("h4096", "h2048"):
+        x, skip, gamma, eps = norm_inputs(name)
+        xt, st, gt = bf16_tensor(x), bf16_tensor(skip), torch.from_numpy(gamma)
+        rn = (xt.float() * torch.rsqrt(xt.float().pow(2).mean(-1, keepdim=True) + eps) * gt.bfloat16().float()).bfloat16()
+        s = xt + st
+        srn = (s.float() * torch.rsqrt(s.float().pow(2).mean(-1, keepdim=True) + eps) * gt.bfloat16().float()).bfloat16()
+        cases.update({f"{name}_rms": rn.view(torch.int16).numpy().view(np.uint16),
+                      f"{name}_skip_rms": srn.view(torch.int16).numpy().view(np.uint16),
+                      f"{name}_sum": s.view(torch.int16).numpy().view(np.uint16),
+                      f"{name}_sha": np.array(sha(x, skip, gamma))})
+    np.savez_compressed(os.path.join(HERE, "norm.npz"), **cases)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["embed"], default=None)
+    ap.add_argument("--only", choices=["embed", "norm"], default=None)
     args = ap.parse_args()
-    if args.only == "embed":
-        make_embed()
+    if args.only:
+        {"embed": make_embed, "norm": make_norm}[args.only]()
         return
     from gguf import GGMLQuantizationType as Q
 
@@ -147,6 +163,7 @@ def main():
             ref[t] += float(wts[t, j]) * (h @ d2[e].T).bfloat16().float()
     np.savez_compressed(os.path.join(HERE, "moe.npz"), out=ref.numpy(), sha=np.array(sha(z, idx, wts, b1, b2)))
     make_embed()
+    make_norm()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -7,7 +7,7 @@ import torch
 
 import oracle as O
 from oracle import inputs as I
-from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, route_inputs, sha
+from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, norm_inputs, route_inputs, sha
 from tests.util import rel
 
 
@@ -126,6 +126,31 @@ def test_embed_ref_empty_ids():
     blk, _ = embed_inputs()
     assert O.embed_ref(blk, np.zeros((0,), np.int64)).shape == (0, 1024)
     assert O.embed_ref(blk, np.zeros((3, 0), np.int64)).shape == (3, 0, 1024)
+
+
+def bf16_ulps(a_bits, b_bits) -> np.ndarray:
+    """Distance in bf16 ulps between two arrays of bf16 bit patterns (same-sign values)."""
+    a = np.asarray(a_bits, np.uint16).astype(np.int32)
+    b = np.asarray(b_bits, np.uint16).astype(np.int32)
+    oa = np.where(a & 0x8000, 0x8000 - a, a)
+    ob = np.where(b & 0x8000, 0x8000 - b, b)
+    return np.abs(oa - ob)
+
+
+@pytest.mark.parametrize("name", ["h4096", "h2048"])
+def test_rms_norm_ref_matches_golden(golden, name):
+    d = golden("norm.npz")
+    x, skip, gamma, eps = norm_inputs(name)
+    assert sha(x, skip, gamma) == str(d[f"{name}_sha"]), "input builder drifted"
+    y, v = O.rms_norm_ref(x, gamma, eps)
+    assert np.array_equal(O.bf16_bits(v), x)
+    ys, s = O.rms_norm_ref(x, gamma, eps, skip=skip)
+    assert np.array_equal(O.bf16_bits(s), d[f"{name}_sum"])  # bf16 add: exact
+    for got, key in ((y, "rms"), (ys, "skip_rms")):
+        # fp64 mean vs the harness's fp32 torch mean: at most one bf16 ulp apart, rarely
+        u = bf16_ulps(O.bf16_bits(got), d[f"{name}_{key}"])
+        assert u.max() <= 1 and u.mean() < 0.01
+        assert rel(got, O.bf16_to_f32(d[f"{name}_{key}"])) < 1e-3
 
 
 def test_bf16_round_matches_torch():
