@@ -34,6 +34,8 @@ SIGNATURES = {
     "gguf_q8_0_embed": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_rms_norm": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _F32, _P]),
     "gguf_moe_route": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),
+    "gguf_moe_route_bf16": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),
+    "gguf_relu2": (_I32, [_P, _P, _I64, _P]),
     "gguf_moe_verify_iq2_xxs": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "gguf_moe_verify_iq2_xxs_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "gguf_gemv_rowsplit": (_I32, [_I32, _P, _P, _P, _P, _I64, _I64, _I64, _P]),

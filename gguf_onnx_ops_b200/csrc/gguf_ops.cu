@@ -427,19 +427,56 @@ int gguf_nvfp4_gemv(const void* x, const void* w, const float* gscale, void* y, 
                 : run_dense<kFmtFP4, 2>(x, w, gscale, y, (int)R, (int)N, (int)K, s);
 }
 
-int gguf_moe_route(const void* x, const float* gate_w, const float* bias, int32_t* idx, float* weights, float* scores,
-                   int64_t R, int64_t K, int64_t E, int64_t topk, float scale, void* stream) {
+extern "C++" {
+namespace gguf_b200 {
+namespace {
+template <typename WT>
+int run_route(const char* op, const void* x, const WT* gate_w, const float* bias, int32_t* idx, float* weights,
+              float* scores, int64_t R, int64_t K, int64_t E, int64_t topk, float scale, void* stream) {
   t_last_error.clear();
   if (!x || !gate_w || !bias || !idx || !weights || !scores)
-    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeRouteGGUF: null tensor pointer");
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": null tensor pointer");
   if (E < 1 || E > 512 || K <= 0 || K % 256 != 0 || topk < 1 || topk > 32 || topk > E || R < 1 || R > (1 << 24))
     return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeRoute: unsupported shape (needs E <= 512, K % 256 == 0, 1 <= topk <= min(32, E))");
-  if (!aligned(x, 16) || !aligned(gate_w, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeRouteGGUF: x and gate_w must be 16-byte aligned");
+  if (!aligned(x, 16) || !aligned(gate_w, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": x and gate_w must be 16-byte aligned");
   const int clusters = static_cast<int>((R + kRouteRows - 1) / kRouteRows);
-  cudaError_t e = launch(route_kernel, dim3(clusters * kRouteCtas), dim3(kRouteWarps * 32), 0, static_cast<cudaStream_t>(stream),
-                         static_cast<const bf16*>(x), gate_w, bias, (int)R, (int)K, (int)E, (int)topk, scale, idx, weights,
-                         scores);
-  if (e != cudaSuccess) return cuda_fail("MoeRouteGGUF launch", e);
+  cudaError_t e = launch(route_kernel<WT>, dim3(clusters * kRouteCtas), dim3(kRouteWarps * 32), 0,
+                         static_cast<cudaStream_t>(stream), static_cast<const bf16*>(x), gate_w, bias, (int)R, (int)K,
+                         (int)E, (int)topk, scale, idx, weights, scores);
+  if (e != cudaSuccess) return cuda_fail((std::string(op) + " launch").c_str(), e);
+  return GGUF_OK;
+}
+}  // namespace
+}  // namespace gguf_b200
+}  // extern "C++"
+
+int gguf_moe_route(const void* x, const float* gate_w, const float* bias, int32_t* idx, float* weights, float* scores,
+                   int64_t R, int64_t K, int64_t E, int64_t topk, float scale, void* stream) {
+  return run_route<float>("MoeRouteGGUF", x, gate_w, bias, idx, weights, scores, R, K, E, topk, scale, stream);
+}
+
+int gguf_moe_route_bf16(const void* x, const void* gate_w, const float* bias, int32_t* idx, float* weights,
+                        float* scores, int64_t R, int64_t K, int64_t E, int64_t topk, float scale, void* stream) {
+  return run_route<bf16>("MoeRoute", x, static_cast<const bf16*>(gate_w), bias, idx, weights, scores, R, K, E, topk,
+                         scale, stream);
+}
+
+int gguf_relu2(const void* x, void* y, int64_t n, void* stream) {
+  t_last_error.clear();
+  if (n < 0) return fail(GGUF_ERR_INVALID_ARGUMENT, "Relu2: negative element count");
+  if (n == 0) return GGUF_OK;
+  if (!x || !y) return fail(GGUF_ERR_INVALID_ARGUMENT, "Relu2: null tensor pointer");
+  if (!aligned(x, 2) || !aligned(y, 2)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Relu2: tensors must be 2-byte aligned");
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  const bool vec = aligned(x, 16) && aligned(y, 16);
+  const int64_t items = vec ? (n + 7) / 8 : n;
+  const int64_t ctas = std::min<int64_t>((items + 255) / 256, static_cast<int64_t>(sms) * 8);
+  const cudaError_t e = launch(vec ? relu2_kernel<true> : relu2_kernel<false>, dim3(static_cast<unsigned>(ctas)),
+                               dim3(256), 0, static_cast<cudaStream_t>(stream), static_cast<const bf16*>(x),
+                               static_cast<bf16*>(y), n);
+  if (e != cudaSuccess) return cuda_fail("Relu2 launch", e);
   return GGUF_OK;
 }
 

@@ -147,6 +147,28 @@ void route_gguf(Ort::KernelContext& c, const Attrs& a) {
                        sc.GetTensorMutableData<float>(), R, K, E, a.topk, a.scale, stream(c)));
 }
 
+void route_bf16(Ort::KernelContext& c, const Attrs& a) {
+  auto x = c.GetInput(0);
+  auto gw = c.GetInput(1);
+  auto xs = shape(x), gs = shape(gw);
+  if (xs.size() != 2 || gs.size() != 2) throw std::invalid_argument("MoeRoute: unsupported shape");
+  const int64_t R = xs[0], K = xs[1], E = gs[0];
+  if (E > 512 || K % 256 != 0 || a.topk > 32 || gs[1] != K || count(c.GetInput(2)) != E)
+    throw std::invalid_argument("MoeRoute: unsupported shape");
+  auto idx = c.GetOutput(0, {R, a.topk});
+  auto wt = c.GetOutput(1, {R, a.topk});
+  auto sc = c.GetOutput(2, {R, E});
+  check(gguf_moe_route_bf16(x.GetTensorRawData(), gw.GetTensorRawData(), c.GetInput(2).GetTensorData<float>(),
+                            idx.GetTensorMutableData<int32_t>(), wt.GetTensorMutableData<float>(),
+                            sc.GetTensorMutableData<float>(), R, K, E, a.topk, a.scale, stream(c)));
+}
+
+void relu2(Ort::KernelContext& c, const Attrs&) {
+  auto x = c.GetInput(0);
+  auto y = c.GetOutput(0, shape(x));
+  check(gguf_relu2(x.GetTensorRawData(), y.GetTensorMutableRawData(), count(x), stream(c)));
+}
+
 void moe_verify(Ort::KernelContext& c, const Attrs& a) {
   if (a.iq2 != 3) throw NotImplemented("MoeVerify: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented");
   auto z = c.GetInput(0);
@@ -216,11 +238,11 @@ const std::vector<OpDesc>& op_table() {
       {"MambaVerify", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {}, nullptr},
       {"MambaVerifyGGUF", {kBF, kBF, kF32, kF32, kF32, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {},
        nullptr},
-      {"MoeRoute", {kBF, kBF, kF32}, {kI32, kF32, kF32}, {}, nullptr},
+      {"MoeRoute", {kBF, kBF, kF32}, {kI32, kF32, kF32}, {}, route_bf16},
       {"MoeRouteGGUF", {kBF, kF32, kF32}, {kI32, kF32, kF32}, {}, route_gguf},
       {"MoeDecode", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32}, {}, nullptr},
       {"MoeVerify", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32, kI32}, {4, 6}, moe_verify},
-      {"Relu2", {kBF}, {kBF}, {}, nullptr},
+      {"Relu2", {kBF}, {kBF}, {}, relu2},
       {"Nvfp4Gemv", {kBF, kU8, kU8, kF32}, {kBF}, {2}, fp4_gemv},
       {"Q8Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q8_gemv},
       {"Q4Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q4_gemv},

@@ -84,8 +84,38 @@ __device__ __forceinline__ void route_select(const float* __restrict__ sr, int r
   }
 }
 
+// 8 consecutive gate weights of one lane: fp32 (MoeRouteGGUF, rounded to bf16 on use) or bf16
+// (MoeRoute).  Both give the same bf16 values to the dot product, so the two ops agree exactly.
+template <typename WT>
+struct GateChunk;
+template <>
+struct GateChunk<float> {
+  float4 a, b;
+  __device__ __forceinline__ static GateChunk load(const float* row, int k) {
+    return {__ldg(reinterpret_cast<const float4*>(row + k)), __ldg(reinterpret_cast<const float4*>(row + k + 4))};
+  }
+  __device__ __forceinline__ static GateChunk zero() {
+    return {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  }
+  __device__ __forceinline__ void to8(float (&wb)[8]) const {
+    wb[0] = round_bf16(a.x); wb[1] = round_bf16(a.y); wb[2] = round_bf16(a.z); wb[3] = round_bf16(a.w);
+    wb[4] = round_bf16(b.x); wb[5] = round_bf16(b.y); wb[6] = round_bf16(b.z); wb[7] = round_bf16(b.w);
+  }
+};
+template <>
+struct GateChunk<bf16> {
+  uint4 a;
+  __device__ __forceinline__ static GateChunk load(const bf16* row, int k) { return {ldg128(row + k)}; }
+  __device__ __forceinline__ static GateChunk zero() { return {make_uint4(0u, 0u, 0u, 0u)}; }
+  __device__ __forceinline__ void to8(float (&wb)[8]) const {
+    wb[0] = bf16_lo(a.x); wb[1] = bf16_hi(a.x); wb[2] = bf16_lo(a.y); wb[3] = bf16_hi(a.y);
+    wb[4] = bf16_lo(a.z); wb[5] = bf16_hi(a.z); wb[6] = bf16_lo(a.w); wb[7] = bf16_hi(a.w);
+  }
+};
+
+template <typename WT>
 __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps * 32)
-    route_kernel(const bf16* __restrict__ x, const float* __restrict__ gw, const float* __restrict__ bias, int R, int K,
+    route_kernel(const bf16* __restrict__ x, const WT* __restrict__ gw, const float* __restrict__ bias, int R, int K,
                  int E, int topk, float scale, int32_t* __restrict__ idx_out, float* __restrict__ w_out,
                  float* __restrict__ scores) {
   const int cluster = blockIdx.x / kRouteCtas, rank = blockIdx.x % kRouteCtas;
@@ -96,29 +126,24 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
   const int e_first = e_lo + warp;
   // The gate weights do not depend on the previous kernel: this warp's first row (up to
   // kRoutePre * 256 elements) is in flight before the dependency wait.
-  float4 pw[2 * kRoutePre];
+  GateChunk<WT> pw[kRoutePre];
 #pragma unroll
   for (int c = 0; c < kRoutePre; ++c) {
     const int k = c * 256 + lane * 8;
-    if (e_first < e_hi && k < K) {
-      const float* wr = gw + static_cast<int64_t>(e_first) * K + k;
-      pw[2 * c] = __ldg(reinterpret_cast<const float4*>(wr));
-      pw[2 * c + 1] = __ldg(reinterpret_cast<const float4*>(wr + 4));
-    } else {
-      pw[2 * c] = pw[2 * c + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    pw[c] = (e_first < e_hi && k < K) ? GateChunk<WT>::load(gw + static_cast<int64_t>(e_first) * K, k)
+                                      : GateChunk<WT>::zero();
   }
   pdl_wait();
   pdl_launch_dependents();
   for (int e = e_first; e < e_hi; e += kRouteWarps) {
-    const float* wr = gw + static_cast<int64_t>(e) * K;
+    const WT* wr = gw + static_cast<int64_t>(e) * K;
     float acc[kRouteRows];
 #pragma unroll
     for (int r = 0; r < kRouteRows; ++r) acc[r] = 0.f;
     // one 8-element chunk at k (this lane's elements k..k+7), accumulated in increasing k
-    auto chunk = [&](const float4 w0, const float4 w1, int k) {
-      const float wb[8] = {round_bf16(w0.x), round_bf16(w0.y), round_bf16(w0.z), round_bf16(w0.w),
-                           round_bf16(w1.x), round_bf16(w1.y), round_bf16(w1.z), round_bf16(w1.w)};
+    auto chunk = [&](const GateChunk<WT> gc, int k) {
+      float wb[8];
+      gc.to8(wb);
 #pragma unroll
       for (int r = 0; r < kRouteRows; ++r) {
         if (r < nrows) {
@@ -137,11 +162,7 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
       // rows outer, chunks inner: acc[r] still accumulates in increasing k
       float wb[kRoutePre][8];
 #pragma unroll
-      for (int c = 0; c < kRoutePre; ++c) {
-        const float4 w0 = pw[2 * c], w1 = pw[2 * c + 1];
-        wb[c][0] = round_bf16(w0.x); wb[c][1] = round_bf16(w0.y); wb[c][2] = round_bf16(w0.z); wb[c][3] = round_bf16(w0.w);
-        wb[c][4] = round_bf16(w1.x); wb[c][5] = round_bf16(w1.y); wb[c][6] = round_bf16(w1.z); wb[c][7] = round_bf16(w1.w);
-      }
+      for (int c = 0; c < kRoutePre; ++c) pw[c].to8(wb[c]);
 #pragma unroll
       for (int r = 0; r < kRouteRows; ++r) {
         if (r >= nrows) break;
@@ -164,8 +185,7 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
       k0 += kRoutePre * 256;
     }
 #pragma unroll 2
-    for (int k = k0; k < K; k += 256)
-      chunk(__ldg(reinterpret_cast<const float4*>(wr + k)), __ldg(reinterpret_cast<const float4*>(wr + k + 4)), k);
+    for (int k = k0; k < K; k += 256) chunk(GateChunk<WT>::load(wr, k), k);
 #pragma unroll
     for (int r = 0; r < kRouteRows; ++r) {
       float v = acc[r];
@@ -442,6 +462,38 @@ __global__ void __launch_bounds__(kEmbedWarps * 32) q8_embed_vec_kernel(const ui
       *reinterpret_cast<uint4*>(out + (u0 + i) * 256 + lane * 8) = o;
     }
     __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Relu2 (src/bolt_ops.cu:700-726): y = bf16(r * r), r = fmaxf(x, 0) in fp32 (NaN -> 0 through fmaxf).
+// kVec: 8 elements per thread with 16-byte loads / stores (aligned tensors), tail elementwise.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float relu2_f(float v) {
+  const float r = fmaxf(v, 0.f);
+  return __fmul_rn(r, r);
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(256) relu2_kernel(const bf16* __restrict__ x, bf16* __restrict__ y, int64_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if constexpr (kVec) {
+    const int64_t n8 = n / 8;
+    for (int64_t i = t0; i < n8; i += stride) {
+      const uint4 v = ldg128(x + 8 * i);
+      uint4 o;
+      o.x = pack_bf16x2(relu2_f(bf16_lo(v.x)), relu2_f(bf16_hi(v.x)));
+      o.y = pack_bf16x2(relu2_f(bf16_lo(v.y)), relu2_f(bf16_hi(v.y)));
+      o.z = pack_bf16x2(relu2_f(bf16_lo(v.z)), relu2_f(bf16_hi(v.z)));
+      o.w = pack_bf16x2(relu2_f(bf16_lo(v.w)), relu2_f(bf16_hi(v.w)));
+      *reinterpret_cast<uint4*>(y + 8 * i) = o;
+    }
+    for (int64_t i = 8 * n8 + t0; i < n; i += stride) y[i] = __float2bfloat16(relu2_f(__bfloat162float(x[i])));
+  } else {
+    for (int64_t i = t0; i < n; i += stride) y[i] = __float2bfloat16(relu2_f(__bfloat162float(x[i])));
   }
 }
 

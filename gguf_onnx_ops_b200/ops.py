@@ -6,12 +6,14 @@ the outputs with the reference's shapes (as ``KernelContext::GetOutput`` would) 
 C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
 
     Q8Gemv(x, w, scales=None, gguf=1)                  -> y        src/bolt_ops.cu:1592-1643, :2018-2027
+    Q4Gemv(x, w, scales=None, iq2=3)                   -> y        src/bolt_ops.cu:1592-1643, :2028-2037
+    Nvfp4Gemv(x, w, w_scale, gscale, gguf=1)           -> y        src/bolt_ops.cu:1411-1469, :2004-2016
     Q8Embed(w, input_ids)                              -> out      src/bolt_ops.cu:1645-1690, :2038-2044
     RmsNorm(x, gamma, epsilon)                         -> y        src/bolt_ops.cu:1692-1864, :2045-2051
     SkipRmsNorm(x, skip, gamma, epsilon)               -> y, sum   src/bolt_ops.cu:1692-1864, :2052-2061
-    Q4Gemv(x, w, scales=None, iq2=3)                   -> y        src/bolt_ops.cu:1592-1643, :2028-2037
-    Nvfp4Gemv(x, w, w_scale, gscale, gguf=1)           -> y        src/bolt_ops.cu:1411-1469, :2004-2016
+    Relu2(x)                                           -> y        src/bolt_ops.cu:700-726, :1997-2003
     MoeRouteGGUF(x, gate_w, bias, topk, scale)         -> idx, weights, scores    src/bolt_ops.cu:512-546
+    MoeRoute(x, gate_w_bf16, bias, topk, scale)        -> idx, weights, scores    src/bolt_ops.cu:513-547, :1947
     MoeVerify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s=None, topk, iq2=3) -> out, h, part, meta
                                                                    src/bolt_ops.cu:1327-1409, :1981-1996
 
@@ -204,6 +206,39 @@ def MoeRouteGGUF(x: torch.Tensor, gate_w: torch.Tensor, bias: torch.Tensor, topk
     scores = torch.empty(R, E, dtype=torch.float32, device=x.device)
     moe_route_into(x, gate_w, bias, idx, wts, scores, R, K, E, topk, scale)
     return idx, wts, scores
+
+
+def moe_route_bf16_into(x, gate_w, bias, idx, wts, scores, R, K, E, topk, scale, stream=None) -> None:
+    check(load().gguf_moe_route_bf16(_ptr(x), _ptr(gate_w), _ptr(bias), _ptr(idx), _ptr(wts), _ptr(scores), R, K, E,
+                                     topk, scale, _stream(stream)))
+
+
+def MoeRoute(x: torch.Tensor, gate_w: torch.Tensor, bias: torch.Tensor, topk: int, scale: float):
+    """MoeRouteGGUF with bf16 gate weights (src/bolt_ops.cu:513-547, :1947-1956)."""
+    _need(x, "x", torch.bfloat16, "MoeRoute")
+    _need(gate_w, "gate_w", torch.bfloat16, "MoeRoute")
+    _need(bias, "bias", torch.float32, "MoeRoute")
+    R, K = x.shape
+    E = gate_w.shape[0]
+    if E > 512 or K % 256 != 0 or topk > 32 or gate_w.shape[1] != K or bias.numel() != E:
+        raise ValueError("MoeRoute: unsupported shape")
+    idx = torch.empty(R, topk, dtype=torch.int32, device=x.device)
+    wts = torch.empty(R, topk, dtype=torch.float32, device=x.device)
+    scores = torch.empty(R, E, dtype=torch.float32, device=x.device)
+    moe_route_bf16_into(x, gate_w, bias, idx, wts, scores, R, K, E, topk, scale)
+    return idx, wts, scores
+
+
+def relu2_into(x, y, n: int, stream=None) -> None:
+    check(load().gguf_relu2(_ptr(x), _ptr(y), n, _stream(stream)))
+
+
+def Relu2(x: torch.Tensor) -> torch.Tensor:
+    """y = bf16(max(x, 0)^2) elementwise (src/bolt_ops.cu:700-726)."""
+    _need(x, "x", torch.bfloat16, "Relu2")
+    y = torch.empty_like(x)
+    relu2_into(x, y, x.numel())
+    return y
 
 
 def moe_verify_into(z, idx, w, fc1_w, fc2_w, out, h, part, meta, R, E, I, topk, stream=None) -> None:

@@ -103,6 +103,19 @@ GGUF_OPS_API int gguf_moe_route(const void* x, const float* gate_w, const float*
                                 void* stream);
 
 /*
+ * MoeRoute: MoeRouteGGUF with bf16 gate weights [E, K] (src/bolt_ops.cu:513-547, :1947-1956); the
+ * same kernel, so for gate weights that are bf16 values both ops return identical outputs.
+ */
+GGUF_OPS_API int gguf_moe_route_bf16(const void* x, const void* gate_w, const float* bias, int32_t* idx,
+                                     float* weights, float* scores, int64_t R, int64_t K, int64_t E, int64_t topk,
+                                     float scale, void* stream);
+
+/*
+ * Relu2: y = bf16(max(x, 0)^2) elementwise over n bf16 values (src/bolt_ops.cu:700-726, :1997-2003).
+ */
+GGUF_OPS_API int gguf_relu2(const void* x, void* y, int64_t n, void* stream);
+
+/*
  * MoeVerify, iq2=3 (expert-grouped relu^2 MoE over raw IQ2_XXS expert tensors):
  *   for each pair p = (t, j), e = idx[t,j]:  h[p] = bf16(relu(bf16(z[t] . W1[e]^T))^2)
  *                                            part[p] = bf16(h[p] . W2[e]^T)   (stored as f32)
