@@ -23,6 +23,9 @@ GGUF_TYPE_Q8_0 = 8
 GGUF_TYPE_IQ2_XXS = 16
 GGUF_TYPE_NVFP4 = 40
 
+# legacy split layouts (include/gguf_ops.h GGUF_LAYOUT_*)
+GGUF_LAYOUT_Q8_SPLIT, GGUF_LAYOUT_Q4_SPLIT, GGUF_LAYOUT_IQ2_CODES, GGUF_LAYOUT_IQ2_NATIVE, GGUF_LAYOUT_NVFP4_SPLIT = range(5)
+
 # name -> (restype, argtypes); mirrors include/gguf_ops.h
 _P, _I64, _I32, _F32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
 SIGNATURES = {
@@ -31,6 +34,7 @@ SIGNATURES = {
     "gguf_q8_0_gemv": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_iq2_xxs_gemv": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_nvfp4_gemv": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "gguf_gemv_legacy": (_I32, [_I32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_q8_0_embed": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_rms_norm": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _F32, _P]),
     "gguf_moe_route": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),

@@ -26,22 +26,54 @@
 namespace gguf_b200 {
 
 constexpr int kFmtQ8 = 0, kFmtIQ2 = 1, kFmtFP4 = 2;
+// Split (pre-GGUF) layouts of the reference's legacy attribute values: weight bytes and scales in
+// two tensors (src/bolt_ops.cu:840-848, tests/test_bolt_ops.py:70-100, 159-181, 210-240).
+//   kFmtQ8S  : Q8Gemv gguf=0       u8 [N, K] = q + 128,             bf16 scale [N, K/32]
+//   kFmtQ4S  : Q4Gemv iq2=0        u8 [N, K/2] nibbles (n - 8),     bf16 scale [N, K/32]
+//   kFmtIQ2C : Q4Gemv iq2=1        u8 [N, K/2] 3-bit codes,         bf16 scale [N, K/32]
+//   kFmtIQ2N : Q4Gemv iq2=2        u8 [N, K/32, 8] IQ2_XXS records, fp16 d bits [N, K/256]
+//   kFmtFP4S : Nvfp4Gemv gguf=0    u8 [N, K/2] E2M1 nibbles,        e4m3fn scale [N, K/16]
+// Byte i of a nibble-packed group holds element 2i in its low and 2i+1 in its high nibble.
+constexpr int kFmtQ8S = 3, kFmtQ4S = 4, kFmtIQ2C = 5, kFmtIQ2N = 6, kFmtFP4S = 7;
 
 template <int F>
 struct FmtInfo;
-// kSeg = smallest K granule whose byte size is a multiple of 16 (segmented bulk copies).
+// kSeg = smallest K granule whose byte size (and, for split layouts, whose scale bytes) is a
+// multiple of 16 (segmented bulk copies).  kScDiv: weight elements per scale byte (0: the scales
+// are inside the GGUF blocks).
 template <>
 struct FmtInfo<kFmtQ8> {
-  static constexpr int kBlock = 32, kBytes = 34, kSeg = 256;
+  static constexpr int kBlock = 32, kBytes = 34, kSeg = 256, kScDiv = 0;
 };
 template <>
 struct FmtInfo<kFmtIQ2> {
-  static constexpr int kBlock = 256, kBytes = 66, kSeg = 2048;
+  static constexpr int kBlock = 256, kBytes = 66, kSeg = 2048, kScDiv = 0;
 };
 template <>
 struct FmtInfo<kFmtFP4> {
-  static constexpr int kBlock = 64, kBytes = 36, kSeg = 256;
+  static constexpr int kBlock = 64, kBytes = 36, kSeg = 256, kScDiv = 0;
 };
+template <>
+struct FmtInfo<kFmtQ8S> {
+  static constexpr int kBlock = 32, kBytes = 32, kSeg = 256, kScDiv = 16;
+};
+template <>
+struct FmtInfo<kFmtQ4S> {
+  static constexpr int kBlock = 32, kBytes = 16, kSeg = 256, kScDiv = 16;
+};
+template <>
+struct FmtInfo<kFmtIQ2C> {
+  static constexpr int kBlock = 32, kBytes = 16, kSeg = 256, kScDiv = 16;
+};
+template <>
+struct FmtInfo<kFmtIQ2N> {
+  static constexpr int kBlock = 32, kBytes = 8, kSeg = 2048, kScDiv = 128;
+};
+template <>
+struct FmtInfo<kFmtFP4S> {
+  static constexpr int kBlock = 32, kBytes = 16, kSeg = 256, kScDiv = 16;
+};
+constexpr bool is_split(int F) { return F >= kFmtQ8S; }
 
 // ---------------------------------------------------------------------------------------------
 // Unaligned (2-byte aligned) reads from a 4-byte aligned base (shared or global).
@@ -147,6 +179,53 @@ __device__ __forceinline__ void fp4_patterns(uint32_t v, uint32_t& lo, uint32_t&
 __device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
   __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Split layouts: lane t of a k-group owns elements 8t..8t+7 (nibble formats: bytes 4t..4t+3 of the
+// group; Q8S: elements 4t..4t+3 and 16+4t..19+4t as Q8_0).  Each helper returns the 4 A words
+// (bf16x2, exact) of one row for the two m16n8k16 steps: (w[0], w[1]) step 0, (w[2], w[3]) step 1.
+// ---------------------------------------------------------------------------------------------
+// Q4S: nibble n -> bf16(128 + n) = 0x4300 | n exactly; minus 136 gives n - 8 (exact).
+__device__ __forceinline__ void q4s_words(uint32_t v, uint32_t (&w)[4]) {
+  const __nv_bfloat162 zp = __floats2bfloat162_rn(136.f, 136.f);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t x = (v >> (8 * p)) & 0xFFu;
+    uint32_t u = 0x43004300u | (x & 0xFu) | ((x & 0xF0u) << 12);
+    __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&u), zp);
+    w[p] = *reinterpret_cast<uint32_t*>(&r);
+  }
+}
+// IQ2C: code c (low 3 bits; bit 3 ignored) -> {8, 25, 43, 0} by c & 3, negative when c & 4.
+// bf16 patterns of the magnitudes in two words: bytes 0-1 = 8, 2-3 = 25, 4-5 = 43, 6-7 = 0.
+__device__ __forceinline__ void iq2c_words(uint32_t v, uint32_t (&w)[4]) {
+  constexpr uint32_t kP0 = 0x41C84100u, kP1 = 0x0000422Cu;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t x = (v >> (8 * p)) & 0xFFu;
+    const uint32_t m0 = x & 3u, m1 = (x >> 4) & 3u;
+    const uint32_t sel = (m0 * 0x22u + 0x10u) | ((m1 * 0x22u + 0x10u) << 8);
+    w[p] = __byte_perm(kP0, kP1, sel) | ((x & 0x04u) << 13) | ((x & 0x40u) << 25);
+  }
+}
+// FP4S: nibble -> bf16 pattern of E2M1 * 2^-126 (as fp4_patterns), pairs (low, high) of each byte.
+__device__ __forceinline__ void fp4s_words(uint32_t v, uint32_t (&w)[4]) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t x = (v >> (8 * p)) & 0xFFu;
+    w[p] = ((x & 0x07u) << 6) | ((x & 0x08u) << 12) | ((x & 0x70u) << 18) | ((x & 0x80u) << 24);
+  }
+}
+// e4m3fn byte (torch.float8_e4m3fn: signed, 0x7F / 0xFF NaN, subnormal for e == 0) -> bf16 bits of
+// value * 2^110 (exact: 4 significant bits, exponent within bf16's normal range).
+__device__ __forceinline__ uint32_t e4m3fn_bf16_bits_x2p110(uint32_t b) {
+  const uint32_t sign = (b & 0x80u) << 8;
+  if ((b & 0x7Fu) == 0x7Fu) return sign | 0x7FC0u;
+  const uint32_t e = (b >> 3) & 15u, m = b & 7u;
+  if (e != 0u) return sign | ((e + 230u) << 7) | (m << 4);
+  if (m == 0u) return sign;
+  return sign | (__float_as_uint(static_cast<float>(m) * 0x1p101f) >> 16);
 }
 
 // IQ2_XXS codebook (bf16x2) replicated 8x into shared memory: entry e, copy c at e*128 + c*16, so

@@ -63,6 +63,11 @@ struct EngineArgs {
   int topk, P, E;
   int32_t* meta;       // moe1: written by CTA 0
   PeerOut po;          // dense, npeer > 0: row-split shard stored into every GPU of the group
+  // split layouts (decode.cuh kFmt*S): the scale tensor, staged after the weights of each stage as
+  // a [16 rows][sc_seg_bytes] slab at offset sc_off (same copy mode as the weights)
+  CUtensorMap smap;    // 2-D map over the scale bytes [all rows, sc_row_bytes] (u8), box 16 x sc_seg_bytes
+  const uint8_t* sc;
+  int sc_row_bytes, sc_seg_bytes, sc_off;
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
@@ -177,6 +182,90 @@ __device__ __forceinline__ void iq2_group_mma(const uint8_t* smem, const uint8_t
   }
 }
 
+// One k-group of a split-layout stage for lane (g, t): rows g / g+8 at byte offsets r0 / r1 of the
+// weight stage and s0 / s1 of the scale slab `sl`.  Weights enter the MMA exactly (decode.cuh);
+// the per-group scale is applied to the fp32 MMA result (FP4S: folded into the exact bf16 weight).
+template <int F, int NT, bool kCoherent>
+__device__ __forceinline__ void split_group_mma(const uint8_t* smem, const uint8_t* st, const uint8_t* sl, uint32_t r0,
+                                                uint32_t r1, uint32_t s0, uint32_t s1, int grp, int t,
+                                                uint32_t lut_lane, const bf16* const (&xr)[NT], int k0,
+                                                float (&acc)[NT][4]) {
+  auto ldx128 = [&](const bf16* p) { return kCoherent ? __ldcg(reinterpret_cast<const uint4*>(p)) : ldg128(p); };
+  auto ldx64 = [&](const bf16* p) { return kCoherent ? __ldcg(reinterpret_cast<const uint2*>(p)) : ldg64(p); };
+  uint32_t A0[4], A1[4];
+  float d0, d1;
+  if constexpr (F == kFmtQ8S) {
+    const uint32_t o = static_cast<uint32_t>(grp) * 32u + 4u * t;
+    q8_to_bf16x4(*reinterpret_cast<const uint32_t*>(st + r0 + o) ^ 0x80808080u, A0[0], A0[1]);
+    q8_to_bf16x4(*reinterpret_cast<const uint32_t*>(st + r0 + o + 16u) ^ 0x80808080u, A0[2], A0[3]);
+    q8_to_bf16x4(*reinterpret_cast<const uint32_t*>(st + r1 + o) ^ 0x80808080u, A1[0], A1[1]);
+    q8_to_bf16x4(*reinterpret_cast<const uint32_t*>(st + r1 + o + 16u) ^ 0x80808080u, A1[2], A1[3]);
+  } else if constexpr (F == kFmtQ4S || F == kFmtIQ2C || F == kFmtFP4S) {
+    const uint32_t o = static_cast<uint32_t>(grp) * 16u + 4u * t;
+    const uint32_t v0 = *reinterpret_cast<const uint32_t*>(st + r0 + o);
+    const uint32_t v1 = *reinterpret_cast<const uint32_t*>(st + r1 + o);
+    if constexpr (F == kFmtQ4S) {
+      q4s_words(v0, A0);
+      q4s_words(v1, A1);
+    } else if constexpr (F == kFmtIQ2C) {
+      iq2c_words(v0, A0);
+      iq2c_words(v1, A1);
+    } else {
+      fp4s_words(v0, A0);
+      fp4s_words(v1, A1);
+      const uint16_t* lut = reinterpret_cast<const uint16_t*>(smem);
+      const uint32_t so = static_cast<uint32_t>(grp) * 2u + static_cast<uint32_t>(t >> 1);
+      const uint32_t S0 = lut[sl[s0 + so]], S1 = lut[sl[s1 + so]];
+      const uint32_t S0x2 = S0 | (S0 << 16), S1x2 = S1 | (S1 << 16);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        A0[p] = hmul2_bits(A0[p], S0x2);
+        A1[p] = hmul2_bits(A1[p], S1x2);
+      }
+    }
+  } else {  // kFmtIQ2N: 8-byte record = 4 grid indices + sign/scale word; d per 256 elements
+    const uint32_t o = static_cast<uint32_t>(grp) * 8u;
+    const uint2 q0 = *reinterpret_cast<const uint2*>(st + r0 + o);
+    const uint2 q1 = *reinterpret_cast<const uint2*>(st + r1 + o);
+    const uint32_t so = static_cast<uint32_t>(grp >> 3) * 2u;
+    const uint32_t gi0 = (q0.x >> (8 * t)) & 0xFFu, gi1 = (q1.x >> (8 * t)) & 0xFFu;
+    const uint4 m0 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi0 << 7));
+    const uint4 m1 = *reinterpret_cast<const uint4*>(smem + lut_lane + (gi1 << 7));
+    iq2_apply_signs(m0, q0.y, 7u * t, A0);
+    iq2_apply_signs(m1, q1.y, 7u * t, A1);
+    d0 = iq2_db(fp16_bits_to_f32(ld_u16(sl, s0 + so)), q0.y);
+    d1 = iq2_db(fp16_bits_to_f32(ld_u16(sl, s1 + so)), q1.y);
+  }
+  if constexpr (F == kFmtQ8S || F == kFmtQ4S || F == kFmtIQ2C) {
+    d0 = __uint_as_float(ld_u16(sl, s0 + static_cast<uint32_t>(grp) * 2u) << 16);  // bf16 scale
+    d1 = __uint_as_float(ld_u16(sl, s1 + static_cast<uint32_t>(grp) * 2u) << 16);
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    uint32_t b0, b1, b2, b3;
+    if constexpr (F == kFmtQ8S) {
+      const uint2 xl = ldx64(xr[nt] + k0 + 4 * t), xh = ldx64(xr[nt] + k0 + 16 + 4 * t);
+      b0 = xl.x, b1 = xl.y, b2 = xh.x, b3 = xh.y;
+    } else {
+      const uint4 xv = ldx128(xr[nt] + k0 + 8 * t);
+      b0 = xv.x, b1 = xv.y, b2 = xv.z, b3 = xv.w;
+    }
+    if constexpr (F == kFmtFP4S) {
+      mma_bf16_16816(acc[nt], A0[0], A1[0], A0[1], A1[1], b0, b1, acc[nt]);
+      mma_bf16_16816(acc[nt], A0[2], A1[2], A0[3], A1[3], b2, b3, acc[nt]);
+    } else {
+      const float z[4] = {0.f, 0.f, 0.f, 0.f};
+      float D[4];
+      mma_bf16_16816(D, A0[0], A1[0], A0[1], A1[1], b0, b1, z);
+      mma_bf16_16816(D, A0[2], A1[2], A0[3], A1[3], b2, b3, D);
+      acc[nt][0] = fmaf(d0, D[0], acc[nt][0]);
+      acc[nt][1] = fmaf(d0, D[1], acc[nt][1]);
+      acc[nt][2] = fmaf(d1, D[2], acc[nt][2]);
+      acc[nt][3] = fmaf(d1, D[3], acc[nt][3]);
+    }
+  }
+}
+
 template <int F, int NT, int KW, int MODE>
 __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_constant__ EngineArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -194,11 +283,14 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
     }
     fence_mbar_init();
   }
-  if constexpr (F == kFmtIQ2) {
+  if constexpr (F == kFmtIQ2 || F == kFmtIQ2N) {
     fill_iq2_lut_bf16<(KW + 1) * 32>(smem, threadIdx.x);
   } else if constexpr (F == kFmtFP4) {
     uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
     for (int i = threadIdx.x; i < 256; i += blockDim.x) sl[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));
+  } else if constexpr (F == kFmtFP4S) {
+    uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sl[i] = static_cast<uint16_t>(e4m3fn_bf16_bits_x2p110(i));
   }
 
   int nitems;
@@ -252,27 +344,42 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
       for (int sp = 0; sp < a.nsplit; ++sp, ++it) {
         const int s = static_cast<int>(it % a.stages);
         uint8_t* dst = stages + s * a.stage_bytes;
+        uint8_t* sdst = dst + a.sc_off;
+        const int64_t row0 = (src - a.w) / a.row_bytes;  // global row of the tile's first row
+        const uint8_t* ssrc = is_split(F) ? a.sc + row0 * a.sc_row_bytes : nullptr;
         if (lane == 0) {
           if (it >= static_cast<uint32_t>(a.stages)) mbar_wait(&empty[s], ((it / a.stages) - 1) & 1, kSiteEmptyWait);
           if (a.contiguous) {
             const uint32_t bytes = static_cast<uint32_t>(rv * a.row_bytes);
             const uint32_t bulk = bytes & ~15u;
             for (uint32_t b = bulk; b < bytes; ++b) dst[b] = src[b];  // < 16 trailing bytes
+            uint32_t sbulk = 0;
+            if constexpr (is_split(F)) {
+              const uint32_t sbytes = static_cast<uint32_t>(rv * a.sc_row_bytes);
+              sbulk = sbytes & ~15u;
+              for (uint32_t b = sbulk; b < sbytes; ++b) sdst[b] = ssrc[b];
+            }
             fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&full[s], bulk);
+            mbar_arrive_expect_tx(&full[s], bulk + sbulk);
             if (bulk) bulk_g2s(dst, src, bulk, &full[s]);
+            if (sbulk) bulk_g2s(sdst, ssrc, sbulk, &full[s]);
           } else if (a.use_tmap) {
-            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(16 * a.stride));
-            const int row0 = static_cast<int>((src - a.w) / a.row_bytes);
-            tma_load_2d(dst, &a.tmap, sp * (a.seg_bytes / 8), row0, &full[s]);
+            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(16 * a.stride + (is_split(F) ? 16 * a.sc_seg_bytes : 0)));
+            tma_load_2d(dst, &a.tmap, sp * (a.seg_bytes / 8), static_cast<int>(row0), &full[s]);
+            if constexpr (is_split(F)) tma_load_2d(sdst, &a.smap, sp * a.sc_seg_bytes, static_cast<int>(row0), &full[s]);
           } else {
-            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.seg_bytes));
+            mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * (a.seg_bytes + (is_split(F) ? a.sc_seg_bytes : 0))));
           }
         }
         __syncwarp();
-        if (!a.contiguous && !a.use_tmap && lane < rv)
+        if (!a.contiguous && !a.use_tmap && lane < rv) {
           bulk_g2s(dst + lane * a.stride, src + static_cast<int64_t>(sp) * a.seg_bytes + static_cast<int64_t>(lane) * a.row_bytes,
                    a.seg_bytes, &full[s]);
+          if constexpr (is_split(F))
+            bulk_g2s(sdst + lane * a.sc_seg_bytes,
+                     ssrc + static_cast<int64_t>(sp) * a.sc_seg_bytes + static_cast<int64_t>(lane) * a.sc_row_bytes,
+                     a.sc_seg_bytes, &full[s]);
+        }
       }
     }
     // drain: the last uses of each stage must have landed before the CTA may exit
@@ -290,7 +397,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
   const int gps = a.kc / 32;  // k-groups per stage
   const int g0 = (warp * gps) / KW, g1 = ((warp + 1) * gps) / KW;
   float post = a.post;
-  if constexpr (MODE == kModeDense && F == kFmtFP4) post *= __ldg(a.gscale);
+  if constexpr (MODE == kModeDense && (F == kFmtFP4 || F == kFmtFP4S)) post *= __ldg(a.gscale);
   const uint32_t lut_lane = static_cast<uint32_t>(lane & 7) * 16u;
   const uint16_t* fp4lut = reinterpret_cast<const uint16_t*>(smem);
 
@@ -347,6 +454,10 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
           }
         } else if constexpr (F == kFmtIQ2) {
           iq2_group_mma<NT, false>(smem, st, r0, r1, grp, t, lut_lane, xr, k0, acc);
+        } else if constexpr (is_split(F)) {
+          const uint32_t scs = static_cast<uint32_t>(a.contiguous ? a.sc_row_bytes : a.sc_seg_bytes);
+          split_group_mma<F, NT, false>(smem, st, st + a.sc_off, r0, r1, g * scs, (g + 8) * scs, grp, t,
+                                                    lut_lane, xr, k0, acc);
         } else {  // NVFP4: group = sub-blocks 2h, 2h+1 of block grp/2
           const uint32_t bo = static_cast<uint32_t>(grp >> 1) * 36u;
           const uint32_t h2 = static_cast<uint32_t>(grp & 1) * 2u;

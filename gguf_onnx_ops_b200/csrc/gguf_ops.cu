@@ -105,7 +105,7 @@ int make_plan(EngineArgs& a, int K, int row_bytes, int NT, bool moe, size_t* sme
   using Fi = FmtInfo<F>;
   a.K = K;
   a.row_bytes = row_bytes;
-  const int lut = F == kFmtIQ2 ? 256 * 8 * 16 : (F == kFmtFP4 ? 512 : 0);
+  const int lut = (F == kFmtIQ2 || F == kFmtIQ2N) ? 256 * 8 * 16 : ((F == kFmtFP4 || F == kFmtFP4S) ? 512 : 0);
   const int red = kKW * NT * 128 * 4;
   const int grp = moe ? (4 * kMaxPairs + kMaxPairs * 8 + 4) * 4 : 0;
   bool seg = (row_bytes % 16 == 0) && (K % Fi::kSeg == 0);
@@ -133,6 +133,13 @@ int make_plan(EngineArgs& a, int K, int row_bytes, int NT, bool moe, size_t* sme
     a.contiguous = 1;
   }
   a.stage_bytes = ((16 * a.stride + 16) + 127) & ~127;  // +16: unaligned-read overrun pad
+  if constexpr (Fi::kScDiv > 0) {  // split layout: the stage's scale slab follows the weights
+    a.sc_row_bytes = K / Fi::kScDiv;
+    a.sc_seg_bytes = kc / Fi::kScDiv;
+    a.sc_off = (16 * a.stride + 16 + 127) & ~127;  // TMA destination: 128-byte aligned
+    const int slab = 16 * (a.contiguous ? a.sc_row_bytes : a.sc_seg_bytes) + 16;
+    a.stage_bytes = ((a.sc_off + slab) + 127) & ~127;
+  }
   const int fixed = lut + red + grp + 2 * 8 * 8 + 256;
   int budget = kSmemBudget;
   int stages = (budget - fixed) / a.stage_bytes;
@@ -174,11 +181,22 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // Segmented engine staging through a 2-D tensor map (see EngineArgs::tmap): rows_total rows of
 // row_bytes (a multiple of 16) starting at a.w, boxes of 16 rows x a.stride bytes.  Leaves the
 // per-row copies in place when the plan or the driver does not allow it.
-void attach_tensor_map(EngineArgs& a, int64_t rows_total) {
+void attach_tensor_map(EngineArgs& a, int64_t rows_total, bool split = false) {
   a.use_tmap = 0;
   if (a.contiguous || a.stride > 2048 || a.stride % 16 || a.row_bytes % 16 || a.seg_bytes % 16) return;
   auto enc = tensor_map_encoder();
   if (!enc) return;
+  if (split) {  // the scale slab rides on a second map; without it both use per-row copies
+    if (a.sc_row_bytes % 16 || a.sc_seg_bytes % 16 || a.sc_seg_bytes > 256) return;
+    cuuint64_t sdims[2] = {static_cast<cuuint64_t>(a.sc_row_bytes), static_cast<cuuint64_t>(rows_total)};
+    cuuint64_t sstride[1] = {static_cast<cuuint64_t>(a.sc_row_bytes)};
+    cuuint32_t sbox[2] = {static_cast<cuuint32_t>(a.sc_seg_bytes), 16u};
+    cuuint32_t ses[2] = {1u, 1u};
+    if (enc(&a.smap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.sc), sdims, sstride, sbox, ses,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return;
+  }
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.row_bytes / 8), static_cast<cuuint64_t>(rows_total)};
   cuuint64_t gstride[1] = {static_cast<cuuint64_t>(a.row_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(a.stride / 8), 16u};
@@ -214,6 +232,35 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
   const int grid = std::min(a.tiles, sms);
   cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("gemv launch", e);
+  return GGUF_OK;
+}
+
+// Split (legacy) layouts on the engine: weights w [N, K/32 * kBytes], scales sc [N, K/kScDiv].
+template <int F, int NT>
+int run_dense_split(const void* x, const void* w, const void* sc, const float* gscale, void* y, int R, int N, int K,
+                    cudaStream_t s) {
+  EngineArgs a = {};
+  size_t smem = 0;
+  int rc = make_plan<F>(a, K, K / 32 * FmtInfo<F>::kBytes, NT, false, &smem);
+  if (rc) return rc;
+  a.w = static_cast<const uint8_t*>(w);
+  a.sc = static_cast<const uint8_t*>(sc);
+  a.rows = N;
+  a.tiles = (N + 15) / 16;
+  attach_tensor_map(a, N, true);
+  a.x = static_cast<const bf16*>(x);
+  a.R = R;
+  a.y = y;
+  a.gscale = gscale;
+  a.post = F == kFmtFP4S ? 65536.0f : 1.0f;
+  int sms = 0;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = engine_kernel<F, NT, kKW, kModeDense>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  const int grid = std::min(a.tiles, sms);
+  cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("legacy-layout gemv launch", e);
   return GGUF_OK;
 }
 
@@ -832,6 +879,45 @@ int gguf_q8_0_embed(const void* w, const int64_t* ids, void* out, int64_t vocab,
                                static_cast<const uint8_t*>(w), ids, vocab, nb, R, static_cast<bf16*>(out));
   if (e != cudaSuccess) return cuda_fail("Q8Embed launch", e);
   return GGUF_OK;
+}
+
+int gguf_gemv_legacy(int layout, const void* x, const void* w, const void* scales, const float* gscale, void* y,
+                     int64_t R, int64_t N, int64_t K, void* stream) {
+  t_last_error.clear();
+  static const char* const kNames[] = {"Q8Gemv gguf=0", "Q4Gemv iq2=0", "Q4Gemv iq2=1", "Q4Gemv iq2=2",
+                                       "Nvfp4Gemv gguf=0"};
+  if (layout < GGUF_LAYOUT_Q8_SPLIT || layout > GGUF_LAYOUT_NVFP4_SPLIT)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "legacy GEMV: unknown layout " + std::to_string(layout));
+  const std::string op = kNames[layout];
+  if (!x || !w || !scales || !y || (layout == GGUF_LAYOUT_NVFP4_SPLIT && !gscale))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": null tensor pointer");
+  const int64_t kmul = layout == GGUF_LAYOUT_IQ2_NATIVE ? 256 : 32;
+  if (K <= 0 || K % kmul != 0 || K > (1 << 20))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": K mismatch (K % " + std::to_string(kmul) + " == 0 required)" +
+                                               dims(R, N, K));
+  if (R < 1 || R > 16) return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": rows must be in [1,16]" + dims(R, N, K));
+  if (!int_range(N)) return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": bad N" + dims(R, N, K));
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(scales, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": x, w and the scale tensor must be 16-byte aligned");
+  auto* s = static_cast<cudaStream_t>(stream);
+  const int r = static_cast<int>(R), n = static_cast<int>(N), k = static_cast<int>(K);
+  switch (layout) {
+    case GGUF_LAYOUT_Q8_SPLIT:
+      return R <= 8 ? run_dense_split<kFmtQ8S, 1>(x, w, scales, gscale, y, r, n, k, s)
+                    : run_dense_split<kFmtQ8S, 2>(x, w, scales, gscale, y, r, n, k, s);
+    case GGUF_LAYOUT_Q4_SPLIT:
+      return R <= 8 ? run_dense_split<kFmtQ4S, 1>(x, w, scales, gscale, y, r, n, k, s)
+                    : run_dense_split<kFmtQ4S, 2>(x, w, scales, gscale, y, r, n, k, s);
+    case GGUF_LAYOUT_IQ2_CODES:
+      return R <= 8 ? run_dense_split<kFmtIQ2C, 1>(x, w, scales, gscale, y, r, n, k, s)
+                    : run_dense_split<kFmtIQ2C, 2>(x, w, scales, gscale, y, r, n, k, s);
+    case GGUF_LAYOUT_IQ2_NATIVE:
+      return R <= 8 ? run_dense_split<kFmtIQ2N, 1>(x, w, scales, gscale, y, r, n, k, s)
+                    : run_dense_split<kFmtIQ2N, 2>(x, w, scales, gscale, y, r, n, k, s);
+    default:
+      return R <= 8 ? run_dense_split<kFmtFP4S, 1>(x, w, scales, gscale, y, r, n, k, s)
+                    : run_dense_split<kFmtFP4S, 2>(x, w, scales, gscale, y, r, n, k, s);
+  }
 }
 
 int gguf_rms_norm(const void* x, const void* skip, const float* gamma, void* y, void* sum, int64_t R, int64_t H,

@@ -95,8 +95,21 @@ void gemv_shapes(Ort::KernelContext& c, int64_t& R, int64_t& N, int64_t& K, std:
   yshape.back() = N;
 }
 
+// Legacy split layouts: weights in input 1, scales in input 2 (src/bolt_ops.cu:1593-1643, :1411-1469).
+void gemv_legacy(Ort::KernelContext& c, int layout, const char* op, int64_t kmul) {
+  int64_t R, N, K;
+  std::vector<int64_t> ys;
+  gemv_shapes(c, R, N, K, ys);
+  if (!present(c, 2)) throw std::invalid_argument(std::string(op) + ": the scale input is required");
+  if (K % kmul != 0) throw std::invalid_argument("QGemv: K mismatch");
+  auto y = c.GetOutput(0, ys);
+  const float* g = layout == GGUF_LAYOUT_NVFP4_SPLIT ? c.GetInput(3).GetTensorData<float>() : nullptr;
+  check(gguf_gemv_legacy(layout, c.GetInput(0).GetTensorRawData(), c.GetInput(1).GetTensorRawData(),
+                         c.GetInput(2).GetTensorRawData(), g, y.GetTensorMutableRawData(), R, N, K, stream(c)));
+}
+
 void q8_gemv(Ort::KernelContext& c, const Attrs& a) {
-  if (a.gguf != 1) throw NotImplemented("Q8Gemv: only the raw GGUF Q8_0 layout (gguf=1) is implemented");
+  if (a.gguf != 1) return gemv_legacy(c, GGUF_LAYOUT_Q8_SPLIT, "Q8Gemv", 32);
   int64_t R, N, K;
   std::vector<int64_t> ys;
   gemv_shapes(c, R, N, K, ys);
@@ -108,7 +121,10 @@ void q8_gemv(Ort::KernelContext& c, const Attrs& a) {
 }
 
 void q4_gemv(Ort::KernelContext& c, const Attrs& a) {
-  if (a.iq2 != 3) throw NotImplemented("Q4Gemv: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented");
+  if (a.iq2 == 0) return gemv_legacy(c, GGUF_LAYOUT_Q4_SPLIT, "Q4Gemv", 32);
+  if (a.iq2 == 1) return gemv_legacy(c, GGUF_LAYOUT_IQ2_CODES, "Q4Gemv iq2=1", 32);
+  if (a.iq2 == 2) return gemv_legacy(c, GGUF_LAYOUT_IQ2_NATIVE, "Q4Gemv iq2=2", 256);
+  if (a.iq2 != 3) throw NotImplemented("Q4Gemv: unknown iq2 value");
   int64_t R, N, K;
   std::vector<int64_t> ys;
   gemv_shapes(c, R, N, K, ys);
@@ -120,7 +136,7 @@ void q4_gemv(Ort::KernelContext& c, const Attrs& a) {
 }
 
 void fp4_gemv(Ort::KernelContext& c, const Attrs& a) {
-  if (a.gguf != 1) throw NotImplemented("Nvfp4Gemv: only the raw GGUF NVFP4 layout (gguf=1) is implemented");
+  if (a.gguf != 1) return gemv_legacy(c, GGUF_LAYOUT_NVFP4_SPLIT, "Nvfp4Gemv", 32);
   int64_t R, N, K;
   std::vector<int64_t> ys;
   gemv_shapes(c, R, N, K, ys);

@@ -17,9 +17,10 @@ C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
     MoeVerify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s=None, topk, iq2=3) -> out, h, part, meta
                                                                    src/bolt_ops.cu:1327-1409, :1981-1996
 
-Only the GGUF layouts are implemented (``gguf=1`` / ``iq2=3``); the legacy layouts raise
-NotImplementedError.  The lower-level ``*_into`` functions write into caller-provided outputs
-(no allocation), for graph capture and benchmarking.
+Every weight layout of the GEMVs is implemented: the GGUF ones (``gguf=1`` / ``iq2=3``) and the
+legacy split layouts (``gguf=0``, ``iq2`` in 0..2, through ``gguf_gemv_legacy``).  The lower-level
+``*_into`` functions write into caller-provided outputs (no allocation), for graph capture and
+benchmarking.
 """
 
 from __future__ import annotations
@@ -74,10 +75,31 @@ def _gemv_shapes(x: torch.Tensor, w: torch.Tensor):
     return R, N, K
 
 
+def gemv_legacy_into(layout: int, x, w, scales, gscale, y, R: int, N: int, K: int, stream=None) -> None:
+    check(load().gguf_gemv_legacy(layout, _ptr(x), _ptr(w), _ptr(scales), _ptr(gscale), _ptr(y), R, N, K,
+                                  _stream(stream)))
+
+
+def _legacy(op, layout, x, w, scales, gscale=None):
+    _need(x, "x", torch.bfloat16, op)
+    _need(w, "w", torch.uint8, op)
+    R, N, K = _gemv_shapes(x, w)
+    y = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    gemv_legacy_into(layout, x, w, scales, gscale, y, R, N, K)
+    return y
+
+
 def Q8Gemv(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor | None = None, gguf: int = 1) -> torch.Tensor:
-    """y[..., N] = x[..., K] @ deq(W)^T with raw GGUF Q8_0 blocks W [N, (K/32)*34]."""
+    """y[..., N] = x[..., K] @ deq(W)^T.  gguf=1: raw GGUF Q8_0 blocks W [N, (K/32)*34]; gguf=0: the
+    split layout W u8 [N, K/32, 32] = q + 128 with bf16 scales [N, K/32] (src/bolt_ops.cu:1617-1640)."""
     if gguf != 1:
-        raise NotImplementedError("Q8Gemv: only the raw GGUF Q8_0 layout (gguf=1) is implemented")
+        _need(w, "w", torch.uint8, "Q8Gemv")
+        _need(scales, "scales", torch.bfloat16, "Q8Gemv")
+        K = x.shape[-1]
+        if K % 32 != 0 or w.dim() < 2 or w.shape[1] * 32 != K or w.numel() != w.shape[0] * K \
+                or scales.numel() != w.shape[0] * (K // 32):
+            raise ValueError("QGemv: K mismatch")
+        return _legacy("Q8Gemv", _lib.GGUF_LAYOUT_Q8_SPLIT, x, w, scales)
     _need(x, "x", torch.bfloat16, "Q8Gemv")
     _need(w, "w", torch.uint8, "Q8Gemv")
     R, N, K = _gemv_shapes(x, w)
@@ -89,9 +111,27 @@ def Q8Gemv(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor | None = None,
 
 
 def Q4Gemv(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor | None = None, iq2: int = 3) -> torch.Tensor:
-    """y[..., N] = x[..., K] @ deq(W)^T with raw GGUF IQ2_XXS super-blocks W [N, (K/256)*66]."""
+    """y[..., N] = x[..., K] @ deq(W)^T.  iq2=3: raw GGUF IQ2_XXS super-blocks W [N, (K/256)*66];
+    iq2=0: 4-bit W [N, K/32, 16] (n - 8) with bf16 scales [N, K/32]; iq2=1: 3-bit IQ2 codes in the
+    same packing; iq2=2: IQ2_XXS records W [N, K/32, 8] with fp16 d bits [N, K/256] carried in a
+    bf16-typed tensor (src/bolt_ops.cu:1593-1643)."""
     if iq2 != 3:
-        raise NotImplementedError("Q4Gemv: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented")
+        if iq2 not in (0, 1, 2):
+            raise NotImplementedError(f"Q4Gemv: unknown iq2={iq2}")
+        _need(w, "w", torch.uint8, "Q4Gemv")
+        _need(scales, "scales", torch.bfloat16, "Q4Gemv")
+        K = x.shape[-1]
+        N = w.shape[0]
+        if iq2 == 2:
+            if K % 256 != 0 or w.dim() != 3 or w.shape[1] * 32 != K or w.shape[2] != 8 or scales.numel() != N * (K // 256):
+                raise ValueError("Q4Gemv iq2=2: needs B [N, K/32, 8] and 1..16 rows")
+            layout = _lib.GGUF_LAYOUT_IQ2_NATIVE
+        else:
+            if K % 32 != 0 or w.dim() < 2 or w.shape[1] * 32 != K or w.numel() != N * K // 2 \
+                    or scales.numel() != N * (K // 32):
+                raise ValueError("QGemv: K mismatch")
+            layout = _lib.GGUF_LAYOUT_IQ2_CODES if iq2 == 1 else _lib.GGUF_LAYOUT_Q4_SPLIT
+        return _legacy("Q4Gemv", layout, x, w, scales)
     _need(x, "x", torch.bfloat16, "Q4Gemv")
     _need(w, "w", torch.uint8, "Q4Gemv")
     R, N, K = _gemv_shapes(x, w)
@@ -104,9 +144,16 @@ def Q4Gemv(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor | None = None,
 
 def Nvfp4Gemv(x: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor | None, gscale: torch.Tensor,
               gguf: int = 1) -> torch.Tensor:
-    """y[..., N] = gscale * (x[..., K] @ deq(W)^T) with raw GGUF NVFP4 blocks W [N, (K/64)*36]."""
+    """y[..., N] = gscale * (x[..., K] @ deq(W)^T).  gguf=1: raw GGUF NVFP4 blocks W [N, (K/64)*36];
+    gguf=0: E2M1 nibbles W [N, K/2] with e4m3fn scales [N, K/16] (src/bolt_ops.cu:1411-1469)."""
     if gguf != 1:
-        raise NotImplementedError("Nvfp4Gemv: only the raw GGUF NVFP4 layout (gguf=1) is implemented")
+        _need(w, "w", torch.uint8, "Nvfp4Gemv")
+        _need(w_scale, "ws", torch.uint8, "Nvfp4Gemv")
+        _need(gscale, "gscale", torch.float32, "Nvfp4Gemv")
+        K = x.shape[-1]
+        if K % 32 != 0 or w.dim() != 2 or w.shape[1] * 2 != K or w_scale.numel() != w.shape[0] * (K // 16):
+            raise ValueError("Nvfp4Gemv: K mismatch (K % 32 required)")
+        return _legacy("Nvfp4Gemv", _lib.GGUF_LAYOUT_NVFP4_SPLIT, x, w, w_scale, gscale)
     _need(x, "x", torch.bfloat16, "Nvfp4Gemv")
     _need(w, "w", torch.uint8, "Nvfp4Gemv")
     _need(gscale, "gscale", torch.float32, "Nvfp4Gemv")

@@ -72,6 +72,31 @@ GGUF_OPS_API int gguf_nvfp4_gemv(const void* x, const void* w, const float* gsca
                                  int64_t K, void* stream);
 
 /*
+ * Legacy (pre-GGUF, "split") weight layouts of the same ops, selected in the reference by attribute
+ * values other than gguf=1 / iq2=3 (src/bolt_ops.cu:840-848, :1411-1469, :1593-1643):
+ *
+ *   layout                     op / attribute       w                         scales
+ *   GGUF_LAYOUT_Q8_SPLIT       Q8Gemv gguf=0        u8 [N, K] = q + 128       bf16 [N, K/32]
+ *   GGUF_LAYOUT_Q4_SPLIT       Q4Gemv iq2=0         u8 [N, K/2] nibbles n     bf16 [N, K/32]    (value (n - 8) * s)
+ *   GGUF_LAYOUT_IQ2_CODES      Q4Gemv iq2=1         u8 [N, K/2] codes c       bf16 [N, K/32]    (value {8,25,43,0}[c&3] * (c&4 ? -1 : 1) * s)
+ *   GGUF_LAYOUT_IQ2_NATIVE     Q4Gemv iq2=2         u8 [N, K/32, 8] records   fp16 bits [N, K/256] (IQ2_XXS blocks minus d)
+ *   GGUF_LAYOUT_NVFP4_SPLIT    Nvfp4Gemv gguf=0     u8 [N, K/2] E2M1 nibbles  e4m3fn [N, K/16], times gscale[0]
+ *
+ * Nibble tensors hold element 2i in the low and 2i+1 in the high nibble of byte i.  x bf16 [R, K],
+ * y bf16 [R, N]; 1 <= R <= 16; K % 32 == 0 (IQ2_NATIVE: K % 256 == 0); x, w and scales 16-byte
+ * aligned.  Weights enter the tensor cores exactly; scales are applied in fp32 after the MMA.
+ */
+enum {
+  GGUF_LAYOUT_Q8_SPLIT = 0,
+  GGUF_LAYOUT_Q4_SPLIT = 1,
+  GGUF_LAYOUT_IQ2_CODES = 2,
+  GGUF_LAYOUT_IQ2_NATIVE = 3,
+  GGUF_LAYOUT_NVFP4_SPLIT = 4
+};
+GGUF_OPS_API int gguf_gemv_legacy(int layout, const void* x, const void* w, const void* scales, const float* gscale,
+                                  void* y, int64_t R, int64_t N, int64_t K, void* stream);
+
+/*
  * Q8Embed:  out[..., k] = bf16(fp32(d) * q[k]) of the rows input_ids[...] of a GGUF Q8_0 embedding
  * table w [vocab, row_bytes] (row_bytes = (K/32)*34); ids outside [0, vocab) read row 0.
  * ids: int64 [R] (any shape, flattened); out: bf16 [R, K].  R = 0 is a no-op.

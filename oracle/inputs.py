@@ -72,6 +72,32 @@ def q8_test_blocks(g: np.random.Generator, n: int, k: int) -> np.ndarray:
     return blk.reshape(n, nb * Q8_0_BYTES)
 
 
+def legacy_case(layout: str, g: np.random.Generator, n: int, k: int):
+    """Weights + scales of a legacy split layout, as the reference harness builds them
+    (tests/test_bolt_ops.py:70-75 NVFP4, :84-93 Q8 / Q4, :159-175 IQ2 codes, :210-223 IQ2 native).
+    Returns (w u8, scales (bf16 bits u16 / e4m3fn u8 / fp16 bits u16))."""
+    nb = k // 32
+    if layout == "q8":
+        w = g.integers(0, 256, size=(n, k), dtype=np.uint8)
+    elif layout == "q4":
+        w = g.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+    elif layout == "iq2c":
+        code = (g.integers(0, 3, size=(n, k)) + 4 * g.integers(0, 2, size=(n, k))).astype(np.uint8)
+        w = (code[:, 0::2] | (code[:, 1::2] << 4)).astype(np.uint8)
+    elif layout == "iq2n":
+        from .quants import iq2_native_from_blocks
+
+        return iq2_native_from_blocks(iq2_test_blocks(g, (n,), k))
+    elif layout == "fp4":
+        w = g.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+        return w, g.integers(0x30, 0x48, size=(n, k // 16), dtype=np.uint8)
+    else:
+        raise ValueError(layout)
+    from .quants import bf16_bits
+
+    return w, bf16_bits((g.random((n, nb)) * 0.02).astype(np.float32))
+
+
 # Config shapes (BASELINE.json "configs", in order).
 CONFIGS = {
     "C0": dict(op="q8_0", N=4096, K=4096, R=(1,)),

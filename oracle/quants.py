@@ -169,3 +169,85 @@ def dequant_nvfp4(raw: np.ndarray) -> np.ndarray:
     nib = np.concatenate([qs & 0x0F, qs >> 4], axis=-1)  # [n, 4, 16]
     vals = _NVFP4_KVALUES[nib]
     return (d * vals).reshape(rows, -1)
+
+
+# ----------------------------------------------------------------------------------------------
+# Split (pre-GGUF) layouts of the reference's legacy attribute values; expected values as the
+# reference harness computes them (tests/test_bolt_ops.py:70-100, 155-181, 210-232).
+# Nibble tensors: element 2i is the low nibble of byte i, element 2i+1 the high nibble.
+# ----------------------------------------------------------------------------------------------
+def _nibbles(w: np.ndarray) -> np.ndarray:
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    return np.stack([w & 0x0F, w >> 4], axis=-1).reshape(w.shape[0], -1)
+
+
+def _group_scale(s_bits: np.ndarray, K: int) -> np.ndarray:
+    """bf16 scale bits [N, K/32] -> fp32 per element [N, K]."""
+    return np.repeat(bf16_to_f32(np.asarray(s_bits, np.uint16)), 32, axis=1).reshape(-1, K)
+
+
+def dequant_q8_split(w: np.ndarray, s_bits: np.ndarray) -> np.ndarray:
+    """Q8Gemv gguf=0: w u8 [N, K] holding q + 128, bf16 scales [N, K/32] -> (w - 128) * s
+    (tests/test_bolt_ops.py:88-95)."""
+    w = np.asarray(w, np.uint8)
+    return (w.astype(np.float32) - np.float32(128)) * _group_scale(s_bits, w.shape[1])
+
+
+def dequant_q4_split(w: np.ndarray, s_bits: np.ndarray) -> np.ndarray:
+    """Q4Gemv iq2=0: nibbles n [N, K/2], bf16 scales [N, K/32] -> (n - 8) * s (:90-95)."""
+    n = _nibbles(w)
+    return (n.astype(np.float32) - np.float32(8)) * _group_scale(s_bits, n.shape[1])
+
+
+IQ2_CODE_VALUES = np.array([8, 25, 43, 0, -8, -25, -43, 0], dtype=np.float32)  # tests/test_bolt_ops.py:156
+
+
+def dequant_iq2_codes(w: np.ndarray, s_bits: np.ndarray) -> np.ndarray:
+    """Q4Gemv iq2=1: 3-bit codes c = mag + 4 * negative in nibbles [N, K/2], bf16 scales [N, K/32]
+    -> {8, 25, 43, 0}[mag] * sign * s (:155-181).  Bit 3 of a nibble is not part of the format and is
+    ignored."""
+    c = _nibbles(w) & 7
+    return IQ2_CODE_VALUES[c] * _group_scale(s_bits, c.shape[1])
+
+
+def iq2_native_from_blocks(blk: np.ndarray):
+    """GGUF IQ2_XXS blocks [N, K/256 * 66] -> (records u8 [N, K/32, 8], fp16 d bits u16 [N, K/256]),
+    the repacking of the reference harness's iq2_repack (tests/test_bolt_ops.py:218-223)."""
+    blk = np.ascontiguousarray(blk, np.uint8)
+    N = blk.shape[0]
+    b = blk.reshape(N, -1, IQ2_XXS_BYTES)
+    rec = np.ascontiguousarray(b[:, :, 2:]).reshape(N, -1, 8)
+    d = np.ascontiguousarray(b[:, :, :2]).view(np.uint16).reshape(N, -1)
+    return rec, d
+
+
+def dequant_iq2_native(rec: np.ndarray, d_bits: np.ndarray) -> np.ndarray:
+    """Q4Gemv iq2=2: records [N, K/32, 8] + fp16 d [N, K/256] -> the gguf-py IQ2_XXS values of the
+    reassembled blocks (exact; the reference kernel rounds each weight to bf16, :237)."""
+    rec = np.asarray(rec, np.uint8)
+    N, g = rec.shape[0], rec.shape[1]
+    d = np.asarray(d_bits, np.uint16).reshape(N, g // 8, 1).view(np.uint8)
+    blk = np.concatenate([d, rec.reshape(N, g // 8, 64)], axis=2)
+    return dequant_iq2_xxs(blk.reshape(N, -1))
+
+
+_E2M1 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6], dtype=np.float32)  # :67
+
+
+def e4m3fn_table() -> np.ndarray:
+    """All 256 bytes as torch.float8_e4m3fn values (signed, bias 7, subnormal for e == 0, 0x7F and
+    0xFF NaN)."""
+    x = np.arange(256, dtype=np.uint32)
+    e = ((x >> 3) & 15).astype(np.float32)
+    m = (x & 7).astype(np.float32)
+    v = np.where(e == 0, m * np.float32(2.0 ** -9), (1 + m / 8) * np.float32(2.0) ** (e - 7)).astype(np.float32)
+    v = np.where(x & 0x80, -v, v).astype(np.float32)
+    return np.where((x & 0x7F) == 0x7F, np.float32(np.nan), v).astype(np.float32)
+
+
+def dequant_nvfp4_split(w: np.ndarray, ws: np.ndarray) -> np.ndarray:
+    """Nvfp4Gemv gguf=0: E2M1 nibbles [N, K/2], e4m3fn scales [N, K/16] -> E2M1 * scale (the
+    global scale is applied by the caller) (tests/test_bolt_ops.py:70-79)."""
+    n = _nibbles(w)
+    s = np.repeat(e4m3fn_table()[np.asarray(ws, np.uint8)], 16, axis=1)
+    return _E2M1[n] * s

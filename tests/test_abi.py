@@ -84,21 +84,34 @@ def test_no_silent_fallback_without_gpu(lib):
     assert lib.gguf_last_error()
 
 
-def test_ops_reject_legacy_layouts():
+def test_ops_validate_legacy_layouts_without_gpu():
+    """Legacy attribute values are implemented: shapes are checked on the host before any launch,
+    and host tensors are refused."""
     import torch
 
     from gguf_onnx_ops_b200 import ops
 
     x = torch.zeros(1, 64, dtype=torch.bfloat16)
     w = torch.zeros(8, 68, dtype=torch.uint8)
-    with pytest.raises(NotImplementedError):
-        ops.Q8Gemv(x, w, gguf=0)
-    with pytest.raises(NotImplementedError):
-        ops.Q4Gemv(x, w, iq2=2)
-    with pytest.raises(NotImplementedError):
-        ops.Nvfp4Gemv(x, w, None, torch.ones(1), gguf=0)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        ops.Q8Gemv(x, w, torch.zeros(8, 2, dtype=torch.bfloat16), gguf=0)
+    with pytest.raises(ValueError):
+        ops.Q4Gemv(x, w, None, iq2=2)
+    with pytest.raises(NotImplementedError, match="unknown iq2"):
+        ops.Q4Gemv(x, w, None, iq2=5)
     with pytest.raises(ValueError, match="CUDA tensor"):
         ops.Q8Gemv(x, w)
+
+
+def test_legacy_entry_rejects_bad_layouts(lib):
+    rc = lib.gguf_gemv_legacy(9, FAKE, FAKE, FAKE, None, FAKE, 1, 64, 64, None)
+    assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT and b"unknown layout" in lib.gguf_last_error()
+    rc = lib.gguf_gemv_legacy(_lib.GGUF_LAYOUT_IQ2_NATIVE, FAKE, FAKE, FAKE, None, FAKE, 1, 64, 96, None)
+    assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT and b"K % 256" in lib.gguf_last_error()
+    rc = lib.gguf_gemv_legacy(_lib.GGUF_LAYOUT_NVFP4_SPLIT, FAKE, FAKE, FAKE, None, FAKE, 1, 64, 64, None)
+    assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT and b"null" in lib.gguf_last_error()
+    rc = lib.gguf_gemv_legacy(_lib.GGUF_LAYOUT_Q8_SPLIT, FAKE, FAKE, FAKE, None, FAKE, 17, 64, 64, None)
+    assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT and b"rows" in lib.gguf_last_error()
 
 
 def test_missing_library_fails_loudly(tmp_path, monkeypatch):

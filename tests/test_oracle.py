@@ -153,6 +153,48 @@ def test_rms_norm_ref_matches_golden(golden, name):
         assert rel(got, O.bf16_to_f32(d[f"{name}_{key}"])) < 1e-3
 
 
+@pytest.mark.parametrize("layout", ["q8", "q4", "iq2c", "iq2n", "fp4"])
+def test_legacy_dequant_matches_harness_expressions(layout):
+    """The split-layout dequantisers against the reference harness's torch expressions."""
+    g = I.rng(77)
+    N, K = 24, 512
+    w, s = I.legacy_case(layout, g, N, K)
+    wt = torch.from_numpy(w)
+    if layout in ("q8", "q4", "iq2c"):
+        sc = torch.from_numpy(s.astype(np.int16)).view(torch.bfloat16).float()
+    if layout == "q8":
+        ref = ((wt.float() - 128).reshape(N, K // 32, 32) * sc.unsqueeze(-1)).reshape(N, K)
+        got = O.dequant_q8_split(w, s)
+    elif layout == "q4":
+        q = wt.reshape(N, K // 32, 16)
+        ref = ((torch.stack([(q & 15).float(), (q >> 4).float()], -1).reshape(N, K // 32, 32) - 8)
+               * sc.unsqueeze(-1)).reshape(N, K)
+        got = O.dequant_q4_split(w, s)
+    elif layout == "iq2c":
+        vals = torch.tensor([8, 25, 43, 0, -8, -25, -43, 0], dtype=torch.float32)
+        code = torch.stack([wt & 15, wt >> 4], -1).reshape(N, K)
+        ref = (vals[code.long()].reshape(N, K // 32, 32) * sc.unsqueeze(-1)).reshape(N, K)
+        got = O.dequant_iq2_codes(w, s)
+    elif layout == "iq2n":
+        blk = np.concatenate([s.reshape(N, K // 256, 1).view(np.uint8), w.reshape(N, K // 256, 64)], axis=2)
+        from gguf import GGMLQuantizationType as Q
+        from gguf import quants
+
+        ref = torch.from_numpy(np.asarray(quants.dequantize(blk.reshape(N, -1), Q.IQ2_XXS), np.float32).reshape(N, K))
+        got = O.dequant_iq2_native(w, s)
+    else:
+        fp4 = torch.tensor([0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.0, -0.5, -1, -1.5, -2, -3, -4, -6])
+        deq = torch.stack([fp4[(wt & 15).long()], fp4[(wt >> 4).long()]], -1).reshape(N, K)
+        ref = deq * torch.from_numpy(s).view(torch.float8_e4m3fn).float().repeat_interleave(16, 1)
+        got = O.dequant_nvfp4_split(w, s)
+    assert np.array_equal(got, ref.numpy())
+
+
+def test_e4m3fn_table_matches_torch():
+    ref = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(O.e4m3fn_table(), ref, equal_nan=True)
+
+
 def test_bf16_round_matches_torch():
     v = (I.rng(9).standard_normal(4096) * 100).astype(np.float32)
     assert np.array_equal(O.bf16_round(v), torch.from_numpy(v).bfloat16().float().numpy())
