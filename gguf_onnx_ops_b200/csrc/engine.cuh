@@ -310,7 +310,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_c
     const int U = s_pair[kMaxPairs * 8];
     nitems = U * a.tiles;
     if constexpr (MODE == kModeMoe1) {
-      if (blockIdx.x == 0) {
+      if (blockIdx.x == 0 && a.meta != nullptr) {
         for (int i = threadIdx.x; i < 1 + 9 * a.P; i += blockDim.x) {
           int v;
           if (i == 0) v = U;

@@ -680,6 +680,125 @@ extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const 
   return GGUF_OK;
 }
 
+// ---- MoeVerify / MoeDecode over the legacy split expert layouts ----
+extern "C++" {
+namespace gguf_b200 {
+namespace {
+// fc1 + fc2 on the engine's MoE modes with split-layout experts, for rows [0, R) (R <= 8,
+// R * topk <= 128); meta may be null (MoeDecode).
+template <int F>
+int run_moe_split(const void* z, const int32_t* idx, const void* fc1_w, const void* fc1_s, const void* fc2_w,
+                  const void* fc2_s, void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s) {
+  constexpr int H = 1024;
+  const int P = R * topk;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  {
+    EngineArgs a = {};
+    size_t smem = 0;
+    if ((rc = make_plan<F>(a, H, H / 32 * FmtInfo<F>::kBytes, 1, true, &smem))) return rc;
+    a.w = static_cast<const uint8_t*>(fc1_w);
+    a.sc = static_cast<const uint8_t*>(fc1_s);
+    a.rows = I;
+    a.tiles = (I + 15) / 16;
+    attach_tensor_map(a, static_cast<int64_t>(E) * I, true);
+    a.x = static_cast<const bf16*>(z);
+    a.R = R;
+    a.y = h;
+    a.post = 1.0f;
+    a.idx = idx;
+    a.topk = topk;
+    a.P = P;
+    a.E = E;
+    a.meta = meta;
+    static std::atomic<uint64_t> done{0};
+    auto kern = engine_kernel<F, 1, kKW, kModeMoe1>;
+    if ((rc = ensure_smem(kern, smem, done))) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(P) * a.tiles, sms));
+    cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
+    if (e != cudaSuccess) return cuda_fail("MoE fc1 launch", e);
+  }
+  {
+    EngineArgs a = {};
+    size_t smem = 0;
+    if ((rc = make_plan<F>(a, I, I / 32 * FmtInfo<F>::kBytes, 1, true, &smem))) return rc;
+    a.w = static_cast<const uint8_t*>(fc2_w);
+    a.sc = static_cast<const uint8_t*>(fc2_s);
+    a.rows = H;
+    a.tiles = H / 16;
+    attach_tensor_map(a, static_cast<int64_t>(E) * H, true);
+    a.x = static_cast<const bf16*>(h);
+    a.R = R;
+    a.y = part;
+    a.post = 1.0f;
+    a.idx = idx;
+    a.topk = topk;
+    a.P = P;
+    a.E = E;
+    a.meta = nullptr;
+    static std::atomic<uint64_t> done{0};
+    auto kern = engine_kernel<F, 1, kKW, kModeMoe2>;
+    if ((rc = ensure_smem(kern, smem, done))) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(P) * a.tiles, sms));
+    cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
+    if (e != cudaSuccess) return cuda_fail("MoE fc2 launch", e);
+  }
+  return GGUF_OK;
+}
+}  // namespace
+}  // namespace gguf_b200
+}  // extern "C++"
+
+extern "C" int gguf_moe_legacy(int layout, const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                               const void* fc1_s, const void* fc2_w, const void* fc2_s, void* out, void* h, float* part,
+                               int32_t* meta, int64_t R, int64_t E, int64_t I, int64_t topk, void* stream) {
+  t_last_error.clear();
+  constexpr int H = 1024;
+  const char* op = meta ? "MoeVerify" : "MoeDecode";
+  if (layout != GGUF_LAYOUT_Q4_SPLIT && layout != GGUF_LAYOUT_IQ2_CODES && layout != GGUF_LAYOUT_IQ2_NATIVE)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": expert layout must be Q4_SPLIT, IQ2_CODES or IQ2_NATIVE");
+  if (!z || !idx || !weights || !fc1_w || !fc1_s || !fc2_w || !fc2_s || !out || !h || !part)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": null tensor pointer");
+  if (topk < 1 || topk > 128 || R < 0 || R > (1 << 20) || E < 1 || E > (1 << 20))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": unsupported rows / topk / experts");
+  if (meta && (R < 1 || R > 8 || R * topk > 128))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: rows must be in [1,8] and rows*topk <= 128");
+  const int64_t imul = layout == GGUF_LAYOUT_IQ2_NATIVE ? 256 : 32;
+  if (I <= 0 || I % imul != 0 || I > (1 << 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": bad inter size (I % " + std::to_string(imul) + " == 0)");
+  if (!aligned(z, 16) || !aligned(fc1_w, 16) || !aligned(fc1_s, 16) || !aligned(fc2_w, 16) || !aligned(fc2_s, 16) ||
+      !aligned(h, 16) || !aligned(part, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": tensors must be 16-byte aligned");
+  if (R == 0) return GGUF_OK;
+  auto* s = static_cast<cudaStream_t>(stream);
+  // rows in chunks the grouped engine takes (<= 8 rows, <= 128 pairs); pair rows of h / part follow
+  const int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(8, 128 / topk));
+  for (int64_t r0 = 0; r0 < R; r0 += chunk) {
+    const int rc_rows = static_cast<int>(std::min(chunk, R - r0));
+    const auto* zc = static_cast<const bf16*>(z) + r0 * H;
+    const int32_t* ic = idx + r0 * topk;
+    void* hc = static_cast<bf16*>(h) + r0 * topk * I;
+    float* pc = part + r0 * topk * H;
+    int rc;
+    const int e = static_cast<int>(E), i = static_cast<int>(I), k = static_cast<int>(topk);
+    if (layout == GGUF_LAYOUT_Q4_SPLIT)
+      rc = run_moe_split<kFmtQ4S>(zc, ic, fc1_w, fc1_s, fc2_w, fc2_s, hc, pc, meta, rc_rows, e, i, k, s);
+    else if (layout == GGUF_LAYOUT_IQ2_CODES)
+      rc = run_moe_split<kFmtIQ2C>(zc, ic, fc1_w, fc1_s, fc2_w, fc2_s, hc, pc, meta, rc_rows, e, i, k, s);
+    else
+      rc = run_moe_split<kFmtIQ2N>(zc, ic, fc1_w, fc1_s, fc2_w, fc2_s, hc, pc, meta, rc_rows, e, i, k, s);
+    if (rc) return rc;
+  }
+  for (int64_t r0 = 0; r0 < R; r0 += 65535) {  // finalize: one CTA per row
+    const unsigned n = static_cast<unsigned>(std::min<int64_t>(65535, R - r0));
+    cudaError_t e = launch(moe_finalize_kernel, dim3(n), dim3(256), 0, s, part + r0 * topk * H, weights + r0 * topk,
+                           idx + r0 * topk, static_cast<int>(topk), H, static_cast<int>(E),
+                           static_cast<bf16*>(out) + r0 * H);
+    if (e != cudaSuccess) return cuda_fail("MoE finalize launch", e);
+  }
+  return GGUF_OK;
+}
+
 // ---- MoeVerify with library-owned scratch (no device allocation by the caller or the library) ----
 // Some callers cannot allocate device memory around this op: a host binding without a CUDA
 // allocator (a cgo / JNI / FFI caller that only holds the model's weight and activation buffers), a

@@ -185,8 +185,38 @@ void relu2(Ort::KernelContext& c, const Attrs&) {
   check(gguf_relu2(x.GetTensorRawData(), y.GetTensorMutableRawData(), count(x), stream(c)));
 }
 
+// MoeVerify iq2 = 0 / 1 / 2 and MoeDecode: experts in a split layout, scales in inputs 4 and 6.
+void moe_legacy(Ort::KernelContext& c, int layout, int64_t topk, bool verify) {
+  auto z = c.GetInput(0);
+  auto zs = shape(z);
+  const char* op = verify ? "MoeVerify" : "MoeDecode";
+  if (zs.size() != 2 || zs[1] != 1024) throw std::invalid_argument(std::string(op) + ": latent size must be 1024");
+  const int64_t R = zs[0], P = R * topk;
+  if (verify && (R < 1 || R > 8 || P > 128))
+    throw std::invalid_argument("MoeVerify: rows must be in [1,8] and rows*topk <= 128");
+  auto w1s = shape(c.GetInput(3));
+  if (w1s.size() < 2) throw std::invalid_argument(std::string(op) + ": fc1_w must be [E, I, ...]");
+  const int64_t E = w1s[0], I = w1s[1];
+  if (!present(c, 4) || !present(c, 6)) throw std::invalid_argument(std::string(op) + ": expert scales are required");
+  auto out = c.GetOutput(0, {R, 1024});
+  auto h = c.GetOutput(1, {P, I});
+  auto part = c.GetOutput(2, {P, 1024});
+  int32_t* meta = nullptr;
+  if (verify) meta = c.GetOutput(3, {1 + 9 * P}).GetTensorMutableData<int32_t>();
+  check(gguf_moe_legacy(layout, z.GetTensorRawData(), c.GetInput(1).GetTensorData<int32_t>(),
+                        c.GetInput(2).GetTensorData<float>(), c.GetInput(3).GetTensorRawData(),
+                        c.GetInput(4).GetTensorRawData(), c.GetInput(5).GetTensorRawData(),
+                        c.GetInput(6).GetTensorRawData(), out.GetTensorMutableRawData(), h.GetTensorMutableRawData(),
+                        part.GetTensorMutableData<float>(), meta, R, E, I, topk, stream(c)));
+}
+
+void moe_decode(Ort::KernelContext& c, const Attrs& a) { moe_legacy(c, GGUF_LAYOUT_Q4_SPLIT, a.topk, false); }
+
 void moe_verify(Ort::KernelContext& c, const Attrs& a) {
-  if (a.iq2 != 3) throw NotImplemented("MoeVerify: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented");
+  if (a.iq2 == 0) return moe_legacy(c, GGUF_LAYOUT_Q4_SPLIT, a.topk, true);
+  if (a.iq2 == 1) return moe_legacy(c, GGUF_LAYOUT_IQ2_CODES, a.topk, true);
+  if (a.iq2 == 2) return moe_legacy(c, GGUF_LAYOUT_IQ2_NATIVE, a.topk, true);
+  if (a.iq2 != 3) throw NotImplemented("MoeVerify: unknown iq2 value");
   auto z = c.GetInput(0);
   auto zs = shape(z);
   if (zs.size() != 2) throw std::invalid_argument("MoeVerify: z must be [R, 1024]");
@@ -256,7 +286,7 @@ const std::vector<OpDesc>& op_table() {
        nullptr},
       {"MoeRoute", {kBF, kBF, kF32}, {kI32, kF32, kF32}, {}, route_bf16},
       {"MoeRouteGGUF", {kBF, kF32, kF32}, {kI32, kF32, kF32}, {}, route_gguf},
-      {"MoeDecode", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32}, {}, nullptr},
+      {"MoeDecode", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32}, {}, moe_decode},
       {"MoeVerify", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32, kI32}, {4, 6}, moe_verify},
       {"Relu2", {kBF}, {kBF}, {}, relu2},
       {"Nvfp4Gemv", {kBF, kU8, kU8, kF32}, {kBF}, {2}, fp4_gemv},

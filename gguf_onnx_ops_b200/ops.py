@@ -16,6 +16,8 @@ C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
     MoeRoute(x, gate_w_bf16, bias, topk, scale)        -> idx, weights, scores    src/bolt_ops.cu:513-547, :1947
     MoeVerify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s=None, topk, iq2=3) -> out, h, part, meta
                                                                    src/bolt_ops.cu:1327-1409, :1981-1996
+    MoeDecode(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk)            -> out, h, part
+                                                                   src/bolt_ops.cu:664-699, :1967-1980
 
 Every weight layout of the GEMVs is implemented: the GGUF ones (``gguf=1`` / ``iq2=3``) and the
 legacy split layouts (``gguf=0``, ``iq2`` in 0..2, through ``gguf_gemv_legacy``).  The lower-level
@@ -293,13 +295,58 @@ def moe_verify_into(z, idx, w, fc1_w, fc2_w, out, h, part, meta, R, E, I, topk, 
                                          _ptr(part), _ptr(meta), R, E, I, topk, _stream(stream)))
 
 
+def moe_legacy_into(layout, z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, out, h, part, meta, R, E, I, topk,
+                    stream=None) -> None:
+    check(load().gguf_moe_legacy(layout, _ptr(z), _ptr(idx), _ptr(w), _ptr(fc1_w), _ptr(fc1_s), _ptr(fc2_w),
+                                 _ptr(fc2_s), _ptr(out), _ptr(h), _ptr(part), _ptr(meta), R, E, I, topk,
+                                 _stream(stream)))
+
+
+_MOE_LAYOUTS = {0: _lib.GGUF_LAYOUT_Q4_SPLIT, 1: _lib.GGUF_LAYOUT_IQ2_CODES, 2: _lib.GGUF_LAYOUT_IQ2_NATIVE}
+
+
+def _moe_legacy(op, z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, iq2, with_meta):
+    for t, n, dt in ((z, "z", torch.bfloat16), (idx, "idx", torch.int32), (w, "weights", torch.float32),
+                     (fc1_w, "fc1_w", torch.uint8), (fc1_s, "fc1_s", torch.bfloat16), (fc2_w, "fc2_w", torch.uint8),
+                     (fc2_s, "fc2_s", torch.bfloat16)):
+        _need(t, n, dt, op)
+    R = z.shape[0]
+    P = R * topk
+    if with_meta and (R < 1 or R > 8 or P > 128):
+        raise ValueError("MoeVerify: rows must be in [1,8] and rows*topk <= 128")
+    if z.shape[1] != 1024:
+        raise ValueError(f"{op}: latent size must be 1024")
+    E, I = fc1_w.shape[0], fc1_w.shape[1]
+    per32 = 8 if iq2 == 2 else 16
+    gsz = 256 if iq2 == 2 else 32
+    if I % gsz != 0 or fc1_w.numel() != E * I * 32 * per32 or fc2_w.numel() != E * 1024 * (I // 32) * per32 \
+            or fc1_s.numel() != E * I * (1024 // gsz) or fc2_s.numel() != E * 1024 * (I // gsz):
+        raise ValueError(f"{op}: bad inter size")
+    out = torch.empty(R, 1024, dtype=torch.bfloat16, device=z.device)
+    h = torch.empty(P, I, dtype=torch.bfloat16, device=z.device)
+    part = torch.empty(P, 1024, dtype=torch.float32, device=z.device)
+    meta = torch.empty(1 + P + P * 8, dtype=torch.int32, device=z.device) if with_meta else None
+    moe_legacy_into(_MOE_LAYOUTS[iq2], z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, out, h, part, meta, R, E, I, topk)
+    return (out, h, part, meta) if with_meta else (out, h, part)
+
+
+def MoeDecode(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, *, topk: int):
+    """relu^2 MoE over 4-bit experts fc1_w [E, I, 512] / fc2_w [E, 1024, I/2] with bf16 scales per 32
+    (src/bolt_ops.cu:664-699).  Returns (out [R,1024] bf16, h [R*topk, I] bf16, part [R*topk, 1024] f32)."""
+    return _moe_legacy("MoeDecode", z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, 0, False)
+
+
 def MoeVerify(z, idx, w, fc1_w, fc1_s=None, fc2_w=None, fc2_s=None, *, topk: int, iq2: int = 3):
-    """Expert-grouped relu^2 MoE over raw GGUF IQ2_XXS expert tensors (iq2=3).
+    """Expert-grouped relu^2 MoE.  iq2=3: raw GGUF IQ2_XXS expert tensors; iq2=0: 4-bit experts with
+    bf16 scales (as MoeDecode); iq2=1: 3-bit IQ2 codes; iq2=2: IQ2_XXS records + fp16 d
+    (src/bolt_ops.cu:1327-1409).
 
     Returns (out [R,1024] bf16, h [R*topk, I] bf16, part [R*topk, 1024] f32, meta [1 + 9*R*topk] i32).
     """
+    if iq2 in (0, 1, 2):
+        return _moe_legacy("MoeVerify", z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, iq2, True)
     if iq2 != 3:
-        raise NotImplementedError("MoeVerify: only the raw GGUF IQ2_XXS layout (iq2=3) is implemented")
+        raise NotImplementedError(f"MoeVerify: unknown iq2={iq2}")
     _need(z, "z", torch.bfloat16, "MoeVerify")
     _need(idx, "idx", torch.int32, "MoeVerify")
     _need(w, "weights", torch.float32, "MoeVerify")

@@ -97,6 +97,21 @@ GGUF_OPS_API int gguf_gemv_legacy(int layout, const void* x, const void* w, cons
                                   void* y, int64_t R, int64_t N, int64_t K, void* stream);
 
 /*
+ * MoeVerify iq2 = 0 / 1 / 2 and MoeDecode (src/bolt_ops.cu:664-699, :1327-1409): the relu^2 MoE of
+ * gguf_moe_verify_iq2_xxs over experts in a legacy split layout (layout GGUF_LAYOUT_Q4_SPLIT for
+ * iq2=0 and MoeDecode, GGUF_LAYOUT_IQ2_CODES for iq2=1, GGUF_LAYOUT_IQ2_NATIVE for iq2=2):
+ *   fc1_w [E, I, 1024/32 * b] + fc1_s [E, I, 1024/g], fc2_w [E, 1024, I/32 * b] + fc2_s [E, 1024, I/g]
+ *   (b = 16 bytes per 32 and g = 32 bf16 scales for Q4 / codes; b = 8 and g = 256 fp16 d for native).
+ * h bf16 [R*topk, I], part f32 [R*topk, 1024], out bf16 [R, 1024]; meta i32 [1 + 9*R*topk] (the
+ * grouping table, MoeVerify) or NULL (MoeDecode, any R: rows are processed in groups of <= 8).
+ * I % 32 == 0 (native: % 256); MoeVerify: 1 <= R <= 8, R*topk <= 128.
+ */
+GGUF_OPS_API int gguf_moe_legacy(int layout, const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                                 const void* fc1_s, const void* fc2_w, const void* fc2_s, void* out, void* h,
+                                 float* part, int32_t* meta, int64_t R, int64_t E, int64_t I, int64_t topk,
+                                 void* stream);
+
+/*
  * Q8Embed:  out[..., k] = bf16(fp32(d) * q[k]) of the rows input_ids[...] of a GGUF Q8_0 embedding
  * table w [vocab, row_bytes] (row_bytes = (K/32)*34); ids outside [0, vocab) read row 0.
  * ids: int64 [R] (any shape, flattened); out: bf16 [R, K].  R = 0 is a no-op.

@@ -33,6 +33,21 @@ def test_library_exports_every_declared_symbol(lib):
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
 
 
+def declared_arg_counts():
+    """name -> number of parameters, from the prototypes in include/*.h."""
+    src = "".join(open(h).read() for h in HEADERS)
+    out = {}
+    for m in re.finditer(r"GGUF_OPS_API\s+[\w\s\*]+?\b(gguf_\w+)\s*\(([^)]*)\)", src):
+        args = m.group(2).strip()
+        out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_header_arity():
+    for name, n in declared_arg_counts().items():
+        assert len(_lib.SIGNATURES[name][1]) == n, f"{name}: header has {n} parameters"
+
+
 def test_version(lib):
     assert b"sm_100a" in lib.gguf_version()
 
