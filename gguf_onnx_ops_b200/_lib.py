@@ -36,6 +36,7 @@ SIGNATURES = {
     "gguf_nvfp4_gemv": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_gemv_legacy": (_I32, [_I32, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_moe_legacy": (_I32, [_I32] + [_P] * 11 + [_I64, _I64, _I64, _I64, _P]),
+    "gguf_mamba_step": (_I32, [_P] * 5 + [_I32] + [_P] * 10 + [_I64] * 6 + [_F32, _F32, _P]),
     "gguf_q8_0_embed": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_rms_norm": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _F32, _P]),
     "gguf_moe_route": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),

@@ -24,6 +24,7 @@ enum DeviceErrorSite : int {
   kSiteEmptyWait = 2,    // producer waited too long for a free stage
   kSiteDrainWait = 3,    // producer waited too long for its last copies at exit
   kSitePeerWait = 5,     // a sharded op waited too long for a peer GPU's completion flag
+  kSiteBadStateRow = 6,  // MambaVerify: the device-side state row was outside [0, state_rows) (row 0 used)
 };
 
 // A wait on an mbarrier that has not completed after this many nanoseconds is treated as a fault:

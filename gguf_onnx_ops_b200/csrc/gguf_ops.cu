@@ -23,6 +23,7 @@
 #include "moe_fused.cuh"
 #include "small_kernels.cuh"
 #include "rms_norm.cuh"
+#include "mamba.cuh"
 
 namespace gguf_b200 {
 
@@ -1037,6 +1038,59 @@ int gguf_gemv_legacy(int layout, const void* x, const void* w, const void* scale
       return R <= 8 ? run_dense_split<kFmtFP4S, 1>(x, w, scales, gscale, y, r, n, k, s)
                     : run_dense_split<kFmtFP4S, 2>(x, w, scales, gscale, y, r, n, k, s);
   }
+}
+
+int gguf_mamba_step(const void* proj, const void* conv_state, const float* ssm_state, const void* conv_w,
+                    const void* conv_b, int conv_w_f32, const float* dt_bias, const float* a_neg, const float* d_skip,
+                    const float* norm_w, const int32_t* state_row, void* y, void* conv_state_out,
+                    float* ssm_state_out, void* xbc_act, float* ypre, int64_t R, int64_t state_rows, int64_t heads,
+                    int64_t head_dim, int64_t d_state, int64_t n_groups, float eps, float time_step_min,
+                    void* stream) {
+  t_last_error.clear();
+  const std::string op = state_row ? "MambaVerify" : "MambaStep";
+  if (head_dim != kMambaHD || d_state != kMambaDS)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": only head_dim=64, d_state=128 are implemented");
+  if (heads < 1 || heads > 4096 || n_groups < 1 || heads % n_groups != 0)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": heads must be a positive multiple of n_groups");
+  if (R < 1 || R > kMambaMaxRows) return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": rows must be in [1,16]");
+  if (state_row && state_rows < R) return fail(GGUF_ERR_INVALID_ARGUMENT, "MambaVerify: state buffer needs >= R rows");
+  if (!proj || !conv_state || !ssm_state || !conv_w || !conv_b || !dt_bias || !a_neg || !d_skip || !norm_w || !y ||
+      !conv_state_out || !ssm_state_out || !xbc_act || !ypre)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": null tensor pointer");
+  if (!aligned(conv_w, conv_w_f32 ? 16 : 8) || !aligned(ssm_state, 4) || !aligned(proj, 2))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, op + ": conv weights must be aligned to one 4-tap row");
+  MambaArgs a = {};
+  a.proj = static_cast<const bf16*>(proj);
+  a.R = static_cast<int>(R);
+  a.di = static_cast<int>(heads * kMambaHD);
+  a.cd = a.di + static_cast<int>(2 * n_groups * kMambaDS);
+  a.proj_stride = a.di + a.cd + static_cast<int>(heads);
+  a.heads = static_cast<int>(heads);
+  a.hpg = static_cast<int>(heads / n_groups);
+  a.ng = static_cast<int>(n_groups);
+  a.conv_in = static_cast<const bf16*>(conv_state);
+  a.conv_w = conv_w;
+  a.conv_b = conv_b;
+  a.conv_out = static_cast<bf16*>(conv_state_out);
+  a.xbc = static_cast<bf16*>(xbc_act);
+  a.ssm_in = ssm_state;
+  a.dt_bias = dt_bias;
+  a.a_neg = a_neg;
+  a.d_skip = d_skip;
+  a.tmin = time_step_min;
+  a.ssm_out = ssm_state_out;
+  a.ypre = ypre;
+  a.state_row = state_row;
+  a.state_rows = static_cast<int>(std::min<int64_t>(state_rows, 1 << 30));
+  auto* s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch(conv_w_f32 ? mamba_conv_ssm_kernel<true> : mamba_conv_ssm_kernel<false>,
+                         dim3(static_cast<unsigned>(heads)), dim3(kMambaThreads), 0, s, a);
+  if (e != cudaSuccess) return cuda_fail((op + " launch").c_str(), e);
+  e = launch(mamba_norm_kernel, dim3(static_cast<unsigned>(R), static_cast<unsigned>(n_groups)), dim3(256), 0, s,
+             a.proj, a.proj_stride, a.di, static_cast<int>(a.di / n_groups), eps, static_cast<const float*>(ypre),
+             norm_w, static_cast<bf16*>(y));
+  if (e != cudaSuccess) return cuda_fail((op + " norm launch").c_str(), e);
+  return GGUF_OK;
 }
 
 int gguf_rms_norm(const void* x, const void* skip, const float* gamma, void* y, void* sum, int64_t R, int64_t H,

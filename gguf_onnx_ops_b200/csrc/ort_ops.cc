@@ -37,6 +37,8 @@ struct NotImplemented : std::runtime_error {
 struct Attrs {
   int64_t gguf = 0, iq2 = 0, topk = 0;
   float scale = 1.0f, epsilon = 1e-5f;
+  int64_t heads = 0, head_dim = 0, d_state = 0, n_groups = 0;  // Mamba*
+  float time_step_min = 0.0f;
 };
 
 int64_t opt_int(const OrtKernelInfo* info, const char* name, int64_t dflt) {
@@ -276,14 +278,42 @@ void rms_norm(Ort::KernelContext& c, const Attrs& a) {
                       stream(c)));
 }
 
+// Mamba*: 9 inputs (+ state_row for Verify), 5 outputs shaped as the reference (src/bolt_ops.cu:319-370).
+template <bool kVerify, bool kF32W>
+void mamba(Ort::KernelContext& c, const Attrs& a) {
+  auto proj = c.GetInput(0);
+  auto ps = shape(proj);
+  if (ps.size() != 2) throw std::invalid_argument("MambaStep: proj must be [R, width]");
+  const int64_t R = ps[0], di = a.heads * a.head_dim, cd = di + 2 * a.n_groups * a.d_state;
+  if (R < 1 || R > 16) throw std::invalid_argument("MambaStep: rows must be in [1,16]");
+  if (ps[1] != di + cd + a.heads) throw std::invalid_argument("MambaStep: bad proj width");
+  const auto cs = shape(c.GetInput(1)), ss = shape(c.GetInput(2));
+  if (cs.empty()) throw std::invalid_argument("MambaStep: bad conv state");
+  auto y = c.GetOutput(0, {R, di});
+  auto conv_out = c.GetOutput(1, cs);
+  auto ssm_out = c.GetOutput(2, ss);
+  auto xbc = c.GetOutput(3, {R, cd});
+  auto ypre = c.GetOutput(4, {R, di});
+  check(gguf_mamba_step(proj.GetTensorRawData(), c.GetInput(1).GetTensorRawData(), c.GetInput(2).GetTensorData<float>(),
+                        c.GetInput(3).GetTensorRawData(), c.GetInput(4).GetTensorRawData(), kF32W ? 1 : 0,
+                        c.GetInput(5).GetTensorData<float>(), c.GetInput(6).GetTensorData<float>(),
+                        c.GetInput(7).GetTensorData<float>(), c.GetInput(8).GetTensorData<float>(),
+                        kVerify ? c.GetInput(9).GetTensorData<int32_t>() : nullptr, y.GetTensorMutableRawData(),
+                        conv_out.GetTensorMutableRawData(), ssm_out.GetTensorMutableData<float>(),
+                        xbc.GetTensorMutableRawData(), ypre.GetTensorMutableData<float>(), R, cs[0], a.heads,
+                        a.head_dim, a.d_state, a.n_groups, a.epsilon, a.time_step_min, stream(c)));
+}
+
 // Names, signatures and optional inputs of the reference's 15 ops (src/bolt_ops.cu:1886-2061).
 const std::vector<OpDesc>& op_table() {
   static const std::vector<OpDesc> t = {
-      {"MambaStep", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {}, nullptr},
-      {"MambaStepGGUF", {kBF, kBF, kF32, kF32, kF32, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {}, nullptr},
-      {"MambaVerify", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {}, nullptr},
+      {"MambaStep", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {}, mamba<false, false>},
+      {"MambaStepGGUF", {kBF, kBF, kF32, kF32, kF32, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {},
+       mamba<false, true>},
+      {"MambaVerify", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {},
+       mamba<true, false>},
       {"MambaVerifyGGUF", {kBF, kBF, kF32, kF32, kF32, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {},
-       nullptr},
+       mamba<true, true>},
       {"MoeRoute", {kBF, kBF, kF32}, {kI32, kF32, kF32}, {}, route_bf16},
       {"MoeRouteGGUF", {kBF, kF32, kF32}, {kI32, kF32, kF32}, {}, route_gguf},
       {"MoeDecode", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32}, {}, moe_decode},
@@ -345,6 +375,11 @@ struct GgufOp : Ort::CustomOpBase<GgufOp, GgufKernel, true> {
       k->a.topk = opt_int(info, "topk", 0);
       k->a.scale = opt_float(info, "scale", 1.0f);
       k->a.epsilon = opt_float(info, "epsilon", 1e-5f);
+      k->a.heads = opt_int(info, "heads", 0);
+      k->a.head_dim = opt_int(info, "head_dim", 0);
+      k->a.d_state = opt_int(info, "d_state", 0);
+      k->a.n_groups = opt_int(info, "n_groups", 0);
+      k->a.time_step_min = opt_float(info, "time_step_min", 0.0f);
       *kernel = k;
       return nullptr;
     } catch (const std::exception& e) {

@@ -18,6 +18,8 @@ C ABI of libgguf_onnx_ops.so on the current torch CUDA stream.
                                                                    src/bolt_ops.cu:1327-1409, :1981-1996
     MoeDecode(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk)            -> out, h, part
                                                                    src/bolt_ops.cu:664-699, :1967-1980
+    MambaStep / MambaStepGGUF / MambaVerify / MambaVerifyGGUF       -> y, conv_state, ssm_state, xbc, ypre
+                                                                   src/bolt_ops.cu:68-378, :1886-1946
 
 Every weight layout of the GEMVs is implemented: the GGUF ones (``gguf=1`` / ``iq2=3``) and the
 legacy split layouts (``gguf=0``, ``iq2`` in 0..2, through ``gguf_gemv_legacy``).  The lower-level
@@ -368,6 +370,80 @@ def MoeVerify(z, idx, w, fc1_w, fc1_s=None, fc2_w=None, fc2_s=None, *, topk: int
     meta = torch.empty(1 + P + P * 8, dtype=torch.int32, device=z.device)
     moe_verify_into(z, idx, w, fc1_w, fc2_w, out, h, part, meta, R, E, I, topk)
     return out, h, part, meta
+
+
+# ------------------------------------------------------------------------------------------------
+# Mamba
+# ------------------------------------------------------------------------------------------------
+def mamba_step_into(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, state_row, y,
+                    conv_out, ssm_out, xbc, ypre, *, R, state_rows, heads, n_groups, eps, tmin, stream=None) -> None:
+    f32w = 1 if conv_w.dtype == torch.float32 else 0
+    check(load().gguf_mamba_step(_ptr(proj), _ptr(conv_state), _ptr(ssm_state), _ptr(conv_w), _ptr(conv_b), f32w,
+                                 _ptr(dt_bias), _ptr(a_neg), _ptr(d_skip), _ptr(norm_w), _ptr(state_row), _ptr(y),
+                                 _ptr(conv_out), _ptr(ssm_out), _ptr(xbc), _ptr(ypre), R, state_rows, heads, 64, 128,
+                                 n_groups, eps, tmin, _stream(stream)))
+
+
+def _mamba(op, proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, D, norm_w, state_row, *, heads, head_dim,
+           d_state, n_groups, epsilon, time_step_min, gguf):
+    wdt = torch.float32 if gguf else torch.bfloat16
+    for t, n, dt in ((proj, "proj", torch.bfloat16), (conv_state, "conv_state", torch.bfloat16),
+                     (ssm_state, "ssm_state", torch.float32), (conv_w, "conv_w", wdt), (conv_b, "conv_b", wdt),
+                     (dt_bias, "dt_bias", torch.float32), (a_neg, "A_neg", torch.float32), (D, "D", torch.float32),
+                     (norm_w, "norm_w", torch.float32)):
+        _need(t, n, dt, op)
+    if head_dim != 64 or d_state != 128:
+        raise ValueError("MambaStep: only head_dim=64, d_state=128 are implemented")
+    R = proj.shape[0]
+    if R < 1 or R > 16:
+        raise ValueError("MambaStep: rows must be in [1,16]")
+    di = heads * head_dim
+    cd = di + 2 * n_groups * d_state
+    if proj.shape[1] != di + cd + heads:
+        raise ValueError("MambaStep: bad proj width")
+    if state_row is not None:
+        _need(state_row, "state_row", torch.int32, op)
+        if conv_state.shape[0] < R:
+            raise ValueError("MambaVerify: state buffer needs >= R rows")
+    dev = proj.device
+    y = torch.empty(R, di, dtype=torch.bfloat16, device=dev)
+    conv_out = torch.empty_like(conv_state)
+    ssm_out = torch.empty_like(ssm_state)
+    xbc = torch.empty(R, cd, dtype=torch.bfloat16, device=dev)
+    ypre = torch.empty(R, di, dtype=torch.float32, device=dev)
+    mamba_step_into(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, D, norm_w, state_row, y, conv_out,
+                    ssm_out, xbc, ypre, R=R, state_rows=conv_state.shape[0], heads=heads, n_groups=n_groups,
+                    eps=epsilon, tmin=time_step_min)
+    return y, conv_out, ssm_out, xbc, ypre
+
+
+def MambaStep(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, *, heads, head_dim=64,
+              d_state=128, n_groups, epsilon=1e-5, time_step_min=0.0):
+    """One Mamba-2 mixer step (src/bolt_ops.cu:304-378).  Returns (y, conv_state_out, ssm_state_out,
+    xbc_act, ypre)."""
+    return _mamba("MambaStep", proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, None,
+                  heads=heads, head_dim=head_dim, d_state=d_state, n_groups=n_groups, epsilon=epsilon,
+                  time_step_min=time_step_min, gguf=False)
+
+
+def MambaStepGGUF(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, **attrs):
+    """MambaStep with fp32 GGUF conv weights / bias (rounded to bf16 on use)."""
+    return _mamba("MambaStepGGUF", proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, None,
+                  gguf=True, **{"head_dim": 64, "d_state": 128, "epsilon": 1e-5, "time_step_min": 0.0, **attrs})
+
+
+def MambaVerify(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, state_row, **attrs):
+    """MambaStep over R speculative tokens from state row *state_row; the state after token r is
+    row r of the outputs (src/bolt_ops.cu:1915-1933)."""
+    return _mamba("MambaVerify", proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, state_row,
+                  gguf=False, **{"head_dim": 64, "d_state": 128, "epsilon": 1e-5, "time_step_min": 0.0, **attrs})
+
+
+def MambaVerifyGGUF(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w, state_row, **attrs):
+    """MambaVerify with fp32 GGUF conv weights / bias."""
+    return _mamba("MambaVerifyGGUF", proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, A_neg, D, norm_w,
+                  state_row, gguf=True,
+                  **{"head_dim": 64, "d_state": 128, "epsilon": 1e-5, "time_step_min": 0.0, **attrs})
 
 
 # ------------------------------------------------------------------------------------------------

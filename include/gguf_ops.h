@@ -112,6 +112,27 @@ GGUF_OPS_API int gguf_moe_legacy(int layout, const void* z, const int32_t* idx, 
                                  void* stream);
 
 /*
+ * MambaStep / MambaVerify / MambaStepGGUF / MambaVerifyGGUF (src/bolt_ops.cu:68-378, :1886-1946):
+ * one Mamba-2 mixer step after the input projection, for R <= 16 rows (tokens).
+ *   proj bf16 [R, di + cd + heads] = [gate | xBC | dt], di = heads * 64, cd = di + 2 * n_groups * 128;
+ *   conv_state bf16 [Rs, cd, 3]; ssm_state f32 [Rs, heads, 128, 64]; conv_w [cd, 4] and conv_b [cd]
+ *   as bf16 (conv_w_f32 = 0) or fp32 rounded to bf16 on use (conv_w_f32 = 1, the GGUF ops);
+ *   dt_bias, a_neg, d_skip f32 [heads]; norm_w f32 [di].
+ * state_row == NULL (Step): the step starts from row 0 and the state after the last row is written
+ * to conv_state_out [1, cd, 3] / ssm_state_out [1, heads, 128, 64].  state_row != NULL (Verify): a
+ * device int32 selecting the input row of the [Rs >= R, ...] buffers; the state after token r goes
+ * to row r of the outputs (a row outside [0, Rs) is read as row 0 and reported by
+ * gguf_device_status).  Outputs: y bf16 [R, di], xbc_act bf16 [R, cd], ypre f32 [R, di].  Outputs
+ * must not alias the state inputs.  head_dim must be 64 and d_state 128 (the reference's limit).
+ */
+GGUF_OPS_API int gguf_mamba_step(const void* proj, const void* conv_state, const float* ssm_state, const void* conv_w,
+                                 const void* conv_b, int conv_w_f32, const float* dt_bias, const float* a_neg,
+                                 const float* d_skip, const float* norm_w, const int32_t* state_row, void* y,
+                                 void* conv_state_out, float* ssm_state_out, void* xbc_act, float* ypre, int64_t R,
+                                 int64_t state_rows, int64_t heads, int64_t head_dim, int64_t d_state,
+                                 int64_t n_groups, float eps, float time_step_min, void* stream);
+
+/*
  * Q8Embed:  out[..., k] = bf16(fp32(d) * q[k]) of the rows input_ids[...] of a GGUF Q8_0 embedding
  * table w [vocab, row_bytes] (row_bytes = (K/32)*34); ids outside [0, vocab) read row 0.
  * ids: int64 [R] (any shape, flattened); out: bf16 [R, K].  R = 0 is a no-op.

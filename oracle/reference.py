@@ -11,6 +11,9 @@
   outside [0, vocab) reading row 0 (``src/bolt_ops.cu:1645-1660``, ``:1674-1687``).
 * ``rms_norm_ref`` -- RmsNorm / SkipRmsNorm: v = x or bf16(x + skip), y = bf16(bf16(gamma) * v *
   rsqrt(mean(v^2) + eps)) (``src/bolt_ops.cu:1692-1815``); mean in fp64, products in fp32.
+* ``mamba_ref``  -- MambaStep: 4-tap causal conv + silu (activations rounded to bf16), the Mamba-2
+  state recurrence and the gated group norm (``tests/test_bolt_ops.py:389-413``,
+  ``src/bolt_ops.cu:68-301``), in fp64 from the bf16 / fp32 inputs.
 * ``rel_l2``    -- the reference's metric ``||a-b|| / ||b||`` (``tests/test_bolt_ops.py:62-64``).
 """
 
@@ -115,3 +118,49 @@ def route_ref(x, gate_w: np.ndarray, bias: np.ndarray, topk: int, scale: float, 
         vs = np.take_along_axis(val, order, axis=1)
         near = (vs[:, topk - 1] - vs[:, topk]) < tie_eps
     return idx, weights, scores, near
+
+
+def _silu(v):
+    return v / (1.0 + np.exp(-v))
+
+
+def mamba_ref(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, heads: int, n_groups: int,
+              eps: float, tmin: float, hd: int = 64, ds: int = 128):
+    """One MambaStep over R rows from one state.
+
+    proj: [R, di + cd + heads] bf16 bits; conv_state: [cd, 3] bf16 bits; ssm_state: f32 [heads, ds, hd];
+    conv_w: f32 [cd, 4] and conv_b f32 [cd] (bf16 values); dt_bias, a_neg, d_skip f32 [heads]; norm_w
+    f32 [di].  Returns per-row lists: (y [R, di] fp64 before bf16 rounding, xbc [R, cd] fp32 holding
+    bf16 values, ypre [R, di], conv_states [R] of [cd, 3], ssm_states [R] of [heads, ds, hd])."""
+    pf = _x_f32(proj).astype(np.float64)
+    R = pf.shape[0]
+    di = heads * hd
+    cd = di + 2 * n_groups * ds
+    gate, xbc_in, dt = pf[:, :di], pf[:, di:di + cd], pf[:, di + cd:]
+    inp = np.concatenate([_x_f32(conv_state).astype(np.float64).T, xbc_in], 0)  # [3 + R, cd]
+    w = np.asarray(conv_w, np.float64)
+    b = np.asarray(conv_b, np.float64)
+    xbc = np.zeros((R, cd), np.float32)
+    for r in range(R):
+        acc = (inp[r:r + 4] * w.T).sum(0) + b
+        xbc[r] = bf16_round(_silu(acc).astype(np.float32))
+    conv_states = [inp[r + 1:r + 4].T.copy() for r in range(R)]
+    xs, Bm, Cm = xbc[:, :di], xbc[:, di:di + n_groups * ds], xbc[:, di + n_groups * ds:]
+    st = np.asarray(ssm_state, np.float64).copy()
+    hpg = heads // n_groups
+    ypre = np.zeros((R, di))
+    states = []
+    for r in range(R):
+        raw = dt[r] + np.asarray(dt_bias, np.float64)
+        dts = np.maximum(np.where(raw > 20.0, raw, np.log1p(np.exp(np.minimum(raw, 20.0)))), tmin)
+        dA = np.exp(np.asarray(a_neg, np.float64) * dts)
+        xh = xs[r].astype(np.float64).reshape(heads, hd)
+        Bh = np.repeat(Bm[r].astype(np.float64).reshape(n_groups, ds), hpg, 0)
+        Ch = np.repeat(Cm[r].astype(np.float64).reshape(n_groups, ds), hpg, 0)
+        st = st * dA[:, None, None] + (dts[:, None] * xh)[:, None, :] * Bh[:, :, None]
+        ypre[r] = ((st * Ch[:, :, None]).sum(1) + np.asarray(d_skip, np.float64)[:, None] * xh).reshape(di)
+        states.append(st.copy())
+    v = (ypre * _silu(gate)).reshape(R, n_groups, di // n_groups)
+    v = v / np.sqrt((v ** 2).mean(-1, keepdims=True) + eps)
+    y = v.reshape(R, di) * np.asarray(norm_w, np.float64)
+    return y, xbc, ypre, conv_states, states

@@ -13,6 +13,7 @@ Every expected value here comes from the reference's own CPU path, not from the 
 * Q8Embed output: the harness's torch expression (tests/test_bolt_ops.py:310-311) with ids outside
   [0, vocab) replaced by row 0, the op's rule (src/bolt_ops.cu:1680);
 * RmsNorm / SkipRmsNorm outputs: the harness's torch expressions (tests/test_bolt_ops.py:321-337);
+* MambaStep outputs: the harness's torch reference loop (tests/test_bolt_ops.py:389-413) at heads=4;
 * the IQ2_XXS codebook: parsed from the reference's src/iq2xxs_grid.h (kIq2xxsGrid, line 6, and
   kIq2xxsGridBf16, line 75).
 
@@ -38,7 +39,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from oracle import inputs as I  # noqa: E402  (input builders only; expected values come from gguf/torch)
-from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, norm_inputs, route_inputs, sha  # noqa: E402
+from tests.golden.cases import (GEMV_CASES, embed_inputs, mamba_inputs, moe_inputs, norm_inputs,  # noqa: E402
+                                route_inputs, sha)
 
 
 def gguf_deq(raw: np.ndarray, qt) -> np.ndarray:
@@ -90,13 +92,52 @@ def make_norm():
     np.savez_compressed(os.path.join(HERE, "norm.npz"), **cases)
 
 
+def make_mamba():
+    m = mamba_inputs()
+    heads, ng, hd, ds = m["heads"], m["n_groups"], 64, 128
+    di = heads * hd
+    cd = di + 2 * ng * ds
+    R = m["proj"].shape[0]
+    proj = bf16_tensor(m["proj"])
+    cst = bf16_tensor(m["cst"])
+    sst = torch.from_numpy(m["sst"])
+    cw = torch.from_numpy(m["cw"]).reshape(cd, 1, 4).bfloat16()
+    cb = torch.from_numpy(m["cb"]).bfloat16()
+    dtb, an, D, nw = (torch.from_numpy(m[k]) for k in ("dtb", "an", "D", "nw"))
+    gate, xbc, dt = proj.split([di, cd, heads], -1)
+    inp = torch.cat([cst[0].T.float(), xbc.float()], 0)
+    conv = torch.zeros(R, cd)
+    for r in range(R):
+        win = inp[r:r + 4]
+        conv[r] = torch.nn.functional.silu((win * cw[:, 0, :].T.float()).sum(0) + cb.float())
+    conv = conv.bfloat16().float()
+    xs, Bm, Cm = conv.split([di, ng * ds, ng * ds], -1)
+    st = sst[0].clone()
+    ys = []
+    for r in range(R):
+        dts = torch.clamp(torch.nn.functional.softplus(dt[r].float() + dtb), min=m["tmin"])
+        dA = torch.exp(an * dts)
+        xh = xs[r].reshape(heads, hd)
+        Bh = Bm[r].reshape(ng, ds).repeat_interleave(heads // ng, 0)
+        Ch = Cm[r].reshape(ng, ds).repeat_interleave(heads // ng, 0)
+        st = st * dA[:, None, None] + (dts[:, None] * xh)[:, None, :] * Bh[:, :, None]
+        ys.append((st * Ch[:, :, None]).sum(1) + D[:, None] * xh)
+    yp = torch.stack(ys).reshape(R, di)
+    g = (yp * torch.nn.functional.silu(gate.float())).reshape(R, ng, di // ng)
+    g = g * torch.rsqrt(g.pow(2).mean(-1, keepdim=True) + m["eps"])
+    y = g.reshape(R, di) * nw
+    np.savez_compressed(os.path.join(HERE, "mamba.npz"), y=y.numpy(), ssm=st.numpy(),
+                        conv=inp[-3:].T.contiguous().bfloat16().view(torch.int16).numpy().view(np.uint16),
+                        sha=np.array(sha(*(m[k] for k in ("proj", "cst", "sst", "cw", "cb", "dtb", "an", "D", "nw")))))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", choices=["embed", "norm"], default=None)
+    ap.add_argument("--only", choices=["embed", "norm", "mamba"], default=None)
     args = ap.parse_args()
     if args.only:
-        {"embed": make_embed, "norm": make_norm}[args.only]()
+        {"embed": make_embed, "norm": make_norm, "mamba": make_mamba}[args.only]()
         return
     from gguf import GGMLQuantizationType as Q
 
@@ -164,6 +205,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "moe.npz"), out=ref.numpy(), sha=np.array(sha(z, idx, wts, b1, b2)))
     make_embed()
     make_norm()
+    make_mamba()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

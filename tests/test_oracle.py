@@ -7,7 +7,7 @@ import torch
 
 import oracle as O
 from oracle import inputs as I
-from tests.golden.cases import GEMV_CASES, embed_inputs, moe_inputs, norm_inputs, route_inputs, sha
+from tests.golden.cases import GEMV_CASES, embed_inputs, mamba_inputs, moe_inputs, norm_inputs, route_inputs, sha
 from tests.util import rel
 
 
@@ -193,6 +193,18 @@ def test_legacy_dequant_matches_harness_expressions(layout):
 def test_e4m3fn_table_matches_torch():
     ref = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
     assert np.array_equal(O.e4m3fn_table(), ref, equal_nan=True)
+
+
+def test_mamba_ref_matches_golden(golden):
+    d = golden("mamba.npz")
+    m = mamba_inputs()
+    assert sha(*(m[k] for k in ("proj", "cst", "sst", "cw", "cb", "dtb", "an", "D", "nw"))) == str(d["sha"])
+    y, xbc, ypre, conv_states, states = O.mamba_ref(m["proj"], m["cst"][0], m["sst"][0], m["cw"], m["cb"], m["dtb"],
+                                                    m["an"], m["D"], m["nw"], m["heads"], m["n_groups"], m["eps"],
+                                                    m["tmin"])
+    assert rel(y, d["y"]) < 1e-5  # fp64 vs the harness's fp32 torch loop
+    assert rel(states[-1], d["ssm"]) < 1e-6
+    assert np.array_equal(O.bf16_bits(conv_states[-1].astype(np.float32)), d["conv"])
 
 
 def test_bf16_round_matches_torch():
