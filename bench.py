@@ -430,6 +430,84 @@ def bench_norm(R, steps, warmup, dev, H=4096, skip=True):
             "op": "SkipRmsNorm (sum written)" if skip else "RmsNorm", "H": H}
 
 
+def _time_rotating(make_call, copies, steps, warmup):
+    """us per call of make_call(i) over `copies` distinct input sets, graph-replayed."""
+    def one_pass():
+        for i in range(copies):
+            make_call(i)
+
+    g = capture(one_pass)
+    ms = time_graph(g, steps, warmup)
+    del g
+    return ms * 1e3 / (steps * copies)
+
+
+def bench_legacy(layout, R, N, K, steps, warmup, dev):
+    """Legacy split-layout GEMV (Q8Gemv gguf=0, Q4Gemv iq2=0/1/2, Nvfp4Gemv gguf=0); algorithmic bytes
+    per call = weight bytes + scale bytes."""
+    import torch
+
+    from gguf_onnx_ops_b200 import _lib, ops
+
+    wb = {_lib.GGUF_LAYOUT_Q8_SPLIT: K, _lib.GGUF_LAYOUT_IQ2_NATIVE: K // 4}.get(layout, K // 2)
+    sb = {_lib.GGUF_LAYOUT_IQ2_NATIVE: K // 128, _lib.GGUF_LAYOUT_NVFP4_SPLIT: K // 16}.get(layout, K // 16)
+    per = N * (wb + sb)
+    copies = n_copies(per)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(layout)
+    ws = [torch.randint(0, 256, (N, wb), generator=gen, device=dev, dtype=torch.uint8) for _ in range(copies)]
+    if layout == _lib.GGUF_LAYOUT_NVFP4_SPLIT:
+        ss = [torch.randint(0x30, 0x48, (N, sb), generator=gen, device=dev, dtype=torch.uint8) for _ in range(copies)]
+    elif layout == _lib.GGUF_LAYOUT_IQ2_NATIVE:
+        ss = [(torch.rand(N, sb // 2, generator=gen, device=dev) * 0.02 + 0.001).half().view(torch.uint8)
+              for _ in range(copies)]
+    else:
+        ss = [(torch.rand(N, sb // 2, generator=gen, device=dev) * 0.02).bfloat16().view(torch.uint8)
+              for _ in range(copies)]
+    x = torch.randn(R, K, device=dev).bfloat16()
+    y = torch.empty(R, N, dtype=torch.bfloat16, device=dev)
+    gs = torch.tensor([0.37], device=dev)
+    us = _time_rotating(lambda i: ops.gemv_legacy_into(layout, x, ws[i], ss[i], gs, y, R, N, K), copies, steps, warmup)
+    return {"us_per_call": round(us, 3), "gbs": round(per / (us * 1e-6) / 1e9, 1), "algorithmic_bytes": per,
+            "shape": f"R={R} N={N} K={K}"}
+
+
+def bench_mamba(R, steps, warmup, dev, heads=128, ng=8, verify=False):
+    """MambaStep (or MambaVerify over R tokens) at heads=128, n_groups=8 (di 8192, cd 10240); bytes per
+    call = fp32 state read once + written once per output row + conv state, proj and outputs."""
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    di, cd = heads * 64, heads * 64 + 2 * ng * 128
+    rows = R if verify else 1
+    state = rows * heads * 128 * 64 * 4
+    per = heads * 128 * 64 * 4 + state + R * (di + cd + heads) * 2 + 2 * rows * cd * 3 * 2 + R * (di * 2 + cd * 2 + di * 4)
+    copies = n_copies(per)
+    proj = torch.randn(R, di + cd + heads, device=dev).bfloat16()
+    cs = [torch.randn(rows, cd, 3, device=dev).bfloat16() for _ in range(copies)]
+    ss = [torch.randn(rows, heads, 128, 64, device=dev) * 0.1 for _ in range(copies)]
+    cso = [torch.empty_like(c) for c in cs]
+    sso = [torch.empty_like(t) for t in ss]
+    cw = (torch.randn(cd, 4, device=dev) * 0.3).bfloat16()
+    cb = (torch.randn(cd, device=dev) * 0.1).bfloat16()
+    dtb, D = torch.randn(heads, device=dev) * 0.3, torch.randn(heads, device=dev)
+    an = -torch.rand(heads, device=dev) * 4 - 0.1
+    nw = torch.rand(di, device=dev) + 0.5
+    y = torch.empty(R, di, dtype=torch.bfloat16, device=dev)
+    xbc = torch.empty(R, cd, dtype=torch.bfloat16, device=dev)
+    ypre = torch.empty(R, di, device=dev)
+    row = torch.zeros(1, dtype=torch.int32, device=dev) if verify else None
+
+    def call(i):
+        ops.mamba_step_into(proj, cs[i], ss[i], cw, cb, dtb, an, D, nw, row, y, cso[i], sso[i], xbc, ypre, R=R,
+                            state_rows=rows, heads=heads, n_groups=ng, eps=1e-5, tmin=0.001)
+
+    us = _time_rotating(call, copies, steps, warmup)
+    return {"us_per_call": round(us, 3), "gbs": round(per / (us * 1e-6) / 1e9, 1), "algorithmic_bytes": per,
+            "op": "MambaVerify" if verify else "MambaStep"}
+
+
 def bench_gguf_load(dev, rows=131072, K=4096, reps=3):
     """GGUF loader: a page-cache resident synthetic file holding one Q8_0 [rows, K] tensor (C4's LM
     head, 557 MB) copied into HBM by gguf_file_upload; GB/s = tensor bytes / wall time of the
@@ -694,6 +772,19 @@ def main():
             line["next_rows"]["RmsNorm_R1"] = bench_norm(1, max(5, args.steps // 2), args.warmup, dev, skip=False)
             torch.cuda.empty_cache()
             line["next_rows"]["GGUF_load_C4_lm_head"] = bench_gguf_load(dev)
+            from gguf_onnx_ops_b200 import _lib as L
+
+            st2 = max(5, args.steps // 2)
+            for name, layout, R, N, K in (("Q8Gemv_gguf0", L.GGUF_LAYOUT_Q8_SPLIT, 1, 4096, 4096),
+                                          ("Q4Gemv_iq2_0", L.GGUF_LAYOUT_Q4_SPLIT, 1, 14336, 4096),
+                                          ("Q4Gemv_iq2_1", L.GGUF_LAYOUT_IQ2_CODES, 8, 14336, 4096),
+                                          ("Q4Gemv_iq2_2", L.GGUF_LAYOUT_IQ2_NATIVE, 1, 14336, 4096),
+                                          ("Nvfp4Gemv_gguf0", L.GGUF_LAYOUT_NVFP4_SPLIT, 1, 13824, 5120)):
+                line["next_rows"][f"{name}_R{R}"] = bench_legacy(layout, R, N, K, st2, args.warmup, dev)
+                torch.cuda.empty_cache()
+            line["next_rows"]["MambaStep_R1"] = bench_mamba(1, st2, args.warmup, dev)
+            line["next_rows"]["MambaVerify_R8"] = bench_mamba(8, st2, args.warmup, dev, verify=True)
+            torch.cuda.empty_cache()
     if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather
         line["sharded"] = {f"C4_R{R}": bench_rowsplit(R, max(5, args.steps // 2), args.warmup, dev, world, rank)
                            for R in (1, 4)}

@@ -80,6 +80,14 @@ __global__ void __launch_bounds__(kMambaThreads) mamba_conv_ssm_kernel(const __g
     }
   }
   const bf16* cin = a.conv_in + static_cast<int64_t>(row) * a.cd * 3;
+  // The head's state does not depend on the conv: its loads are in flight during the conv phase.
+  const int p = tid & (kMambaHD - 1), q = tid >> 6;
+  const int64_t row_stride = static_cast<int64_t>(a.heads) * kMambaDS * kMambaHD;
+  const int64_t head_off = (static_cast<int64_t>(h) * kMambaDS + q * 32) * kMambaHD + p;
+  const float* sp = a.ssm_in + static_cast<int64_t>(row) * row_stride + head_off;
+  float st[32];
+#pragma unroll
+  for (int n = 0; n < 32; ++n) st[n] = __ldcs(sp + n * kMambaHD);
 
   // ---- conv of this head's 64 x channels and its group's 128 B + 128 C channels ----
   for (int i = tid; i < kMambaHD + 2 * kMambaDS; i += kMambaThreads) {
@@ -138,13 +146,6 @@ __global__ void __launch_bounds__(kMambaThreads) mamba_conv_ssm_kernel(const __g
   __syncthreads();
 
   // ---- state recurrence: thread (p, q) owns state[h][32q .. 32q + 31][p] ----
-  const int p = tid & (kMambaHD - 1), q = tid >> 6;
-  const int64_t row_stride = static_cast<int64_t>(a.heads) * kMambaDS * kMambaHD;
-  const int64_t head_off = (static_cast<int64_t>(h) * kMambaDS + q * 32) * kMambaHD + p;
-  const float* sp = a.ssm_in + static_cast<int64_t>(row) * row_stride + head_off;
-  float st[32];
-#pragma unroll
-  for (int n = 0; n < 32; ++n) st[n] = sp[n * kMambaHD];
   const float A = __ldg(a.a_neg + h), D = __ldg(a.d_skip + h);
   for (int r = 0; r < R; ++r) {
     const float dt = sDt[r];
