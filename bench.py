@@ -551,19 +551,28 @@ def bench_gguf_load(dev, rows=131072, K=4096, reps=3):
 
 
 def bench_e2e_gemv(op, R, N, K, steps, warmup, dev, state):
-    """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host."""
+    """Public-API end to end: pinned host x -> device, one pass over the weight copies, every y -> pinned host
+    (on a copy stream, overlapped with the next calls); the step ends when every y is on the host."""
     import torch
 
     ws, x, ys, gs, wbytes, copies = state
     xh = torch.randn(R, K).bfloat16().pin_memory()
     yh = torch.empty(copies, R, N, dtype=torch.bfloat16).pin_memory()
     xd = torch.empty_like(x)
+    # each call's y goes back to the host on a copy stream as soon as its GEMV ends, overlapping the
+    # following GEMVs (the serving pattern: outputs stream out while the next op computes)
+    copy_stream = torch.cuda.Stream()
+    done = [torch.cuda.Event() for _ in range(copies)]
 
     def step():
         xd.copy_(xh, non_blocking=True)
         for i, (w, y) in enumerate(zip(ws, ys)):
             gemv_call(op, xd, w, y, gs, R, N, K)
-            yh[i].copy_(y, non_blocking=True)
+            done[i].record()
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(done[i])
+                yh[i].copy_(y, non_blocking=True)
+        torch.cuda.current_stream().wait_stream(copy_stream)
 
     g = capture(step)
     ms = time_graph(g, steps, warmup)
