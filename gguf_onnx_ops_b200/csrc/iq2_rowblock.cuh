@@ -63,25 +63,7 @@ __global__ void __launch_bounds__(kRbWarps * 32, 1) iq2_rowblock_kernel(const Ro
   const int blk0 = pair * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
   if (half == 0 && lane == 0 && blk0 < a.blocks) fill(blk0);
 
-  // tables (16 replicas of each 8-byte entry; loads first, then stores)
-  {
-    constexpr int kStores = (256 + 128) * 8, kIters = (kStores + kRbWarps * 32 - 1) / (kRbWarps * 32);
-    uint2 v[kIters];
-#pragma unroll
-    for (int j = 0; j < kIters; ++j) {
-      const int i = threadIdx.x + j * kRbWarps * 32, ent = i >> 3;
-      v[j] = i >= kStores ? make_uint2(0u, 0u)
-                          : (ent < 256 ? __ldg(reinterpret_cast<const uint2*>(&g_iq2_mag_u8[ent][0]))
-                                       : __ldg(reinterpret_cast<const uint2*>(&g_iq2_sign_mask[ent - 256][0])));
-      const uint32_t op = ent < 256 ? 0x40404040u : 0u, and_ = ent < 256 ? 0xFFFFFFFFu : 0x3F3F3F3Fu;
-      v[j] = make_uint2((v[j].x & and_) | op, (v[j].y & and_) | op);
-    }
-#pragma unroll
-    for (int j = 0; j < kIters; ++j) {
-      const int i = threadIdx.x + j * kRbWarps * 32;
-      if (i < kStores) *reinterpret_cast<uint4*>(smem + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(v[j].x, v[j].y, v[j].x, v[j].y);
-    }
-  }
+  i8_fill_tables<kRbWarps * 32>(smem, threadIdx.x);  // tables at offset 0 (kI8Lut bytes)
 
   pdl_wait();  // x is produced by the previous kernel
   // ---- x -> limbs: thread i converts elements 8i..8i+7 (group i >> 2 of slice i >> 5) ----
@@ -169,10 +151,8 @@ __global__ void __launch_bounds__(kRbWarps * 32, 1) iq2_rowblock_kernel(const Ro
         uint32_t A[4][2];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          const uint32_t gx = e == 0 ? (rc[r].x << 7) : (rc[r].x >> (8 * e - 7));
-          const uint32_t sy = e == 0 ? (rc[r].y << 7) : (e == 1 ? rc[r].y : (rc[r].y >> (7 * e - 7)));
-          const uint2 X = *reinterpret_cast<const uint2*>(smem + ((gx & 0x7F80u) | lane_off));
-          const uint2 M = *reinterpret_cast<const uint2*>(smem + kI8MagLut + ((sy & 0x3F80u) | lane_off));
+          const uint2 X = *reinterpret_cast<const uint2*>(smem + i8_mag_addr(rc[r].x, e, lane_off));
+          const uint2 M = *reinterpret_cast<const uint2*>(smem + i8_sgn_addr(rc[r].y, e, lane_off | 128u));
           A[r][0] = X.x - 2u * (X.x & M.x);
           A[r][1] = X.y - 2u * (X.y & M.y);
         }

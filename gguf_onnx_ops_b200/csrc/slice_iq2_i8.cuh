@@ -30,9 +30,20 @@
 
 namespace gguf_b200 {
 
-constexpr int kI8MagLut = 256 * 128;  // 256 grid entries x 16 replicas x 8 bytes
-constexpr int kI8SgnLut = 128 * 128;  // 128 sign patterns x 16 replicas x 8 bytes
-constexpr int kI8Lut = kI8MagLut + kI8SgnLut;
+// Shared-memory tables: 256-byte slot e holds the 16 replicas (8 bytes each, replica = lane & 15) of
+// codebook entry e as 64 + magnitude bytes (slot bytes 0..127) and, for e < 128, of sign pattern e
+// as 0x3F per negative byte (slot bytes 128..255).  With a 256-byte slot the magnitude address of
+// grid byte k of a record word is one byte-permute: [lane_off, byte k, 0, 0].
+constexpr int kI8Lut = 256 * 256;
+
+__device__ __forceinline__ uint32_t i8_mag_addr(uint32_t grid_word, int e, uint32_t lane_off) {
+  return __byte_perm(grid_word, lane_off, 0x5504u | (static_cast<uint32_t>(e) << 4));
+}
+// Sign field e (bits 7e..7e+6 of the aux word) * 256 + 128 + lane_off; lane_off128 = lane_off | 128.
+__device__ __forceinline__ uint32_t i8_sgn_addr(uint32_t aux, int e, uint32_t lane_off128) {
+  const uint32_t f = e == 0 ? (aux << 8) : (e == 1 ? (aux << 1) : (aux >> (7 * e - 8)));
+  return (f & 0x7F00u) | lane_off128;
+}
 
 __device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1) {
@@ -170,7 +181,7 @@ __device__ __forceinline__ void i8_records_any(const uint8_t* st, uint32_t r0, u
 __device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[4], uint32_t dbits, const I8XFrag& f,
                                          float& acc0, float& acc1) {
   const int lane = threadIdx.x & 31, t = lane & 3;
-  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u, lane_off128 = lane_off | 128u;
   const int q0 = (lane & ~3) | ((2 * t) & 3), q1 = (lane & ~3) | ((2 * t + 1) & 3);
   const int sel_sh = t >= 2 ? 4 : 0;
   int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
@@ -179,11 +190,8 @@ __device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[
     uint32_t A[4][2];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      // table offsets: (grid byte e) * 128 and (sign field e) * 128, one shift + one LOP3 each
-      const uint32_t gx = e == 0 ? (rc[r].x << 7) : (rc[r].x >> (8 * e - 7));
-      const uint32_t sy = e == 0 ? (rc[r].y << 7) : (e == 1 ? rc[r].y : (rc[r].y >> (7 * e - 7)));
-      const uint2 X = *reinterpret_cast<const uint2*>(smem + ((gx & 0x7F80u) | lane_off));
-      const uint2 M = *reinterpret_cast<const uint2*>(smem + kI8MagLut + ((sy & 0x3F80u) | lane_off));
+      const uint2 X = *reinterpret_cast<const uint2*>(smem + i8_mag_addr(rc[r].x, e, lane_off));
+      const uint2 M = *reinterpret_cast<const uint2*>(smem + i8_sgn_addr(rc[r].y, e, lane_off128));
       A[r][0] = X.x - 2u * (X.x & M.x);  // 64 + s*m per byte, no borrow between bytes
       A[r][1] = X.y - 2u * (X.y & M.y);
     }
@@ -211,8 +219,8 @@ __device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[
   acc1 = (f2 * (f.xs0 * h10) + f3 * (f.xs1 * h11)) * d1s;
 }
 
-// 16 replicas of each 8-byte table entry at shared offset 0 (64 + magnitudes, then the sign masks),
-// two replicas per 16-byte store; called by threads 0..kThreads-1, each issuing all of its loads
+// 16 replicas of each 8-byte table entry at shared offset 0 (64 + magnitudes and sign masks in the
+// 256-byte slots described at kI8Lut), two replicas per 16-byte store; called by threads 0..kThreads-1, each issuing all of its loads
 // before its first store (one L2 round trip).
 template <int kThreads>
 __device__ __forceinline__ void i8_fill_tables(uint8_t* smem, int tid) {
@@ -231,7 +239,8 @@ __device__ __forceinline__ void i8_fill_tables(uint8_t* smem, int tid) {
 #pragma unroll
   for (int j = 0; j < kIters; ++j) {
     const int i = tid + j * kThreads;
-    if (i < kStores) *reinterpret_cast<uint4*>(smem + (i >> 3) * 128 + (i & 7) * 16) = make_uint4(v[j].x, v[j].y, v[j].x, v[j].y);
+    const int ent = i >> 3, slot = ent < 256 ? ent * 256 : (ent - 256) * 256 + 128;
+    if (i < kStores) *reinterpret_cast<uint4*>(smem + slot + (i & 7) * 16) = make_uint4(v[j].x, v[j].y, v[j].x, v[j].y);
   }
 }
 
