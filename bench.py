@@ -673,11 +673,17 @@ def cpu_baseline(op, R, N, K, budget_s=10.0):
     t0 = time.perf_counter()
     run(w)
     dt = time.perf_counter() - t0
+    # second figure: the matmul alone on the pre-dequantised fp32 weights
+    d = torch.from_numpy(np.concatenate(list(pool.map(deq, [w[i:i + chunk] for i in range(0, rows, chunk)]))))
+    t0 = time.perf_counter()
+    _ = xf @ d.T
+    dt_mm = time.perf_counter() - t0
     pool.shutdown()
     bytes_ = rows * ROW_BYTES[op](K)
     return dict(value=bytes_ / dt / 1e9, unit="GB/s", cores=cores, kind="port",
                 sample=f"{rows} of {N} rows, R={R}, K={K}: numpy dequantise ({cores} threads) + torch fp32 matmul",
-                seconds=dt)
+                seconds=dt, matmul_only_gbs=bytes_ / dt_mm / 1e9,
+                matmul_only_note="torch fp32 x @ W^T on pre-dequantised W, GB/s of the GGUF bytes those rows hold")
 
 
 # ------------------------------------------------------------------------------------------------
