@@ -508,6 +508,38 @@ def bench_mamba(R, steps, warmup, dev, heads=128, ng=8, verify=False):
             "op": "MambaVerify" if verify else "MambaStep"}
 
 
+def bench_fused_norm_gemv(steps, warmup, dev, N=14336, K=4096):
+    """Decode step of config 1 with its input norm: SkipRmsNorm then Q4Gemv iq2=3 (two launches, PDL
+    chained) against the fused single launch; same rotating weight copies."""
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    wbytes = N * (K // 256) * 66
+    copies = n_copies(wbytes)
+    base = gen_weights("iq2_xxs", N, K, seed=1, dev=dev)
+    ws = replicate(base, copies)
+    del base
+    x = torch.randn(1, K, device=dev).bfloat16()
+    sk = torch.randn(1, K, device=dev).bfloat16()
+    gamma = torch.rand(K, device=dev) + 0.5
+    xn, sm = torch.empty_like(x), torch.empty_like(x)
+    y = torch.empty(1, N, dtype=torch.bfloat16, device=dev)
+
+    def chain(i):
+        ops.rms_norm_into(x, sk, gamma, xn, sm, 1, K, 1e-5)
+        ops.iq2_xxs_gemv_into(xn, ws[i], y, 1, N, K)
+
+    def fused(i):
+        ops.rms_norm_iq2_xxs_gemv_into(x, sk, gamma, 1e-5, ws[i], y, xn, sm, N, K)
+
+    us_chain = _time_rotating(chain, copies, steps, warmup)
+    us_fused = _time_rotating(fused, copies, steps, warmup)
+    del ws
+    return {"us_norm_then_gemv": round(us_chain, 3), "us_fused": round(us_fused, 3),
+            "gbs_fused": round(wbytes / (us_fused * 1e-6) / 1e9, 1), "shape": f"R=1 N={N} K={K} (SkipRmsNorm + Q4Gemv iq2=3)"}
+
+
 def bench_gguf_load(dev, rows=131072, K=4096, reps=3):
     """GGUF loader: a page-cache resident synthetic file holding one Q8_0 [rows, K] tensor (C4's LM
     head, 557 MB) copied into HBM by gguf_file_upload; GB/s = tensor bytes / wall time of the
@@ -797,6 +829,8 @@ def main():
                                           ("Nvfp4Gemv_gguf0", L.GGUF_LAYOUT_NVFP4_SPLIT, 1, 13824, 5120)):
                 line["next_rows"][f"{name}_R{R}"] = bench_legacy(layout, R, N, K, st2, args.warmup, dev)
                 torch.cuda.empty_cache()
+            line["next_rows"]["SkipRmsNorm_Q4Gemv_C1_R1"] = bench_fused_norm_gemv(st2, args.warmup, dev)
+            torch.cuda.empty_cache()
             line["next_rows"]["MambaStep_R1"] = bench_mamba(1, st2, args.warmup, dev)
             line["next_rows"]["MambaVerify_R8"] = bench_mamba(8, st2, args.warmup, dev, verify=True)
             torch.cuda.empty_cache()

@@ -39,6 +39,7 @@ SIGNATURES = {
     "gguf_mamba_step": (_I32, [_P] * 5 + [_I32] + [_P] * 10 + [_I64] * 6 + [_F32, _F32, _P]),
     "gguf_q8_0_embed": (_I32, [_P, _P, _P, _I64, _I64, _I64, _P]),
     "gguf_rms_norm": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _F32, _P]),
+    "gguf_rms_norm_iq2_xxs_gemv": (_I32, [_P, _P, _P, _F32, _P, _P, _P, _P, _I64, _I64, _P]),
     "gguf_moe_route": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),
     "gguf_moe_route_bf16": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _F32, _P]),
     "gguf_relu2": (_I32, [_P, _P, _I64, _P]),

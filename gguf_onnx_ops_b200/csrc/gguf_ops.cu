@@ -301,9 +301,25 @@ int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
 }
 
 // IQ2_XXS R = 1 on the integer tensor cores (slice_iq2_i8.cuh); same staging plan as run_slice_r1.
+struct FusedNorm {  // optional (Skip)RmsNorm prologue of the single-row IQ2_XXS GEMV
+  const float* gamma;
+  const void* skip;
+  void* x_norm_out;
+  void* sum_out;
+  float eps;
+};
+
 template <int kW>
-int run_slice_iq2_i8(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
+int run_slice_iq2_i8(const void* x, const void* w, void* y, int N, int K, cudaStream_t s,
+                     const FusedNorm* norm = nullptr) {
   SliceArgs a = {};
+  if (norm) {
+    a.gamma = norm->gamma;
+    a.skip = static_cast<const bf16*>(norm->skip);
+    a.x_norm_out = static_cast<bf16*>(norm->x_norm_out);
+    a.sum_out = static_cast<bf16*>(norm->sum_out);
+    a.eps = norm->eps;
+  }
   a.w = static_cast<const uint8_t*>(w);
   a.x = static_cast<const bf16*>(x);
   a.y = static_cast<bf16*>(y);
@@ -1091,6 +1107,20 @@ int gguf_mamba_step(const void* proj, const void* conv_state, const float* ssm_s
              norm_w, static_cast<bf16*>(y));
   if (e != cudaSuccess) return cuda_fail((op + " norm launch").c_str(), e);
   return GGUF_OK;
+}
+
+int gguf_rms_norm_iq2_xxs_gemv(const void* x, const void* skip, const float* gamma, float eps, const void* w,
+                               void* y, void* x_norm_out, void* sum_out, int64_t N, int64_t K, void* stream) {
+  t_last_error.clear();
+  if (!x || !gamma || !w || !y) return fail(GGUF_ERR_INVALID_ARGUMENT, "RmsNorm+Q4Gemv: null tensor pointer");
+  if (K != 4096) return fail(GGUF_ERR_INVALID_ARGUMENT, "RmsNorm+Q4Gemv: the fused single-row kernel needs K = 4096");
+  if (!int_range(N)) return fail(GGUF_ERR_INVALID_ARGUMENT, "RmsNorm+Q4Gemv: bad N" + dims(1, N, K));
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(gamma, 16) || (skip && !aligned(skip, 16)) ||
+      (x_norm_out && !aligned(x_norm_out, 16)) || (sum_out && !aligned(sum_out, 16)))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "RmsNorm+Q4Gemv: tensors must be 16-byte aligned");
+  const FusedNorm fn{gamma, skip, x_norm_out, skip ? sum_out : nullptr, eps};
+  return run_slice_iq2_i8<16>(x, w, y, static_cast<int>(N), static_cast<int>(K), static_cast<cudaStream_t>(stream),
+                              &fn);
 }
 
 int gguf_rms_norm(const void* x, const void* skip, const float* gamma, void* y, void* sum, int64_t R, int64_t H,

@@ -26,6 +26,7 @@
 #pragma once
 
 #include "engine.cuh"
+#include "rms_norm.cuh"
 #include "slice_r1.cuh"
 
 namespace gguf_b200 {
@@ -301,8 +302,23 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
   pdl_wait();  // x is produced by the previous kernel
 
   // ---- x fragments of this warp's slice: lane l converts elements 8l..8l+7 (group l >> 2) ----
+  uint4 xv = ldg128(a.x + warp * 256 + 8 * lane);
+  if (a.gamma != nullptr) {
+    // fused (Skip)RmsNorm: thread t holds chunk t of the 4096-element row, the layout of the
+    // standalone kernel's 512 threads, so the mean of squares (and every output bit) is the same
+    // (the host enables it for K = 4096 only, where kW = 16 warps = 512 threads)
+    if (a.skip != nullptr) {
+      xv = bf16x8_add(xv, ldg128(a.skip + warp * 256 + 8 * lane));
+      if (blockIdx.x == 0 && a.sum_out != nullptr)
+        *reinterpret_cast<uint4*>(a.sum_out + warp * 256 + 8 * lane) = xv;
+    }
+    const float rs = rsqrtf(norm_block_sum(norm_accumulate(0.f, xv, 1.0f / static_cast<float>(a.K)), red) + a.eps);
+    xv = norm_scale8(xv, load_gamma8(a.gamma, warp * 32 + lane), rs);
+    if (blockIdx.x == 0 && a.x_norm_out != nullptr)
+      *reinterpret_cast<uint4*>(a.x_norm_out + warp * 256 + 8 * lane) = xv;
+  }
   I8XFrag xf;
-  i8_x_frag(ldg128(a.x + warp * 256 + 8 * lane), xf);
+  i8_x_frag(xv, xf);
   const bool al = (warp & 1) != 0;  // odd super-block: records 4-byte aligned
   const uint32_t so = static_cast<uint32_t>(warp) * 66u;
   const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);

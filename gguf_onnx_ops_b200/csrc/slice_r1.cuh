@@ -44,6 +44,13 @@ struct SliceArgs {
   int stride, stage_bytes, stages;
   int off_stage, off_red, off_bar;
   PeerOut po;  // npeer > 0: row-split shard, y stored into every GPU of the group (slice_r1_kernel)
+  // fused (Skip)RmsNorm prologue (slice_iq2_i8_kernel, K = 4096): x <- RmsNorm(x [+ skip]) with the
+  // standalone op's arithmetic (rms_norm.cuh); CTA 0 writes the normalised row / the sum if asked
+  const float* gamma;  // null: no norm
+  const bf16* skip;
+  bf16* x_norm_out;
+  bf16* sum_out;
+  float eps;
 };
 
 template <int F>

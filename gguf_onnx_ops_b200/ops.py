@@ -235,6 +235,32 @@ def SkipRmsNorm(x: torch.Tensor, skip: torch.Tensor, gamma: torch.Tensor, epsilo
     return (y, s) if return_sum else (y,)
 
 
+def rms_norm_iq2_xxs_gemv_into(x, skip, gamma, eps, w, y, x_norm, sum_out, N: int, K: int, stream=None) -> None:
+    check(load().gguf_rms_norm_iq2_xxs_gemv(_ptr(x), _ptr(skip), _ptr(gamma), eps, _ptr(w), _ptr(y), _ptr(x_norm),
+                                            _ptr(sum_out), N, K, _stream(stream)))
+
+
+def SkipRmsNormQ4Gemv(x: torch.Tensor, skip: torch.Tensor | None, gamma: torch.Tensor, w: torch.Tensor,
+                      epsilon: float = 1e-5):
+    """Fused decode step (an extension, not a reference op): y = Q4Gemv iq2=3(RmsNorm(x [+ skip])) for one
+    row, K = 4096.  Returns (y [1, N], x_norm [1, K], sum [1, K] or None), bit-identical to SkipRmsNorm /
+    RmsNorm followed by Q4Gemv."""
+    _need(x, "x", torch.bfloat16, "SkipRmsNormQ4Gemv")
+    _need(gamma, "gamma", torch.float32, "SkipRmsNormQ4Gemv")
+    _need(w, "w", torch.uint8, "SkipRmsNormQ4Gemv")
+    K = x.shape[-1]
+    N = w.shape[0]
+    if x.numel() != K or K != 4096 or gamma.numel() != K or w.numel() != N * (K // 256) * IQ2_XXS_BYTES:
+        raise ValueError("SkipRmsNormQ4Gemv: needs one row of K = 4096 and w [N, (K/256)*66]")
+    if skip is not None:
+        _need(skip, "skip", torch.bfloat16, "SkipRmsNormQ4Gemv")
+    y = torch.empty(1, N, dtype=torch.bfloat16, device=x.device)
+    x_norm = torch.empty(1, K, dtype=torch.bfloat16, device=x.device)
+    s = torch.empty(1, K, dtype=torch.bfloat16, device=x.device) if skip is not None else None
+    rms_norm_iq2_xxs_gemv_into(x, skip, gamma, epsilon, w, y, x_norm, s, N, K)
+    return y, x_norm, s
+
+
 # ------------------------------------------------------------------------------------------------
 # Router + MoE
 # ------------------------------------------------------------------------------------------------

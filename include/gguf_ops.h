@@ -153,6 +153,18 @@ GGUF_OPS_API int gguf_rms_norm(const void* x, const void* skip, const float* gam
                                int64_t H, float eps, void* stream);
 
 /*
+ * (Skip)RmsNorm fused into the single-row IQ2_XXS GEMV (no counterpart in the reference, which runs
+ * the two ops as separate kernels): y = Q4Gemv_iq2=3(RmsNorm(x [+ skip], gamma, eps), w), one launch.
+ * Every CTA normalises the row in its prologue with the standalone op's arithmetic, so y, and the
+ * optional x_norm_out (the normalised row) and sum_out (bf16(x + skip)), are bit-identical to
+ * gguf_rms_norm followed by gguf_iq2_xxs_gemv.  x, skip, x_norm_out, sum_out bf16 [1, K]; gamma fp32
+ * [K]; w raw IQ2_XXS [N, K/256*66]; K = 4096; skip, x_norm_out and sum_out may be NULL.
+ */
+GGUF_OPS_API int gguf_rms_norm_iq2_xxs_gemv(const void* x, const void* skip, const float* gamma, float eps,
+                                            const void* w, void* y, void* x_norm_out, void* sum_out, int64_t N,
+                                            int64_t K, void* stream);
+
+/*
  * MoeRouteGGUF:  scores[R,E] = sigmoid(x[R,K] @ bf16(gate_w)^T);  idx[R,topk] = top-k of scores + bias
  * (descending, ties to the lower expert index);  weights = s_sel / (sum s_sel + 1e-20) * scale.
  * x bf16 [R,K]; gate_w f32 [E,K]; bias f32 [E] -> idx i32 [R,topk], weights f32 [R,topk], scores f32 [R,E].
