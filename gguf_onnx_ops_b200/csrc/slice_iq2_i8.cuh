@@ -299,6 +299,8 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
   __syncthreads();
 
   const int g = lane >> 2, t = lane & 3;
+  Gamma8 gm;  // fused norm: gamma is a weight, fetched before the dependency wait
+  if (a.gamma != nullptr) gm = load_gamma8(a.gamma, warp * 32 + lane);
   pdl_wait();  // x is produced by the previous kernel
 
   // ---- x fragments of this warp's slice: lane l converts elements 8l..8l+7 (group l >> 2) ----
@@ -313,7 +315,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
         *reinterpret_cast<uint4*>(a.sum_out + warp * 256 + 8 * lane) = xv;
     }
     const float rs = rsqrtf(norm_block_sum(norm_accumulate(0.f, xv, 1.0f / static_cast<float>(a.K)), red) + a.eps);
-    xv = norm_scale8(xv, load_gamma8(a.gamma, warp * 32 + lane), rs);
+    xv = norm_scale8(xv, gm, rs);
     if (blockIdx.x == 0 && a.x_norm_out != nullptr)
       *reinterpret_cast<uint4*>(a.x_norm_out + warp * 256 + 8 * lane) = xv;
   }
