@@ -19,6 +19,7 @@
 #include "engine.cuh"
 #include "slice_r1.cuh"
 #include "slice_iq2_i8.cuh"
+#include "slice_fp4_i8.cuh"
 #include "iq2_rowblock.cuh"
 #include "moe_fused.cuh"
 #include "small_kernels.cuh"
@@ -285,7 +286,7 @@ int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
   a.stage_bytes = ((16 * st + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
   const int lut = (SliceFmt<F>::kLut + 127) & ~127, red = 2 * kW * 16 * 4;
   a.stages = std::min(8, (kSmemBudgetMax - lut - red - 256) / a.stage_bytes);
-  if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "K too large for the single-row staging plan");
+  if (a.stages < 2) return -1;  // does not fit: the caller falls back to the engine
   a.off_stage = lut;
   a.off_red = lut + a.stages * a.stage_bytes;
   a.off_bar = a.off_red + red;
@@ -301,6 +302,37 @@ int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
 }
 
 // IQ2_XXS R = 1 on the integer tensor cores (slice_iq2_i8.cuh); same staging plan as run_slice_r1.
+// NVFP4 R = 1 on the integer tensor cores (slice_fp4_i8.cuh): K = 128 * kW * kSPW.
+template <int kW, int kSPW>
+int run_slice_fp4_i8(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s) {
+  SliceArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.x = static_cast<const bf16*>(x);
+  a.gscale = gscale;
+  a.y = static_cast<bf16*>(y);
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 64 * 36;  // K % 128 == 0: a multiple of 8 words
+  a.tiles = (N + 15) / 16;
+  a.stride = a.row_bytes + ((32 - a.row_bytes % 128) + 128) % 128;  // pitch = 32 mod 128 bytes
+  a.stage_bytes = ((16 * a.stride) + 127) & ~127;
+  const int red_per_stage = kW * 16 * 4 + 4;
+  a.stages = std::min(8, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "K too large for the single-row staging plan");
+  a.off_stage = 0;
+  a.off_red = a.stages * a.stage_bytes;
+  a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = slice_fp4_i8_kernel<kW, kSPW>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("single-row NVFP4 GEMV launch", e);
+  return GGUF_OK;
+}
+
 struct FusedNorm {  // optional (Skip)RmsNorm prologue of the single-row IQ2_XXS GEMV
   const float* gamma;
   const void* skip;
@@ -391,10 +423,22 @@ int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
       default: return -1;
     }
   }
+  if (F == kFmtFP4 && fast == 4) {  // integer-decode variant (cross-check / comparison)
+    switch (K) {
+      case 2048: return run_slice_fp4_i8<16, 1>(x, w, gscale, y, N, K, s);
+      case 4096: return run_slice_fp4_i8<16, 2>(x, w, gscale, y, N, K, s);
+      case 5120: return run_slice_fp4_i8<20, 2>(x, w, gscale, y, N, K, s);
+      case 6144: return run_slice_fp4_i8<16, 3>(x, w, gscale, y, N, K, s);
+      case 8192: return run_slice_fp4_i8<16, 4>(x, w, gscale, y, N, K, s);
+      default: break;
+    }
+  }
   switch (K) {
     case 2048: return run_slice_r1<F, 8, 1>(x, w, gscale, y, N, K, s);
     case 4096: return run_slice_r1<F, 16, 1>(x, w, gscale, y, N, K, s);
     case 5120: return run_slice_r1<F, 20, 1>(x, w, gscale, y, N, K, s);
+    case 6144: return F == kFmtFP4 ? run_slice_r1<F, 12, 2>(x, w, gscale, y, N, K, s) : -1;
+    case 8192: return F == kFmtFP4 ? run_slice_r1<F, 16, 2>(x, w, gscale, y, N, K, s) : -1;
     default: return -1;
   }
 }
@@ -442,7 +486,7 @@ const char* gguf_last_error(void) { return t_last_error.c_str(); }
 
 void gguf_set_pdl(int enable) { g_pdl.store(enable ? 1 : 0); }
 
-void gguf_set_fast_paths(int enable) { g_fast.store(enable < 0 ? 0 : (enable > 3 ? 1 : enable)); }
+void gguf_set_fast_paths(int enable) { g_fast.store(enable < 0 ? 0 : (enable > 4 ? 1 : enable)); }
 
 int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, int64_t K, void* stream) {
   t_last_error.clear();

@@ -294,7 +294,8 @@ GGUF_OPS_API void gguf_set_pdl(int enable);
 /* Tuning / testing: enable (1, default) or disable (0) the shape-specialised kernels (the single-row
  * kernels and the fused MoeVerify); disabled, every call uses the generic engine.  2 and 3 = as 1,
  * but single-row IQ2_XXS uses the bf16 tensor-core slice kernel (2) or the integer row-block kernel
- * (3) instead of the integer slice kernel (cross-checks of the decoders). */
+ * (3) instead of the integer slice kernel; 4 = as 1, but single-row NVFP4 uses the integer-decode
+ * slice kernel instead of the bf16 one (cross-checks of the decoders). */
 GGUF_OPS_API void gguf_set_fast_paths(int enable);
 
 #ifdef __cplusplus

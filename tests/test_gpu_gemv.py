@@ -209,6 +209,54 @@ def test_single_row_fast_path(cuda, op, N, K, xscale):
     assert_device_ok()
 
 
+@pytest.mark.parametrize("K", [2048, 4096, 5120, 6144, 8192])
+def test_nvfp4_single_row_integer_kernel(cuda, K):
+    """The single-row NVFP4 kernels (bf16 slice, the default, and the integer-decode variant, mode 4)
+    against the oracle and the generic engine, with every scale byte present (gguf-py UE4M3: 0x7F -> 0,
+    otherwise bit 7 ignored)."""
+    N = 333
+    g = I.rng(K + 7)
+    w = I.nvfp4_weights(g, N, K, 0, 255)
+    x = I.bf16_normal(g, (1, K), 2.0)
+    extra = {"gscale": np.array([0.37], np.float32)}
+    ref = oracle_y("nvfp4", x, w, extra, np.arange(N))
+    y = run_gemv("nvfp4", x, w, extra, cuda)
+    assert rel(y, ref) < TOL
+    try:
+        ops.set_fast_paths(4)
+        y4 = run_gemv("nvfp4", x, w, extra, cuda)
+        ops.set_fast_paths(False)
+        y0 = run_gemv("nvfp4", x, w, extra, cuda)
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y4, ref) < TOL and rel(y, y4) < 2e-3
+    assert rel(y, y0) < 2e-3
+    assert_device_ok()
+
+
+@pytest.mark.parametrize("case", ["wide_range", "zero_groups", "subnormal", "outlier_per_group"])
+def test_nvfp4_single_row_activation_ranges(cuda, case):
+    """The integer NVFP4 path scales each 16-element sub-block of x by its maximum (as IQ2_XXS does
+    per 32): wide ranges, zero / subnormal sub-blocks and outliers stay within the op tolerance."""
+    N, K = 512, 5120
+    _, w, extra = I.gemv_case("nvfp4", 1, N, K, seed=12)
+    g = I.rng(98)
+    xf = g.standard_normal(K).astype(np.float32)
+    if case == "wide_range":
+        xf *= np.exp2(g.integers(-24, 12, K)).astype(np.float32)
+    elif case == "zero_groups":
+        xf.reshape(-1, 16)[::3] = 0.0
+    elif case == "subnormal":
+        xf.reshape(-1, 16)[::2] *= np.float32(2.0 ** -130)
+    else:
+        xf.reshape(-1, 16)[:, 5] *= 3000.0
+    x = O.bf16_bits(xf).reshape(1, K)
+    y = run_gemv("nvfp4", x, w, extra, cuda)
+    assert np.isfinite(y).all()
+    assert rel(y, oracle_y("nvfp4", x, w, extra, np.arange(N))) < TOL
+    assert_device_ok()
+
+
 @pytest.mark.parametrize("case", ["wide_range", "zero_groups", "subnormal", "outlier_per_group"])
 def test_iq2_single_row_activation_ranges(cuda, case):
     """Single-row IQ2_XXS carries each 32-element group of x as a 2-limb fixed-point integer scaled by
