@@ -54,7 +54,45 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
+    ap.add_argument("--cpu-table", action="store_true",
+                    help="print the reference CPU path's time per BASELINE config (host cores only) and exit")
     return ap.parse_args()
+
+
+def cpu_table():
+    """The reference harness's CPU path per BASELINE config on this host: bounded row samples of
+    dequantise + fp32 matmul and of the matmul alone, scaled to µs per full call; for C3 the oracle's
+    per-(row, expert) MoE loop on 6 distinct experts per row."""
+    import oracle as O
+    from oracle import inputs as I
+
+    out = {}
+    for name, op, R, N, K in ([("C0", "q8_0", 1, 4096, 4096)] +
+                              [("C1", "iq2_xxs", R, 14336, 4096) for R in (1, 4, 8)] +
+                              [("C2", "nvfp4", R, 13824, 5120) for R in (1, 8, 16)] +
+                              [("C4", "q8_0", R, 131072, 4096) for R in (1, 4, 8, 16)]):
+        cb = cpu_baseline(op, R, N, K, budget_s=2.0)
+        wbytes = N * ROW_BYTES[op](K)
+        out[f"{name}_R{R}"] = {"cores": cb["cores"], "dequant_matmul_us": round(wbytes / (cb["value"] * 1e9) * 1e6, 1),
+                               "matmul_only_us": round(wbytes / (cb["matmul_only_gbs"] * 1e9) * 1e6, 1),
+                               "sample": cb["sample"]}
+    for R in (1, 4, 8):
+        g = I.rng(R)
+        E, H, Idim, topk = 128, 1024, 1792, 6
+        z = I.bf16_normal(g, (R, H))
+        idx = np.stack([g.permutation(E)[:topk] for _ in range(R)]).astype(np.int32)
+        w = g.random((R, topk)).astype(np.float32)
+        used = sorted(set(idx.reshape(-1).tolist()))
+        t0 = time.perf_counter()
+        d1 = {e: O.dequant_iq2_xxs(I.iq2_xxs_weights(g, (Idim,), H)) for e in used}
+        d2 = {e: O.dequant_iq2_xxs(I.iq2_xxs_weights(g, (H,), Idim)) for e in used}
+        t1 = time.perf_counter()
+        O.moe_ref(z, idx, w, d1, d2)
+        t2 = time.perf_counter()
+        out[f"C3_R{R}"] = {"cores": 1, "dequant_matmul_us": round((t2 - t0) * 1e6, 1),
+                           "matmul_only_us": round((t2 - t1) * 1e6, 1),
+                           "sample": f"{len(used)} experts: numpy dequantise + fp64 per-pair loop (1 thread)"}
+    print(json.dumps(out), flush=True)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -739,6 +777,9 @@ def traffic_per_launch():
 
 def main():
     args = parse_args()
+    if args.cpu_table:
+        cpu_table()
+        return
     import torch
 
     hd = HEADLINE
