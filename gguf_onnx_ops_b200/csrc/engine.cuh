@@ -266,8 +266,10 @@ __device__ __forceinline__ void split_group_mma(const uint8_t* smem, const uint8
   }
 }
 
+// Two CTAs fit on an SM (registers <= 60, shared memory <= half): the dense GEMV runs two per SM, and
+// consecutive kernels on a stream can overlap under programmatic dependent launch.
 template <int F, int NT, int KW, int MODE>
-__global__ void __launch_bounds__((KW + 1) * 32, 1) engine_kernel(const __grid_constant__ EngineArgs a) {
+__global__ void __launch_bounds__((KW + 1) * 32, 2) engine_kernel(const __grid_constant__ EngineArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   uint64_t* empty = full + a.stages;

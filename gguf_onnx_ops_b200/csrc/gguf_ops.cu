@@ -231,7 +231,7 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
   static std::atomic<uint64_t> done{0};
   auto kern = engine_kernel<F, NT, kKW, kModeDense>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  const int grid = std::min(a.tiles, sms);
+  const int grid = std::min(a.tiles, 2 * sms);  // two CTAs per SM (engine_kernel launch bounds)
   cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("gemv launch", e);
   return GGUF_OK;
@@ -260,7 +260,7 @@ int run_dense_split(const void* x, const void* w, const void* sc, const float* g
   static std::atomic<uint64_t> done{0};
   auto kern = engine_kernel<F, NT, kKW, kModeDense>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  const int grid = std::min(a.tiles, sms);
+  const int grid = std::min(a.tiles, 2 * sms);  // two CTAs per SM (engine_kernel launch bounds)
   cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("legacy-layout gemv launch", e);
   return GGUF_OK;
@@ -706,7 +706,7 @@ extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const 
     static std::atomic<uint64_t> done{0};
     auto kern = engine_kernel<kFmtIQ2, 1, kKW, kModeMoe1>;
     if ((rc = ensure_smem(kern, smem, done))) return rc;
-    const int grid = static_cast<int>(std::min<int64_t>(P * a.tiles, sms));
+    const int grid = static_cast<int>(std::min<int64_t>(P * a.tiles, 2 * sms));
     cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fc1 launch", e);
   }
@@ -731,7 +731,7 @@ extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const 
     static std::atomic<uint64_t> done{0};
     auto kern = engine_kernel<kFmtIQ2, 1, kKW, kModeMoe2>;
     if ((rc = ensure_smem(kern, smem, done))) return rc;
-    const int grid = static_cast<int>(std::min<int64_t>(P * a.tiles, sms));
+    const int grid = static_cast<int>(std::min<int64_t>(P * a.tiles, 2 * sms));
     cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fc2 launch", e);
   }
@@ -775,7 +775,7 @@ int run_moe_split(const void* z, const int32_t* idx, const void* fc1_w, const vo
     static std::atomic<uint64_t> done{0};
     auto kern = engine_kernel<F, 1, kKW, kModeMoe1>;
     if ((rc = ensure_smem(kern, smem, done))) return rc;
-    const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(P) * a.tiles, sms));
+    const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(P) * a.tiles, 2 * sms));
     cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
     if (e != cudaSuccess) return cuda_fail("MoE fc1 launch", e);
   }
@@ -800,7 +800,7 @@ int run_moe_split(const void* z, const int32_t* idx, const void* fc1_w, const vo
     static std::atomic<uint64_t> done{0};
     auto kern = engine_kernel<F, 1, kKW, kModeMoe2>;
     if ((rc = ensure_smem(kern, smem, done))) return rc;
-    const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(P) * a.tiles, sms));
+    const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(P) * a.tiles, 2 * sms));
     cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
     if (e != cudaSuccess) return cuda_fail("MoE fc2 launch", e);
   }
