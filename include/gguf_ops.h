@@ -31,7 +31,7 @@ enum {
   GGUF_OK = 0,
   GGUF_ERR_INVALID_ARGUMENT = 1, /* shape / attribute / alignment contract violated (ORT_INVALID_ARGUMENT / ORT_FAIL) */
   GGUF_ERR_CUDA = 2,             /* a CUDA launch or runtime call failed */
-  GGUF_ERR_NOT_IMPLEMENTED = 3,  /* legacy (non-GGUF) layout requested */
+  GGUF_ERR_NOT_IMPLEMENTED = 3,  /* an attribute value outside the reference's set was requested */
   GGUF_ERR_DEVICE = 4,           /* a kernel reported a device-side error (bounded wait expired) */
   GGUF_ERR_IO = 5                /* a file could not be opened or mapped (gguf_file.h) */
 };
@@ -222,7 +222,7 @@ GGUF_OPS_API int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* i
 
 /*
  * Row-split (tensor-parallel) GEMV with the all-gather fused into the kernel (no counterpart in the
- * reference, which runs on one GPU; SURVEY row-split of the LM-head-sized Q8Gemv).  GPU `rank` of
+ * reference, which runs on one GPU; meant for LM-head-sized Q8Gemv calls).  GPU `rank` of
  * `world` holds rows [row0, row0 + rows) of W (w_shard, raw GGUF rows) and computes those outputs
  * for all R activation rows; every value is stored directly into the full y [R, n_total] of every
  * GPU of the group (peer pointers opened with gguf_ipc_open, NVLink stores), and the launch ends
@@ -246,8 +246,8 @@ GGUF_OPS_API int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard
                                     const GgufPeerOut* out, int64_t R, int64_t rows, int64_t K, void* stream);
 
 /*
- * Expert-parallel MoeVerify iq2=3 (no counterpart in the reference; SURVEY expert split of
- * MoeVerify): GPU `rank` holds experts [expert_offset, expert_offset + E_local) (fc1_w / fc2_w are
+ * Expert-parallel MoeVerify iq2=3 (no counterpart in the reference, which runs on one GPU): GPU
+ * `rank` holds experts [expert_offset, expert_offset + E_local) (fc1_w / fc2_w are
  * those experts' tensors) and processes the pairs routed to them; idx holds global expert ids (the
  * router is replicated).  The f32 [R, 1024] partial outputs are summed across the group through peer
  * memory (every GPU stores its partial into its slot of every GPU's buffer, epoch flags, bounded

@@ -98,7 +98,7 @@ def legacy_case(layout: str, g: np.random.Generator, n: int, k: int):
     return w, bf16_bits((g.random((n, nb)) * 0.02).astype(np.float32))
 
 
-# Config shapes (BASELINE.json "configs", in order).
+# Shapes of the benchmark configurations C0..C4 (the GEMV / MoE decode calls being measured).
 CONFIGS = {
     "C0": dict(op="q8_0", N=4096, K=4096, R=(1,)),
     "C1": dict(op="iq2_xxs", N=14336, K=4096, R=(1, 4, 8)),

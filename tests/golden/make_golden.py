@@ -21,7 +21,7 @@ Inputs use the reference test builders (iq2_native_blocks, the Q8 block builder,
 builder of tests/test_bolt_ops.py:210-215, :290-294, :274-275) with numpy RNG, plus the BASELINE
 config distributions at reduced sizes.
 
-    python tests/golden/make_golden.py [--reference /root/reference] [--only embed]
+    python tests/golden/make_golden.py --reference <reference checkout> [--only embed|norm|mamba]
 """
 
 from __future__ import annotations
@@ -133,7 +133,8 @@ def make_mamba():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GGUF_REFERENCE_DIR", ""),
+                    help="checkout of the reference (its src/iq2xxs_grid.h is parsed for the codebook fixture)")
     ap.add_argument("--only", choices=["embed", "norm", "mamba"], default=None)
     args = ap.parse_args()
     if args.only:
@@ -142,6 +143,8 @@ def main():
     from gguf import GGMLQuantizationType as Q
 
     # 1. IQ2_XXS codebook of the reference
+    if not args.reference:
+        ap.error("--reference (or GGUF_REFERENCE_DIR) must name the reference checkout")
     g64, gbf = parse_reference_grid(args.reference)
     np.savez_compressed(os.path.join(HERE, "iq2xxs_grid.npz"), grid_u64=g64, grid_bf16x2=gbf)
 
