@@ -221,18 +221,21 @@ __device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[
 }
 
 // 16 replicas of each 8-byte table entry at shared offset 0 (64 + magnitudes and sign masks in the
-// 256-byte slots described at kI8Lut), two replicas per 16-byte store; called by threads 0..kThreads-1, each issuing all of its loads
-// before its first store (one L2 round trip).
-template <int kThreads>
+// 256-byte slots described at kI8Lut), two replicas per 16-byte store; called by threads
+// 0..kThreads-1, each issuing all of its loads before its first store (one L2 round trip).  With
+// kSign8 the sign half of every slot e (not only e < 128) holds sign pattern e & 127, so that an
+// 8-bit field of the aux word whose top bit belongs to the next field indexes it directly.
+template <int kThreads, bool kSign8 = false>
 __device__ __forceinline__ void i8_fill_tables(uint8_t* smem, int tid) {
-  constexpr int kStores = (256 + 128) * 8, kIters = (kStores + kThreads - 1) / kThreads;
+  constexpr int kSigns = kSign8 ? 256 : 128;
+  constexpr int kStores = (256 + kSigns) * 8, kIters = (kStores + kThreads - 1) / kThreads;
   uint2 v[kIters];
 #pragma unroll
   for (int j = 0; j < kIters; ++j) {
     const int i = tid + j * kThreads, ent = i >> 3;
     v[j] = i >= kStores ? make_uint2(0u, 0u)
                         : (ent < 256 ? __ldg(reinterpret_cast<const uint2*>(&g_iq2_mag_u8[ent][0]))
-                                     : __ldg(reinterpret_cast<const uint2*>(&g_iq2_sign_mask[ent - 256][0])));
+                                     : __ldg(reinterpret_cast<const uint2*>(&g_iq2_sign_mask[(ent - 256) & 127][0])));
     // magnitudes -> 64 + m (m < 64), sign masks -> 0x3F per negative byte
     const uint32_t op = ent < 256 ? 0x40404040u : 0u, and_ = ent < 256 ? 0xFFFFFFFFu : 0x3F3F3F3Fu;
     v[j] = make_uint2((v[j].x & and_) | op, (v[j].y & and_) | op);

@@ -41,6 +41,7 @@ struct SliceArgs {
   const float* gscale;  // NVFP4 only
   bf16* y;
   int N, K, row_bytes, tiles;
+  int R;  // activation rows (slice_iq2_i8_rows_kernel; the single-row kernels ignore it)
   int stride, stage_bytes, stages;
   int off_stage, off_red, off_bar;
   PeerOut po;  // npeer > 0: row-split shard, y stored into every GPU of the group (slice_r1_kernel)
