@@ -334,6 +334,28 @@ int run_slice_fp4_i8(const void* x, const void* w, const float* gscale, void* y,
   return GGUF_OK;
 }
 
+// IQ2_XXS whole-tile staging (slice_iq2_i8.cuh, slice_iq2_i8_rows.cuh): rows land at pitch
+// a.stride.  With the row bytes a multiple of 32, rows g and g+4 would share shared-memory banks in
+// the eight-quad record loads; then the tile comes as one 2-D tensor box of 16 rows x (row bytes +
+// 16) (the pad past the row end zero-filled), else as one bulk copy at pitch = row bytes.
+void attach_slice_tmap(SliceArgs& a) {
+  a.stride = a.row_bytes;
+  a.use_tmap = 0;
+  if (a.row_bytes % 32 != 0 || a.row_bytes / 8 + 2 > 256) return;
+  auto enc = tensor_map_encoder();
+  if (!enc) return;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(a.row_bytes / 8), static_cast<cuuint64_t>(a.N)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(a.row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(a.row_bytes / 8 + 2), 16u};
+  cuuint32_t estride[2] = {1u, 1u};
+  if (enc(&a.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(a.w), dims, gstride, box, estride,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return;
+  a.use_tmap = 1;
+  a.stride = a.row_bytes + 16;
+}
+
 struct FusedNorm {  // optional (Skip)RmsNorm prologue of the single-row IQ2_XXS GEMV
   const float* gamma;
   const void* skip;
@@ -360,8 +382,8 @@ int run_slice_iq2_i8(const void* x, const void* w, void* y, int N, int K, cudaSt
   a.K = K;
   a.row_bytes = K / 256 * 66;
   a.tiles = (N + 15) / 16;
-  a.stride = a.row_bytes;  // whole-tile copies: rows contiguous in the stage
-  a.stage_bytes = ((16 * a.row_bytes + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
+  attach_slice_tmap(a);  // whole-tile copies (rows at pitch a.stride)
+  a.stage_bytes = ((16 * a.stride + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
   const int red_per_stage = kW * 16 * 4 + 4;  // reduction slot + counter
   a.stages = std::min(8, (kSmemBudgetMax - kI8Lut - 256) / (a.stage_bytes + red_per_stage + 16));
   if (a.stages < 2) return fail(GGUF_ERR_INVALID_ARGUMENT, "K too large for the single-row staging plan");
@@ -392,8 +414,8 @@ int run_slice_iq2_i8_rows(const void* x, const void* w, void* y, int R, int N, i
   a.K = K;
   a.row_bytes = K / 256 * 66;
   a.tiles = (N + 15) / 16;
-  a.stride = a.row_bytes;
-  a.stage_bytes = ((16 * a.row_bytes + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
+  attach_slice_tmap(a);
+  a.stage_bytes = ((16 * a.stride + 32) + 127) & ~127;  // +32: unaligned-window overrun pad
   const int red_per_stage = kW * 4 * kNR * 16 * 4 + 4;  // reduction slot + counter
   a.stages = std::min(8, (kSmemBudgetMax - kI8Lut - 256) / (a.stage_bytes + red_per_stage + 16));
   if (a.stages < 2) return -1;  // does not fit: the caller falls back to the engine

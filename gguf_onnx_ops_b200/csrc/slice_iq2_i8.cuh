@@ -256,7 +256,7 @@ __device__ __forceinline__ void i8_fill_tables(uint8_t* smem, int tid) {
 // the stage's records before incrementing, so the refill cannot overwrite data still in use, and a
 // slot is rewritten only after its stage has been refilled, i.e. after it was summed.
 template <int kW>
-__global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArgs a) {
+__global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const __grid_constant__ SliceArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   uint8_t* stages = smem + a.off_stage;
@@ -274,14 +274,17 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const SliceArg
   __syncthreads();
   pdl_launch_dependents();
 
-  // stage s <- tile `tile` (warp 0; lanes < rows copy one row each)
-  // stage s <- tile `tile`: its rows are contiguous in HBM and land contiguous in the stage (row
-  // stride = row bytes), so one bulk copy moves the whole tile (the copy engine's throughput per
-  // SM is bounded by copies in flight, not bytes: 1 KB row copies would cap a GPU near 2.4 TB/s).
-  // A tail of < 16 bytes (only when rows * row bytes is not a multiple of 16) is copied with plain
-  // loads before the arrive, whose release orders it for the consumers.
+  // stage s <- tile `tile` (lane 0 of the calling warp): one copy per tile (the copy engine's
+  // throughput per SM is bounded by copies in flight, not bytes: 1 KB row copies would cap a GPU
+  // near 2.4 TB/s).  Either one 2-D tensor box at the padded pitch a.stride (row bytes a multiple of
+  // 32, see attach_slice_tmap) or one bulk copy with the rows contiguous (pitch = row bytes); there a
+  // tail of < 16 bytes (rows * row bytes not a multiple of 16) is copied with plain loads before the
+  // arrive, whose release orders it for the consumers.
   auto fill = [&](int s, int tile) {
-    if (lane == 0) {
+    if (lane == 0 && a.use_tmap) {  // one 2-D box at the padded pitch a.stride (see attach_slice_tmap)
+      mbar_arrive_expect_tx(&full[s], 16u * static_cast<uint32_t>(a.stride));
+      tma_load_2d(stages + s * a.stage_bytes, &a.tmap, 0, tile * 16, &full[s]);
+    } else if (lane == 0) {
       const int rv = min(16, a.N - tile * 16);
       const uint32_t bytes = static_cast<uint32_t>(rv * a.row_bytes), main = bytes & ~15u;
       const uint8_t* src = a.w + static_cast<int64_t>(tile) * 16 * a.row_bytes;

@@ -137,10 +137,13 @@ __device__ __forceinline__ void i8_rows_slice(const uint8_t* smem, const uint8_t
 }
 
 // Staging and the cross-warp reduction follow slice_iq2_i8_kernel: warp w owns slice w of K for the
-// whole launch, a stage holds one 16-row tile (one bulk copy), the last warp to finish a tile sums
-// the stage's reduction slot in warp order, stores y [R, N] and refills the stage.
+// whole launch, a stage holds one 16-row tile, the last warp to finish a tile sums the stage's
+// reduction slot in warp order, stores y [R, N] and refills the stage.  The tile arrives as one bulk
+// copy (rows contiguous, pitch = row bytes) or, where that pitch would put rows g and g+4 on the same
+// shared-memory banks (row bytes = 0 mod 32 words), as one 2-D tensor box with a 16-byte row pad:
+// the record loads of the eight quads (rows 0..7, then 8..15) then hit eight distinct bank pairs.
 template <int kW, int kNR>
-__global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_rows_kernel(const SliceArgs a) {
+__global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
   constexpr int kRX = 4 * kNR;  // activation rows per launch (padded)
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
@@ -160,7 +163,10 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_rows_kernel(const Sli
   pdl_launch_dependents();
 
   auto fill = [&](int s, int tile) {
-    if (lane == 0) {
+    if (lane == 0 && a.use_tmap) {
+      mbar_arrive_expect_tx(&full[s], 16u * static_cast<uint32_t>(a.stride));
+      tma_load_2d(stages + s * a.stage_bytes, &a.tmap, 0, tile * 16, &full[s]);
+    } else if (lane == 0) {
       const int rv = min(16, a.N - tile * 16);
       const uint32_t bytes = static_cast<uint32_t>(rv * a.row_bytes), main = bytes & ~15u;
       const uint8_t* src = a.w + static_cast<int64_t>(tile) * 16 * a.row_bytes;
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_rows_kernel(const Sli
   const int g = lane >> 2, t = lane & 3;
   const bool al = (warp & 1) != 0;  // odd super-block: records 4-byte aligned
   const uint32_t so = static_cast<uint32_t>(warp) * 66u;
-  const uint32_t r0 = static_cast<uint32_t>(g * a.row_bytes), r1 = static_cast<uint32_t>((g + 8) * a.row_bytes);
+  const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
   int s = 0;
   uint32_t ph = 0;
   for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {

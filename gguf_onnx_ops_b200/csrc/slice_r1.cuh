@@ -52,6 +52,10 @@ struct SliceArgs {
   bf16* x_norm_out;
   bf16* sum_out;
   float eps;
+  // slice_iq2_i8_rows_kernel: when use_tmap, a stage is one 2-D box of 16 rows x `stride` bytes
+  // (the row bytes plus a 16-byte pad, zero-filled past the row end) instead of one bulk copy
+  CUtensorMap tmap;
+  int use_tmap;
 };
 
 template <int F>
