@@ -660,7 +660,7 @@ int gguf_relu2(const void* x, void* y, int64_t n, void* stream) {
 
 namespace gguf_b200 {
 namespace {
-// MoeVerify iq2=3 as: zero the phase counters (first 4P bytes of out), one fused persistent kernel
+// MoeVerify iq2=3 as: zero the phase counters (first 4P bytes of out, moe_zero_kernel), one fused persistent kernel
 // (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.
 int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w, void* out,
                   void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s,
@@ -699,7 +699,7 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
-  cudaError_t e = cudaMemsetAsync(out, 0, static_cast<size_t>(P) * sizeof(int), s);
+  cudaError_t e = launch(moe_zero_kernel, dim3(1), dim3(128), 0, s, static_cast<int*>(out), P);
   if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
   static std::atomic<uint64_t> done{0};
   if (R == 1 && g_fast.load() == 1) {

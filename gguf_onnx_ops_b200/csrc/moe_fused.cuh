@@ -19,8 +19,8 @@
 // grid holds one CTA per SM, so the waits always end.  The leader prefetches the team's next item
 // while the team computes, which overlaps the W2 fetch with the tail of phase 1.
 //
-// done[] lives in the first bytes of the `out` tensor (zeroed by the host with cudaMemsetAsync
-// before the launch; `out` is only written by the finalize kernel that follows).
+// done[] lives in the first bytes of the `out` tensor (zeroed by moe_zero_kernel, launched just
+// before this kernel; `out` is only written by the finalize kernel that follows).
 #pragma once
 
 #include "engine.cuh"

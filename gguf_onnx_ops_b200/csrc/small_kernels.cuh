@@ -205,6 +205,19 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
 }
 
 // ---------------------------------------------------------------------------------------------
+// MoeVerify phase counters: n ints zeroed by one small kernel that takes part in the programmatic
+// dependent launch chain (a memset node would end it: the fused MoE kernel could then not be
+// resident, its tables filled, before the router finishes).  It waits for its predecessor (the
+// counters live in `out`, which the previous call's finalize wrote) and lets its dependent launch at
+// once; the dependent's own wait then covers these stores.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) moe_zero_kernel(int* __restrict__ p, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = 0;
+}
+
+// ---------------------------------------------------------------------------------------------
 // MoeVerify finalize: out[t, n] = bf16(sum_j w[t, j] * part[t*topk + j, n]), f32, j ascending
 // (src/bolt_ops.cu:627-662).  Pairs whose expert id is out of range contribute nothing.
 // ---------------------------------------------------------------------------------------------
