@@ -697,7 +697,7 @@ def bench_moe(R, steps, warmup, dev):
     calls = steps * rounds * copies
     us = ms * 1e3 / calls
     return dict(us_per_call=us, gbs=bytes_call / (us * 1e-6) / 1e9, weight_bytes=bytes_call, unique_experts=U,
-                copies=copies, rounds=rounds, kernels_per_call=5)
+                copies=copies, rounds=rounds, kernels_per_call=4)
 
 
 # ------------------------------------------------------------------------------------------------

@@ -706,15 +706,15 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     // one row: the integer single-row decode; tables at offset 0 and a smaller reduction buffer
     MoeFusedArgs b = a;
     b.off_stage = kI8Lut;
-    b.off_red = b.off_stage + kMoeTeams * 2 * a.stage_bytes;
-    b.off_bar = b.off_red + kMoeTeams * 2 * kMoeTeamWarps * 16 * 4;
-    b.off_grp = b.off_bar + kMoeTeams * 4 * 8;
+    b.off_red = b.off_stage + kMoeR1Teams * 2 * a.stage_bytes;
+    b.off_bar = b.off_red + kMoeR1Teams * 2 * kMoeTeamWarps * 16 * 4;
+    b.off_grp = b.off_bar + kMoeR1Teams * 4 * 8;
     const size_t smem1 = b.off_grp + grp;
     if (smem1 > static_cast<size_t>(kSmemBudgetMax))
       return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
     static std::atomic<uint64_t> done1{0};
     if ((rc = ensure_smem(moe_r1_i8_kernel, smem1, done1))) return rc;
-    e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeWarps * 32), smem1, s, b);
+    e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   } else {
     auto kern = moe_fused_kernel;

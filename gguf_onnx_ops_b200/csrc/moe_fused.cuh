@@ -47,6 +47,10 @@ struct MoeFusedArgs {
 
 constexpr int kMoeDoneWaitSite = 4;
 constexpr int kMoeTeams = 4, kMoeTeamWarps = 4, kMoeWarps = kMoeTeams * kMoeTeamWarps;
+// The single-row kernel runs five teams per CTA (20 warps): 5 x 148 teams cover a decode step's
+// phase-1 items (6 experts x I/16 = 672 at I = 1792) in one round, where four teams per CTA left
+// the last expert's fc1 tiles for a second round that its fc2 items then waited for.
+constexpr int kMoeR1Teams = 5, kMoeR1Warps = kMoeR1Teams * kMoeTeamWarps;
 
 __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeFusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -219,7 +223,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
 // converting the pair's h slice (read through L2) right before each.  Work split, staging, phase
 // order and outputs are those of moe_fused_kernel.  Tables (48 KB) sit at shared offset 0.
 // ---------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_r1_i8_kernel(const MoeFusedArgs a) {
+__global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const MoeFusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int team = warp / kMoeTeamWarps, tw = warp % kMoeTeamWarps;
@@ -237,7 +241,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_r1_i8_kernel(const MoeF
     }
     fence_mbar_init();
   }
-  i8_fill_tables<kMoeWarps * 32>(smem, threadIdx.x);
+  i8_fill_tables<kMoeR1Warps * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
   moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
   const int* s_uexp = s_grp + 3 * kMaxPairs;
@@ -254,7 +258,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_r1_i8_kernel(const MoeF
   pdl_launch_dependents();
 
   const int n1 = U * a.T1, n2 = U * a.T2, nitems = n1 + n2;
-  const int teams = kMoeTeams * static_cast<int>(gridDim.x);
+  const int teams = kMoeR1Teams * static_cast<int>(gridDim.x);
   const int first = team * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
   auto item_of = [&](int q, int& phase, int& u, int& tile) {
     if (q < n1) {
