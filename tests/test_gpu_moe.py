@@ -66,6 +66,11 @@ def test_route_ties_to_lower_index(cuda):
     assert np.allclose(w, 0.2)
 
 
+def assert_status_clean():
+    rc, site = _lib.device_status()
+    assert rc == 0, site
+
+
 def moe_gpu(z, idx, w, w1, w2, topk, dev):
     out, h, part, meta = ops.MoeVerify(bf16_t(z, dev), torch.from_numpy(idx).to(dev), torch.from_numpy(w).to(dev),
                                        u8_t(w1, dev), None, u8_t(w2, dev), None, topk=topk, iq2=3)
@@ -112,7 +117,8 @@ def test_moe_config_c3_routed(cuda, R):
     check_moe(c["z"], idx, w.astype(np.float32), c["w1"], c["w2"], 6, cuda)
 
 
-@pytest.mark.parametrize("R,E,Idim,topk", [(8, 12, 2048, 6), (8, 16, 256, 16), (1, 240, 1536, 9), (3, 5, 512, 5)])
+@pytest.mark.parametrize("R,E,Idim,topk", [(8, 12, 2048, 6), (8, 16, 256, 16), (1, 240, 1536, 9), (3, 5, 512, 5),
+                                          (1, 7, 512, 1), (2, 9, 256, 2), (5, 20, 768, 3), (4, 40, 512, 8)])
 def test_moe_shapes(cuda, R, E, Idim, topk):
     g = I.rng(R * 100 + E)
     z = I.bf16_normal(g, (R, 1024), 0.5)
@@ -121,6 +127,30 @@ def test_moe_shapes(cuda, R, E, Idim, topk):
     w1 = I.iq2_test_blocks(g, (E, Idim), 1024)
     w2 = I.iq2_test_blocks(g, (E, 1024), Idim)
     check_moe(z, idx, w, w1, w2, topk, cuda)
+
+
+def test_moe_out_of_range_experts(cuda):
+    """Pairs whose expert id is out of range contribute nothing to out (a row with none left is zero);
+    the fused weighted sum counts only the valid pairs of each row."""
+    R, E, Idim, topk = 3, 6, 512, 4
+    g = I.rng(77)
+    z = I.bf16_normal(g, (R, 1024), 0.5)
+    idx = np.array([[0, 3, 5, 1], [2, -1, 4, 9], [6, -3, 100, -1]], dtype=np.int32)
+    w = g.random((R, topk)).astype(np.float32)
+    w1 = I.iq2_test_blocks(g, (E, Idim), 1024)
+    w2 = I.iq2_test_blocks(g, (E, 1024), Idim)
+    out, _, part, _ = moe_gpu(z, idx, w, w1, w2, topk, cuda)
+    valid = (idx >= 0) & (idx < E)
+    idx_ok = np.where(valid, idx, 0).astype(np.int32)
+    w_ok = np.where(valid, w, 0.0).astype(np.float32)
+    d1 = {e: O.dequant_iq2_xxs(w1[e]) for e in range(E)}
+    d2 = {e: O.dequant_iq2_xxs(w2[e]) for e in range(E)}
+    rout, _, rpart = O.moe_ref(z, idx_ok, w_ok, d1, d2)
+    assert rel(out[:2], O.bf16_round(rout[:2])) < 5e-3
+    assert (out[2] == 0).all()
+    pv = valid.reshape(-1)
+    assert rel(part[pv], rpart[pv]) < 5e-3
+    assert_status_clean()
 
 
 def test_moe_rejects_bad_rows(cuda):
