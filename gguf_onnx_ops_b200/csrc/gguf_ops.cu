@@ -20,6 +20,7 @@
 #include "slice_r1.cuh"
 #include "slice_iq2_i8.cuh"
 #include "slice_iq2_i8_rows.cuh"
+#include "slice_q8_i8_rows.cuh"
 #include "slice_fp4_i8.cuh"
 #include "iq2_rowblock.cuh"
 #include "moe_fused.cuh"
@@ -445,6 +446,51 @@ int try_iq2_rows(const void* x, const void* w, void* y, int R, int N, int K, cud
   }
 }
 
+// Q8_0 2 <= R <= 4 * kNR on the integer tensor cores (slice_q8_i8_rows.cuh): 16 whole rows per
+// stage at pitch row bytes + 16, two or more stages.
+template <int kW, int kNR>
+int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s) {
+  SliceArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.x = static_cast<const bf16*>(x);
+  a.y = static_cast<bf16*>(y);
+  a.R = R;
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 32 * 34;  // K % 256 == 0: a multiple of 16
+  a.tiles = (N + 15) / 16;
+  a.stride = a.row_bytes + 16;
+  a.stage_bytes = (16 * a.stride + 127) & ~127;
+  const int red_per_stage = kW * 4 * kNR * 16 * 4 + 4;  // reduction slot + counter
+  a.stages = std::min(4, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return -1;  // does not fit: the caller falls back to the engine
+  a.off_stage = 0;
+  a.off_red = a.stages * a.stage_bytes;
+  a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = slice_q8_i8_rows_kernel<kW, kNR>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("few-row Q8_0 GEMV launch", e);
+  return GGUF_OK;
+}
+
+// Dispatches 2 <= R <= 8 Q8_0 to the few-row integer kernel when K allows it; -1 otherwise.
+int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s) {
+  if (g_fast.load() != 1 || R < 2 || R > 16) return -1;
+  if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<16, 4>(x, w, y, R, N, K, s) : -1;
+  const bool two = R > 4;
+  switch (K) {
+    case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s);
+    case 4096: return two ? run_slice_q8_i8_rows<16, 2>(x, w, y, R, N, K, s) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s);
+    case 5120: return two ? run_slice_q8_i8_rows<20, 2>(x, w, y, R, N, K, s) : run_slice_q8_i8_rows<20, 1>(x, w, y, R, N, K, s);
+    default: return -1;
+  }
+}
+
 // IQ2_XXS R = 1, 16-row blocks owned by warp pairs (iq2_rowblock.cuh).  Returns -1 when the shape
 // does not fit its plan (K % 512, one stage of every pair in shared memory).
 int run_iq2_rowblock(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
@@ -564,6 +610,9 @@ int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (R == 1) {
     const int rc = try_slice_r1<kFmtQ8>(x, w, nullptr, y, (int)N, (int)K, s);
+    if (rc >= 0) return rc;
+  } else {
+    const int rc = try_q8_rows(x, w, y, (int)R, (int)N, (int)K, s);
     if (rc >= 0) return rc;
   }
   return R <= 8 ? run_dense<kFmtQ8, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)

@@ -32,12 +32,13 @@ __device__ __forceinline__ void imma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
 
-// B fragments and per-(activation row, group) constants of one 256-element slice.
-template <int kNR>
+// B fragments and per-(activation row, group) constants of one 256-element slice (kOff: with the
+// offset sums that an unsigned A operand needs).
+template <int kNR, bool kOff = true>
 struct I8RowsX {
-  uint32_t b[kNR][8][2];  // [MMA set][group][k-slots 4t.. / 4t+16..]
-  float xs[kNR][8];       // 2^(E - 13) of activation row 4m + t, group j (this lane's C columns)
-  int nxoff[kNR][8];      // -64 * sum(x_int) of the same (the low-limb column's C input)
+  uint32_t b[kNR][8][2];           // [MMA set][group][k-slots 4t.. / 4t+16..]
+  float xs[kNR][8];                // 2^(E - 13) of activation row 4m + t, group j (this lane's C columns)
+  int nxoff[kOff ? kNR : 1][8];    // -64 * sum(x_int) of the same (the low-limb column's C input)
 };
 
 // Lane (g, t), MMA set m: B column g = activation row 4m + (g >> 1), limb g & 1; the lane converts
@@ -49,8 +50,8 @@ struct I8RowsX {
 // r = p + (1.5 * 2^23 + c) rounds p to an integer (nearest, ties to even) in the low mantissa bits:
 // the low 16 bits of r are those of x_int + c.  The low-limb lanes take c = 0 and byte 0 (x_int mod
 // 256, the s8 low limb); the high-limb lanes take c = 128 and byte 1 ((x_int + 128) >> 8).
-template <int kNR>
-__device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice, I8RowsX<kNR>& f) {
+template <int kNR, bool kOff = true>
+__device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice, I8RowsX<kNR, kOff>& f) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const bool lo_limb = (g & 1) != 0;
   const uint32_t c = lo_limb ? 0u : 128u, k = lo_limb ? 0u : 1u;
@@ -87,14 +88,16 @@ __device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice
         r[i] = __float_as_uint((v * s1) * s2 + magic);
         rsum += r[i];
       }
-      int xsum = static_cast<int>(rsum - 8u * (0x4B400000u + c));  // sum of x_int (mod 2^32, exact)
-      xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
-      xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
       f.b[m][j][0] = __byte_perm(__byte_perm(r[0], r[1], sel), __byte_perm(r[2], r[3], sel), 0x5410);
       f.b[m][j][1] = __byte_perm(__byte_perm(r[4], r[5], sel), __byte_perm(r[6], r[7], sel), 0x5410);
       // this lane's C columns (2t, 2t+1) are activation row 4m + t, converted by quad 2t (lane 8t)
       f.xs[m][j] = ldexpf(1.0f, __shfl_sync(0xffffffffu, emax, 8 * t) - 140);  // 2^(E - 13), E = emax - 127
-      f.nxoff[m][j] = -64 * __shfl_sync(0xffffffffu, xsum, 8 * t);
+      if constexpr (kOff) {
+        int xsum = static_cast<int>(rsum - 8u * (0x4B400000u + c));  // sum of x_int (mod 2^32, exact)
+        xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+        xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+        f.nxoff[m][j] = -64 * __shfl_sync(0xffffffffu, xsum, 8 * t);
+      }
     }
   }
 }

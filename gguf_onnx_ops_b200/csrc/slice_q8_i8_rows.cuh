@@ -1,0 +1,140 @@
+// Few-row Q8_0 GEMV (2 <= R <= 4 * kNR) on the integer tensor cores.  A Q8_0 block is an fp16 scale
+// d and 32 int8 quants, so the quants are the MMA's A operand as they are (s8, no decode step):
+// the launch is bound by HBM and by the per-block epilogue, not by a codebook.
+//
+// MMA layout (mma.sync m16n8k32, s8 x s8 -> s32), as in the few-row IQ2_XXS kernel
+// (slice_iq2_i8_rows.cuh): one MMA covers one 32-element block of a 16-row tile; lane (g, t) supplies
+// quants 8t..8t+7 of rows g and g+8 (k-slots 4t..4t+3 and 4t+16..4t+19), the 8 columns are four
+// activation rows x two signed limbs of x_int = x * 2^(13 - E) (i8_rows_x: E per 32-element group),
+// and C column pair (2t, 2t+1) of lane (g, t) is activation row t.  Epilogue per (row, block):
+// y += (256 C_hi + C_lo) * 2^(E - 13) * d, in fp32.  No offset term: the quants are signed.
+//
+// Staging: a tile is 16 whole rows (K / 32 * 34 bytes each), one bulk copy per row into a stage
+// whose row pitch is the row bytes + 16, which keeps the eight quads' loads off a common bank (a
+// pitch of 0 mod 32 words would put all eight rows on the same banks).  Rows are 17K/16 bytes, so a
+// 16-row tile is large (K = 4096: 68 KB); two stages already hold ~140 KB of a GPU-wide ~20 MB in
+// flight, and the per-tile compute is well below the tile's HBM time.
+#pragma once
+
+#include "slice_iq2_i8_rows.cuh"
+
+namespace gguf_b200 {
+
+__device__ __forceinline__ void imma_s8s8_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// One 16-row x 256-column slice (8 Q8_0 blocks per row) against the kNR MMA sets; st = the stage,
+// r0 / r1 = byte offsets of rows g / g+8, so = the slice's byte offset in a row (272 * slice).
+template <int kNR>
+__device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t so,
+                                              const I8RowsX<kNR, false>& f, float (&acc)[kNR][2]) {
+  const uint32_t t = threadIdx.x & 3;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t ob = so + 34u * j;  // block j: d at ob, quants at ob + 2 (4-byte aligned iff j is odd)
+    const uint2 q0 = lds8(st, r0 + ob + 2u + 8u * t, (j & 1) != 0);
+    const uint2 q1 = lds8(st, r1 + ob + 2u + 8u * t, (j & 1) != 0);
+    const float d0 = fp16_bits_to_f32(ld_u16(st, r0 + ob)), d1 = fp16_bits_to_f32(ld_u16(st, r1 + ob));
+#pragma unroll
+    for (int m = 0; m < kNR; ++m) {
+      int cc[4];
+      imma_s8s8_c(cc, q0.x, q1.x, q0.y, q1.y, f.b[m][j][0], f.b[m][j][1]);
+      const float p = f.xs[m][j];
+      acc[m][0] = fmaf(static_cast<float>(cc[0] * 256 + cc[1]), p * d0, acc[m][0]);
+      acc[m][1] = fmaf(static_cast<float>(cc[2] * 256 + cc[3]), p * d1, acc[m][1]);
+    }
+  }
+}
+
+// Warp w owns slice w of K for the whole launch; the last warp to finish a tile sums the stage's
+// reduction slot in warp order (deterministic), stores y [R, N] and refills the stage (the
+// last-arriver scheme of slice_iq2_i8_kernel).
+template <int kW, int kNR>
+__global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
+  constexpr int kRX = 4 * kNR;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+  uint8_t* stages = smem + a.off_stage;
+  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [stages][kW][kRX][16]
+  int* cnt = reinterpret_cast<int*>(red + a.stages * kW * kRX * 16);  // [stages]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      cnt[s] = 0;
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // stage s <- tile `tile` (the calling warp): lane 0 announces the bytes, lanes < rows copy a row each
+  auto fill = [&](int s, int tile) {
+    const int rv = min(16, a.N - tile * 16);
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes));
+    __syncwarp();
+    if (lane < rv)
+      bulk_g2s(stages + s * a.stage_bytes + lane * a.stride, a.w + (static_cast<int64_t>(tile) * 16 + lane) * a.row_bytes,
+               static_cast<uint32_t>(a.row_bytes), &full[s]);
+  };
+  if (warp == 0)
+    for (int j = 0; j < a.stages; ++j) {
+      const int tile = blockIdx.x + j * gridDim.x;
+      if (tile < a.tiles) fill(j, tile);
+    }
+  pdl_wait();  // x is produced by the previous kernel
+
+  I8RowsX<kNR, false> xf;  // signed quants: no offset sums
+  i8_rows_x<kNR, false>(a.x, a.R, a.K, warp, xf);
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t so = static_cast<uint32_t>(warp) * 272u;
+  const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
+  int s = 0;
+  uint32_t ph = 0;
+  for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
+    mbar_wait(&full[s], ph, kSiteFullWait);
+    float acc[kNR][2];
+#pragma unroll
+    for (int m = 0; m < kNR; ++m) acc[m][0] = acc[m][1] = 0.f;
+    q8_rows_slice<kNR>(stages + s * a.stage_bytes, r0, r1, so, xf, acc);
+
+    float* rb = red + (s * kW + warp) * kRX * 16;
+#pragma unroll
+    for (int m = 0; m < kNR; ++m) {
+      rb[(4 * m + t) * 16 + g] = acc[m][0];
+      rb[(4 * m + t) * 16 + g + 8] = acc[m][1];
+    }
+    __syncwarp();  // orders the lanes' slot writes before lane 0's release below
+    int last = 0;
+    if (lane == 0) last = atom_add_acq_rel_cta(&cnt[s], 1) == kW - 1;
+    if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this tile are in the slot
+      const float* rs = red + s * kW * kRX * 16;
+#pragma unroll
+      for (int o = lane; o < kRX * 16; o += 32) {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};  // fixed summation order: 4 strided partial sums, then a tree
+#pragma unroll
+        for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rs[w2 * kRX * 16 + o];
+        const int xr = o >> 4, row = tile * 16 + (o & 15);
+        if (xr < a.R && row < a.N) a.y[static_cast<int64_t>(xr) * a.N + row] = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+      }
+      __syncwarp();
+      if (lane == 0) cnt[s] = 0;
+      const int next = tile + a.stages * static_cast<int>(gridDim.x);
+      if (next < a.tiles) {
+        fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
+        fill(s, next);
+      }
+    }
+    if (++s == a.stages) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+}
+
+}  // namespace gguf_b200

@@ -229,6 +229,26 @@ def test_iq2_few_row_integer_kernel(cuda, R, N, K, xscale):
     assert_device_ok()
 
 
+@pytest.mark.parametrize("R", [2, 3, 4, 5, 8, 12, 16])
+@pytest.mark.parametrize("N,K,xscale", [(37, 2048, 1.0), (200, 4096, 1.0), (1000, 4096, 3000.0), (61, 5120, 1.0)])
+def test_q8_few_row_integer_kernel(cuda, R, N, K, xscale):
+    """The few-row Q8_0 kernel (2 <= R <= 16: the int8 quants as the MMA's A operand, activation rows x
+    signed limbs as columns; R > 8 at K = 4096 only) against the oracle and the generic engine, ragged
+    N and outliers."""
+    _, w, _ = I.gemv_case("q8_0", 1, N, K, seed=N + K + R)
+    x = I.bf16_normal(I.rng(N * K + R), (R, K), xscale)
+    x[:, 7] = O.bf16_bits(O.bf16_to_f32(x[:, 7]) * np.float32(300.0))  # bf16 bits: one outlier column
+    y = run_gemv("q8_0", x, w, {}, cuda)
+    assert rel(y, oracle_y("q8_0", x, w, {})) < TOL
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_gemv("q8_0", x, w, {}, cuda)
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+    assert_device_ok()
+
+
 @pytest.mark.parametrize("K", [2048, 4096, 5120, 6144, 8192])
 def test_nvfp4_single_row_integer_kernel(cuda, K):
     """The single-row NVFP4 kernels (bf16 slice, the default, and the integer-decode variant, mode 4)
