@@ -449,8 +449,10 @@ int try_iq2_rows(const void* x, const void* w, void* y, int R, int N, int K, cud
 // Q8_0 2 <= R <= 4 * kNR on the integer tensor cores (slice_q8_i8_rows.cuh): 16 whole rows per
 // stage at pitch row bytes + 16, two or more stages.
 template <int kW, int kNR>
-int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s) {
+int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s,
+                         const PeerOut* po) {
   SliceArgs a = {};
+  if (po) a.po = *po;
   a.w = static_cast<const uint8_t*>(w);
   a.x = static_cast<const bf16*>(x);
   a.y = static_cast<bf16*>(y);
@@ -478,15 +480,19 @@ int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, in
   return GGUF_OK;
 }
 
-// Dispatches 2 <= R <= 8 Q8_0 to the few-row integer kernel when K allows it; -1 otherwise.
-int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s) {
-  if (g_fast.load() != 1 || R < 2 || R > 16) return -1;
-  if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<16, 4>(x, w, y, R, N, K, s) : -1;
+// Dispatches 1 <= R <= 16 Q8_0 to the few-row integer kernel when K allows it (R > 8: K = 4096
+// only); -1 otherwise.  One row uses four-row MMA columns with three empty rows: the quants need
+// no decode, so the kernel is HBM-bound at large N even so (C4 R = 1: 91 µs, 0.96 of peak, where
+// the bf16 slice kernel took 115 µs).
+int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s,
+                const PeerOut* po = nullptr) {
+  if (g_fast.load() != 1 || R < 1 || R > 16) return -1;
+  if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<16, 4>(x, w, y, R, N, K, s, po) : -1;
   const bool two = R > 4;
   switch (K) {
-    case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s);
-    case 4096: return two ? run_slice_q8_i8_rows<16, 2>(x, w, y, R, N, K, s) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s);
-    case 5120: return two ? run_slice_q8_i8_rows<20, 2>(x, w, y, R, N, K, s) : run_slice_q8_i8_rows<20, 1>(x, w, y, R, N, K, s);
+    case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s, po);
+    case 4096: return two ? run_slice_q8_i8_rows<16, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s, po);
+    case 5120: return two ? run_slice_q8_i8_rows<20, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<20, 1>(x, w, y, R, N, K, s, po);
     default: return -1;
   }
 }
@@ -556,10 +562,16 @@ int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
   }
 }
 
-// Row-split shard: the bf16 slice kernel for R = 1 (K in its instantiated set), else the engine.
+// Row-split shard: Q8_0 through the few-row integer kernel (any R it takes; R = 1 at K = 2048 stays
+// on the bf16 slice kernel as in gguf_q8_0_gemv), else the bf16 slice kernel for R = 1 (K in its
+// instantiated set), else the engine.
 template <int F>
 int run_rowsplit(const void* x, const void* w, const float* gscale, int R, int rows, int K, cudaStream_t s,
                  const PeerOut& po) {
+  if (F == kFmtQ8 && !(R == 1 && K == 2048)) {
+    const int rc = try_q8_rows(x, w, nullptr, R, rows, K, s, &po);
+    if (rc >= 0) return rc;
+  }
   const bool slice_ok = R == 1 && (K / FmtInfo<F>::kBlock * FmtInfo<F>::kBytes) % 16 == 0;
   if (slice_ok) {
     switch (K) {
@@ -608,11 +620,13 @@ int gguf_q8_0_gemv(const void* x, const void* w, void* y, int64_t R, int64_t N, 
     return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: needs B [N, (K/32)*34], K % 64 == 0 and 1..16 rows" + dims(R, N, K));
   if (!aligned(w, 16) || !aligned(x, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "Q8Gemv gguf=1: x and w must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {  // R = 1 at K = 2048: the bf16 slice kernel (more warps per SM than the 8 of the few-row kernel)
+    const int rc = (R == 1 && K == 2048) ? try_slice_r1<kFmtQ8>(x, w, nullptr, y, (int)N, (int)K, s)
+                                         : try_q8_rows(x, w, y, (int)R, (int)N, (int)K, s);
+    if (rc >= 0) return rc;
+  }
   if (R == 1) {
     const int rc = try_slice_r1<kFmtQ8>(x, w, nullptr, y, (int)N, (int)K, s);
-    if (rc >= 0) return rc;
-  } else {
-    const int rc = try_q8_rows(x, w, y, (int)R, (int)N, (int)K, s);
     if (rc >= 0) return rc;
   }
   return R <= 8 ? run_dense<kFmtQ8, 1>(x, w, nullptr, y, (int)R, (int)N, (int)K, s)

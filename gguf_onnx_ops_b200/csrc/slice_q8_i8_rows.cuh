@@ -1,4 +1,4 @@
-// Few-row Q8_0 GEMV (2 <= R <= 4 * kNR) on the integer tensor cores.  A Q8_0 block is an fp16 scale
+// Few-row Q8_0 GEMV (1 <= R <= 4 * kNR) on the integer tensor cores.  A Q8_0 block is an fp16 scale
 // d and 32 int8 quants, so the quants are the MMA's A operand as they are (s8, no decode step):
 // the launch is bound by HBM and by the per-block epilogue, not by a codebook.
 //
@@ -8,6 +8,9 @@
 // activation rows x two signed limbs of x_int = x * 2^(13 - E) (i8_rows_x: E per 32-element group),
 // and C column pair (2t, 2t+1) of lane (g, t) is activation row t.  Epilogue per (row, block):
 // y += (256 C_hi + C_lo) * 2^(E - 13) * d, in fp32.  No offset term: the quants are signed.
+//
+// Row-split shards (a.po.npeer > 0): y goes to every GPU of the group with peer stores, and the
+// launch ends once every GPU's shard is present (peer_complete), as in slice_r1_kernel.
 //
 // Staging: a tile is 16 whole rows (K / 32 * 34 bytes each), one bulk copy per row into a stage
 // whose row pitch is the row bytes + 16, which keeps the eight quads' loads off a common bank (a
@@ -120,7 +123,11 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
 #pragma unroll
         for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rs[w2 * kRX * 16 + o];
         const int xr = o >> 4, row = tile * 16 + (o & 15);
-        if (xr < a.R && row < a.N) a.y[static_cast<int64_t>(xr) * a.N + row] = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+        if (xr < a.R && row < a.N) {
+          const bf16 yv = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+          if (a.po.npeer) peer_store(a.po, xr, row, yv);  // row-split shard: into every GPU's y
+          else a.y[static_cast<int64_t>(xr) * a.N + row] = yv;
+        }
       }
       __syncwarp();
       if (lane == 0) cnt[s] = 0;
@@ -134,6 +141,10 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
       s = 0;
       ph ^= 1u;
     }
+  }
+  if (a.po.npeer) {  // all-gather completion: every last arriver's stores are behind the barrier
+    __syncthreads();
+    if (threadIdx.x == 0) peer_complete(a.po);
   }
 }
 
