@@ -434,10 +434,12 @@ int run_slice_iq2_i8_rows(const void* x, const void* w, void* y, int R, int N, i
   return GGUF_OK;
 }
 
-// Dispatches 2 <= R <= 4 IQ2_XXS to the few-row integer kernel when K allows it; -1 otherwise.  (Five
-// to eight rows, a second MMA set on the same decoded tile, measured no faster than the engine.)
+// Dispatches 2 <= R <= 8 IQ2_XXS to the few-row integer kernel when K allows it (R > 4, a second MMA
+// set on the same decoded tile: K = 4096 only, 17.5 against the engine's 18.2-18.5 µs at C1); -1
+// otherwise.
 int try_iq2_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s) {
-  if (g_fast.load() != 1 || R < 2 || R > 4) return -1;
+  if (g_fast.load() != 1 || R < 2 || R > 8) return -1;
+  if (R > 4) return K == 4096 ? run_slice_iq2_i8_rows<16, 2>(x, w, y, R, N, K, s) : -1;
   switch (K) {
     case 2048: return run_slice_iq2_i8_rows<8, 1>(x, w, y, R, N, K, s);
     case 4096: return run_slice_iq2_i8_rows<16, 1>(x, w, y, R, N, K, s);

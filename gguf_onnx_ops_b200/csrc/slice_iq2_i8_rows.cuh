@@ -1,6 +1,6 @@
 // Few-row IQ2_XXS GEMV on the integer tensor cores: the single-row kernel's exact u8 weights
 // (64 + s * m, from the same shared tables, slice_iq2_i8.cuh) against 4 * kNR activation rows per
-// launch (the host uses kNR = 1, i.e. 2 <= R <= 4; kNR = 2 measured no faster than the engine).
+// launch (kNR = 1 for 2 <= R <= 4, kNR = 2 for 5 <= R <= 8 at K = 4096).
 //
 // MMA layout (mma.sync m16n8k32, u8 x s8 -> s32).  One MMA covers one 32-element group of a 16-row
 // tile: its k-slots 4t..4t+3 / 4t+16..4t+19 hold elements 8t..8t+3 / 8t+4..8t+7 of the group, so lane
@@ -41,59 +41,65 @@ struct I8RowsX {
   int nxoff[kOff ? kNR : 1][8];    // -64 * sum(x_int) of the same (the low-limb column's C input)
 };
 
-// Lane (g, t), MMA set m: B column g = activation row 4m + (g >> 1), limb g & 1; the lane converts
-// elements 8t..8t+7 of each group of that row (the quad g covers the group: its maximum and sum are
-// reduced over the quad).  Rows >= R read as zeros.
+// Lane (g, t), MMA set m: B column g = activation row 4m + (g >> 1), limb g & 1, k-slots of elements
+// 8t..8t+7 of each group of that row.  The two lanes of a column pair (g even: high limb, g odd: low
+// limb, lanes l and l ^ 4) share the conversion: the even lane converts elements 8t..8t+3, the odd
+// one 8t+4..8t+7, each forms both limbs of its four and one shuffle swaps the word the other needs.
+// Group maximum and sum are reduced over the eight lanes of the column pair's two quads.  Rows >= R
+// read as zeros.
 //
 // Conversion without branches: p = x * 2^(13 - E) as two exact power-of-two products (the first is
 // 2^64 for groups below 2^-63, so that neither factor leaves the normal range), then
-// r = p + (1.5 * 2^23 + c) rounds p to an integer (nearest, ties to even) in the low mantissa bits:
-// the low 16 bits of r are those of x_int + c.  The low-limb lanes take c = 0 and byte 0 (x_int mod
-// 256, the s8 low limb); the high-limb lanes take c = 128 and byte 1 ((x_int + 128) >> 8).
+// r = p + (1.5 * 2^23 + 128) rounds p to an integer (nearest, ties to even) whose low 16 bits are
+// those of x_int + 128: byte 1 is the high limb (x_int + 128) >> 8 and byte 0 ^ 0x80 the low limb
+// x_int mod 256.
 template <int kNR, bool kOff = true>
 __device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice, I8RowsX<kNR, kOff>& f) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const bool lo_limb = (g & 1) != 0;
-  const uint32_t c = lo_limb ? 0u : 128u, k = lo_limb ? 0u : 1u;
-  const float magic = 12582912.0f + static_cast<float>(c);
-  const uint32_t sel = k | ((4u + k) << 4);  // [r0 byte k, r1 byte k, ...]
-  uint4 xv[kNR][8];
+  const bool odd = (g & 1) != 0;
+  const float magic = 12582912.0f + 128.0f;
+  uint2 xv[kNR][8];
 #pragma unroll
   for (int m = 0; m < kNR; ++m) {
     const int xr = 4 * m + (g >> 1);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      xv[m][j] = xr < R ? ldg128(x + static_cast<int64_t>(xr) * K + slice * 256 + 32 * j + 8 * t)
-                        : make_uint4(0u, 0u, 0u, 0u);
+      xv[m][j] = xr < R ? __ldg(reinterpret_cast<const uint2*>(x + static_cast<int64_t>(xr) * K + slice * 256 + 32 * j +
+                                                               8 * t + (odd ? 4 : 0)))
+                        : make_uint2(0u, 0u);
   }
 #pragma unroll
   for (int m = 0; m < kNR; ++m) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint32_t wv[4] = {xv[m][j].x, xv[m][j].y, xv[m][j].z, xv[m][j].w};
+      const uint32_t wv[2] = {xv[m][j].x, xv[m][j].y};
       // largest |x| of the group: bf16 magnitudes order like their bit patterns
-      const uint32_t m2 = __vmaxu2(__vmaxu2(wv[0] & 0x7FFF7FFFu, wv[1] & 0x7FFF7FFFu),
-                                   __vmaxu2(wv[2] & 0x7FFF7FFFu, wv[3] & 0x7FFF7FFFu));
+      const uint32_t m2 = __vmaxu2(wv[0] & 0x7FFF7FFFu, wv[1] & 0x7FFF7FFFu);
       uint32_t mb = max(m2 & 0xFFFFu, m2 >> 16);
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
       mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
       mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
       const int emax = max(1, static_cast<int>(mb >> 7));  // biased exponent of the maximum, E = emax - 127
       const bool tiny = emax < 64;
       const float s1 = tiny ? 18446744073709551616.0f : 1.0f;  // 2^64
       const float s2 = __uint_as_float(static_cast<uint32_t>(267 - emax - (tiny ? 64 : 0)) << 23);  // 2^(140 - emax) / s1
-      uint32_t r[8], rsum = 0u;
+      uint32_t r[4], rsum = 0u;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
         const float v = __uint_as_float(i & 1 ? (wv[i >> 1] & 0xFFFF0000u) : (wv[i >> 1] << 16));
         r[i] = __float_as_uint((v * s1) * s2 + magic);
         rsum += r[i];
       }
-      f.b[m][j][0] = __byte_perm(__byte_perm(r[0], r[1], sel), __byte_perm(r[2], r[3], sel), 0x5410);
-      f.b[m][j][1] = __byte_perm(__byte_perm(r[4], r[5], sel), __byte_perm(r[6], r[7], sel), 0x5410);
-      // this lane's C columns (2t, 2t+1) are activation row 4m + t, converted by quad 2t (lane 8t)
+      const uint32_t hi = __byte_perm(__byte_perm(r[0], r[1], 0x0051u), __byte_perm(r[2], r[3], 0x0051u), 0x5410u);
+      const uint32_t lo = __byte_perm(__byte_perm(r[0], r[1], 0x0040u), __byte_perm(r[2], r[3], 0x0040u), 0x5410u) ^ 0x80808080u;
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, odd ? hi : lo, 4);  // partner's word for my column
+      f.b[m][j][0] = odd ? other : hi;  // elements 8t..8t+3
+      f.b[m][j][1] = odd ? lo : other;  // elements 8t+4..8t+7
+      // this lane's C columns (2t, 2t+1) are activation row 4m + t, converted by quads 2t, 2t + 1 (lane 8t)
       f.xs[m][j] = ldexpf(1.0f, __shfl_sync(0xffffffffu, emax, 8 * t) - 140);  // 2^(E - 13), E = emax - 127
       if constexpr (kOff) {
-        int xsum = static_cast<int>(rsum - 8u * (0x4B400000u + c));  // sum of x_int (mod 2^32, exact)
+        int xsum = static_cast<int>(rsum - 4u * (0x4B400000u + 128u));  // sum of x_int (mod 2^32, exact)
+        xsum += __shfl_xor_sync(0xffffffffu, xsum, 4);
         xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
         xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
         f.nxoff[m][j] = -64 * __shfl_sync(0xffffffffu, xsum, 8 * t);

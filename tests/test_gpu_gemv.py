@@ -212,9 +212,9 @@ def test_single_row_fast_path(cuda, op, N, K, xscale):
 @pytest.mark.parametrize("R", [2, 3, 4, 5, 8])
 @pytest.mark.parametrize("N,K,xscale", [(37, 2048, 1.0), (200, 4096, 1.0), (1000, 4096, 3000.0), (61, 5120, 1.0)])
 def test_iq2_few_row_integer_kernel(cuda, R, N, K, xscale):
-    """The few-row IQ2_XXS kernel (2 <= R <= 4: activation rows x limbs as MMA columns; R = 5, 8 take
-    the engine) against the oracle and the generic engine, ragged N, one outlier column per row and a
-    x3000 scale."""
+    """The few-row IQ2_XXS kernel (2 <= R <= 8: activation rows x limbs as MMA columns; R > 4 at
+    K = 4096 only, else the engine) against the oracle and the generic engine, ragged N, one outlier
+    column per row and a x3000 scale."""
     _, w, _ = I.gemv_case("iq2_xxs", 1, N, K, seed=N + K + R)
     x = I.bf16_normal(I.rng(N * K + R), (R, K), xscale)
     x[:, 7] = O.bf16_bits(O.bf16_to_f32(x[:, 7]) * np.float32(300.0))  # bf16 bits: one outlier column
