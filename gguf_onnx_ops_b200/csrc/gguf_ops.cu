@@ -21,6 +21,7 @@
 #include "slice_iq2_i8.cuh"
 #include "slice_iq2_i8_rows.cuh"
 #include "slice_q8_i8_rows.cuh"
+#include "slice_fp4_rows.cuh"
 #include "slice_fp4_i8.cuh"
 #include "iq2_rowblock.cuh"
 #include "moe_fused.cuh"
@@ -499,6 +500,62 @@ int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cuda
   }
 }
 
+// NVFP4 2 <= R <= 8 on the bf16 tensor cores with the activation rows as MMA columns
+// (slice_fp4_rows.cuh): 16 whole rows per stage at pitch row bytes + 32.
+template <int kW>
+int run_slice_fp4_rows(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
+  SliceArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.x = static_cast<const bf16*>(x);
+  a.gscale = gscale;
+  a.y = static_cast<bf16*>(y);
+  a.R = R;
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 64 * 36;  // K % 256 == 0: a multiple of 16
+  a.tiles = (N + 15) / 16;
+  a.stride = a.row_bytes + 32;  // row words = 8 or 24 mod 32 for K = 2048, 4096, 5120
+  a.stage_bytes = (16 * a.stride + 127) & ~127;
+  const int lut = 512, red_per_stage = kW * 8 * 16 * 4 + 4;
+  a.stages = std::min(4, (kSmemBudgetMax - lut - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return -1;
+  a.off_stage = lut;
+  a.off_red = lut + a.stages * a.stage_bytes;
+  a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = slice_fp4_rows_kernel<kW>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("few-row NVFP4 GEMV launch", e);
+  return GGUF_OK;
+}
+
+template <int F>
+int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s);
+
+// Dispatches 2 <= R <= 16 NVFP4 to the few-row kernel when K allows it (R > 8: two launches, rows
+// 0..7 and 8..R-1, each streaming the weights once); -1 otherwise.
+int try_fp4_rows(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
+  if (g_fast.load() != 1 || R < 2 || R > 16) return -1;
+  if (K != 2048 && K != 4096 && K != 5120) return -1;
+  if (R > 8) {
+    const int rc = try_fp4_rows(x, w, gscale, y, 8, N, K, s);
+    if (rc != GGUF_OK) return rc;
+    const bf16* x8 = static_cast<const bf16*>(x) + static_cast<int64_t>(8) * K;
+    bf16* y8 = static_cast<bf16*>(y) + static_cast<int64_t>(8) * N;
+    return R - 8 == 1 ? try_slice_r1<kFmtFP4>(x8, w, gscale, y8, N, K, s) : try_fp4_rows(x8, w, gscale, y8, R - 8, N, K, s);
+  }
+  switch (K) {
+    case 2048: return run_slice_fp4_rows<8>(x, w, gscale, y, R, N, K, s);
+    case 4096: return run_slice_fp4_rows<16>(x, w, gscale, y, R, N, K, s);
+    case 5120: return run_slice_fp4_rows<20>(x, w, gscale, y, R, N, K, s);
+    default: return -1;
+  }
+}
+
 // IQ2_XXS R = 1, 16-row blocks owned by warp pairs (iq2_rowblock.cuh).  Returns -1 when the shape
 // does not fit its plan (K % 512, one stage of every pair in shared memory).
 int run_iq2_rowblock(const void* x, const void* w, void* y, int N, int K, cudaStream_t s) {
@@ -664,6 +721,9 @@ int gguf_nvfp4_gemv(const void* x, const void* w, const float* gscale, void* y, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (R == 1) {
     const int rc = try_slice_r1<kFmtFP4>(x, w, gscale, y, (int)N, (int)K, s);
+    if (rc >= 0) return rc;
+  } else {
+    const int rc = try_fp4_rows(x, w, gscale, y, (int)R, (int)N, (int)K, s);
     if (rc >= 0) return rc;
   }
   return R <= 8 ? run_dense<kFmtFP4, 1>(x, w, gscale, y, (int)R, (int)N, (int)K, s)

@@ -1,0 +1,150 @@
+// Few-row NVFP4 GEMV (2 <= R <= 8) on the bf16 tensor cores: the activation rows are the 8 columns
+// of mma.sync m16n8k16, so one decoded tile serves every row (the single-row kernel, slice_r1.cuh,
+// spends its columns on a block-diagonal B instead).
+//
+// Decode (as slice_r1.cuh): a nibble n becomes the bf16 pattern of E2M1(n) * 2^-126 with
+// (n * 0x1040) & 0x81C0, and one bf16 multiply by the sub-block's UE4M3 scale * 2^110 (a 256-entry
+// table in shared memory) makes the weight exact and normal; the epilogue multiplies by
+// 2^16 * gscale.  Because the scale is inside A, the MMAs of a whole slice accumulate into one C:
+// no per-sub-block epilogue.
+//
+// k-slot mapping: lane (g, t) decodes sub-block t (elements 16t..16t+15) of every 64-element block
+// of its slice, for rows g and g+8.  In GGUF NVFP4, element j < 8 of a sub-block is the low nibble
+// of its byte j and element j + 8 the high nibble, so the sub-block's two nibble words give, per
+// MMA q = 0..3 (word q >> 1, shifted by 8 for odd q), the element pairs (0,2) (8,10), (1,3) (9,11),
+// (4,6) (12,14), (5,7) (13,15) as k-slots (2t, 2t+1) and (2t+8, 2t+9).  The B fragment of column g
+// is activation row g at the same element pairs (rows >= R read as zeros), fixed for the launch;
+// C column pair (2t, 2t+1) of lane (g, t) is activation rows 2t, 2t+1.
+//
+// Staging and reduction as the few-row Q8_0 kernel (slice_q8_i8_rows.cuh): 16 whole rows per stage,
+// one bulk copy per row at a pitch of row bytes + 32 (with the row words = 0 or 16 mod 32 the eight
+// quads' loads would share banks), the last warp to finish a tile sums the slot in warp order.
+#pragma once
+
+#include "slice_r1.cuh"
+#include "slice_iq2_i8.cuh"
+
+namespace gguf_b200 {
+
+template <int kW>
+__global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid_constant__ SliceArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
+  uint8_t* stages = smem + a.off_stage;
+  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [stages][kW][8 activation rows][16]
+  int* cnt = reinterpret_cast<int*>(red + a.stages * kW * 8 * 16);  // [stages]
+  const uint16_t* fp4lut = reinterpret_cast<const uint16_t*>(smem);  // [256] scale * 2^110, bf16 bits
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      cnt[s] = 0;
+    }
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 256; i += kW * 32)
+    reinterpret_cast<uint16_t*>(smem)[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));
+  __syncthreads();
+  pdl_launch_dependents();
+
+  // stage s <- tile `tile` (the calling warp): lane 0 announces the bytes, lanes < rows copy a row each
+  auto fill = [&](int s, int tile) {
+    const int rv = min(16, a.N - tile * 16);
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes));
+    __syncwarp();
+    if (lane < rv)
+      bulk_g2s(stages + s * a.stage_bytes + lane * a.stride, a.w + (static_cast<int64_t>(tile) * 16 + lane) * a.row_bytes,
+               static_cast<uint32_t>(a.row_bytes), &full[s]);
+  };
+  if (warp == 0)
+    for (int j = 0; j < a.stages; ++j) {
+      const int tile = blockIdx.x + j * gridDim.x;
+      if (tile < a.tiles) fill(j, tile);
+    }
+  const float post = 65536.0f * __ldg(a.gscale);  // a weight: read before the wait
+  pdl_wait();  // x is produced by the previous kernel
+
+  const int g = lane >> 2, t = lane & 3;
+  // ---- B fragments: activation row g, elements 16t..16t+15 of the slice's four blocks ----
+  uint32_t xb[4][4][2];  // [block][MMA][b0 / b1]
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    uint4 u0 = make_uint4(0u, 0u, 0u, 0u), u1 = u0;
+    if (g < a.R) {
+      const bf16* xp = a.x + static_cast<int64_t>(g) * a.K + warp * 256 + 64 * b + 16 * t;
+      u0 = ldg128(xp);
+      u1 = ldg128(xp + 8);
+    }
+    xb[b][0][0] = pair_lo(u0.x, u0.y);  // (x0, x2)
+    xb[b][0][1] = pair_lo(u1.x, u1.y);  // (x8, x10)
+    xb[b][1][0] = pair_hi(u0.x, u0.y);  // (x1, x3)
+    xb[b][1][1] = pair_hi(u1.x, u1.y);  // (x9, x11)
+    xb[b][2][0] = pair_lo(u0.z, u0.w);  // (x4, x6)
+    xb[b][2][1] = pair_lo(u1.z, u1.w);  // (x12, x14)
+    xb[b][3][0] = pair_hi(u0.z, u0.w);  // (x5, x7)
+    xb[b][3][1] = pair_hi(u1.z, u1.w);  // (x13, x15)
+  }
+  const uint32_t so = static_cast<uint32_t>(warp) * 144u;  // four 36-byte blocks per slice
+  const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
+  int s = 0;
+  uint32_t ph = 0;
+  for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
+    mbar_wait(&full[s], ph, kSiteFullWait);
+    const uint8_t* st = stages + s * a.stage_bytes;
+    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t bo0 = r0 + so + 36u * b, bo1 = r1 + so + 36u * b;  // block: 4 scale bytes, 32 nibble bytes
+      const uint32_t* w0 = reinterpret_cast<const uint32_t*>(st + bo0 + 4u + 8u * t);
+      const uint32_t* w1 = reinterpret_cast<const uint32_t*>(st + bo1 + 4u + 8u * t);
+      const uint32_t v0[2] = {w0[0], w0[1]}, v1[2] = {w1[0], w1[1]};
+      const uint32_t s0 = fp4lut[st[bo0 + t]], s1 = fp4lut[st[bo1 + t]];
+      const uint32_t S0 = s0 | (s0 << 16), S1 = s1 | (s1 << 16);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t u0 = (q & 1) ? (v0[q >> 1] >> 8) : v0[q >> 1];
+        const uint32_t u1 = (q & 1) ? (v1[q >> 1] >> 8) : v1[q >> 1];
+        // low nibbles of bytes 0, 2 of the (shifted) word and their high nibbles -> exact bf16 pairs
+        const uint32_t a0 = hmul2_bits(((u0 & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S0);
+        const uint32_t a2 = hmul2_bits(((u0 & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S0);
+        const uint32_t a1 = hmul2_bits(((u1 & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S1);
+        const uint32_t a3 = hmul2_bits(((u1 & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S1);
+        mma_bf16_16816(c[q & 1], a0, a1, a2, a3, xb[b][q][0], xb[b][q][1], c[q & 1]);
+      }
+    }
+    // lane's C: rows g / g+8 x activation rows 2t, 2t+1
+    float* rb = red + (s * kW + warp) * 8 * 16;
+    rb[(2 * t) * 16 + g] = (c[0][0] + c[1][0]) * post;
+    rb[(2 * t + 1) * 16 + g] = (c[0][1] + c[1][1]) * post;
+    rb[(2 * t) * 16 + g + 8] = (c[0][2] + c[1][2]) * post;
+    rb[(2 * t + 1) * 16 + g + 8] = (c[0][3] + c[1][3]) * post;
+    __syncwarp();  // orders the lanes' slot writes before lane 0's release below
+    int last = 0;
+    if (lane == 0) last = atom_add_acq_rel_cta(&cnt[s], 1) == kW - 1;
+    if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this tile are in the slot
+      const float* rs = red + s * kW * 8 * 16;
+#pragma unroll
+      for (int o = lane; o < 8 * 16; o += 32) {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};  // fixed summation order: 4 strided partial sums, then a tree
+#pragma unroll
+        for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rs[w2 * 8 * 16 + o];
+        const int xr = o >> 4, row = tile * 16 + (o & 15);
+        if (xr < a.R && row < a.N) a.y[static_cast<int64_t>(xr) * a.N + row] = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+      }
+      __syncwarp();
+      if (lane == 0) cnt[s] = 0;
+      const int next = tile + a.stages * static_cast<int>(gridDim.x);
+      if (next < a.tiles) {
+        fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
+        fill(s, next);
+      }
+    }
+    if (++s == a.stages) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+}
+
+}  // namespace gguf_b200

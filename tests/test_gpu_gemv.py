@@ -249,6 +249,28 @@ def test_q8_few_row_integer_kernel(cuda, R, N, K, xscale):
     assert_device_ok()
 
 
+@pytest.mark.parametrize("R", [2, 3, 5, 8, 9, 12, 16])
+@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (333, 5120)])
+def test_nvfp4_few_row_kernel(cuda, R, N, K):
+    """The few-row NVFP4 kernel (2 <= R <= 8: activation rows as the MMA columns, scales inside the
+    exact bf16 weights; R > 8 as two launches, R = 9 with the single-row kernel for the last row)
+    against the oracle and the generic engine, every scale byte present."""
+    g = I.rng(K + 11 * R + N)
+    w = I.nvfp4_weights(g, N, K, 0, 255)
+    x = I.bf16_normal(g, (R, K), 2.0)
+    extra = {"gscale": np.array([0.37], np.float32)}
+    y = run_gemv("nvfp4", x, w, extra, cuda)
+    assert np.isfinite(y).all()
+    assert rel(y, oracle_y("nvfp4", x, w, extra, np.arange(N))) < TOL
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_gemv("nvfp4", x, w, extra, cuda)
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+    assert_device_ok()
+
+
 @pytest.mark.parametrize("K", [2048, 4096, 5120, 6144, 8192])
 def test_nvfp4_single_row_integer_kernel(cuda, K):
     """The single-row NVFP4 kernels (bf16 slice, the default, and the integer-decode variant, mode 4)
