@@ -2,7 +2,8 @@
 
 Every rank builds the same seeded weights, keeps its row shard, and checks the row-split GEMV with
 the fused peer-store all-gather against the single-GPU op on the full matrix, over several calls
-(both output buffers)."""
+(both output buffers): bit-identical where both run the same kernel (Q8_0), within 2e-3 rel-L2
+where the single-GPU op has a specialised kernel the shard does not use."""
 
 import os
 import sys
@@ -49,11 +50,12 @@ def main():
                 y = sharded(x)
                 ref = single(op, x, wt, gs)
                 torch.cuda.synchronize()
-                if op == "iq2_xxs" and R == 1:  # single GPU runs the integer kernel, the shard the bf16 one
+                if op == "q8_0":  # the shard runs the single-GPU op's kernel on its rows: bit-identical
+                    ok = torch.equal(y, ref)
+                else:  # IQ2_XXS / NVFP4: the single-GPU op takes the integer or few-row kernels, the shard
+                    # the bf16 slice kernel or the engine (same exact weights, another summation order)
                     err = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
                     ok = err < 2e-3
-                else:
-                    ok = torch.equal(y, ref)
                 if not ok:
                     failures.append((op, N, K, R, it))
         sharded.close()
