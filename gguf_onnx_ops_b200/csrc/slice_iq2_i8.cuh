@@ -12,10 +12,10 @@
 //
 // Activations.  Each 32-element group of x (the sub-block the weight scale belongs to) is converted
 // once per launch to integers x_int = x * 2^(14 - E), E = the exponent of the group's largest
-// |x|, |x_int| <= 32640, split as x_int = 256 * hi + lo (hi s8, lo u8).  The conversion is integer
-// only and exact for every element within a factor 2^7 of the group maximum (the bf16 significand
-// then fits); smaller elements are rounded to a step of 2^(E - 14), i.e. 2^-14 of the group
-// maximum.  Products and sums are exact in s32; the epilogue applies 2^(E - 14) and the weight scale
+// |x|, |x_int| <= 32640, split as x_int = 256 * hi + lo (hi s8, lo u8).  The conversion (exact
+// power-of-two products, then a round-to-integer by adding 1.5 * 2^23) is exact for every element
+// within a factor 2^7 of the group maximum (the bf16 significand then fits); smaller elements are
+// rounded (nearest, ties to even) to a step of 2^(E - 14), i.e. 2^-14 of the group maximum.  Products and sums are exact in s32; the epilogue applies 2^(E - 14) and the weight scale
 // in fp32.
 //
 // MMA layout (block-diagonal B, as in the bf16 slice kernel): k-slots 4t..4t+3 belong to group t
@@ -113,17 +113,26 @@ __device__ __forceinline__ void i8_x_frag(const uint4 xv, I8XFrag& f) {
   mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
   mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
   const int emax = max(1, static_cast<int>(mb >> 7));  // effective biased exponent of the maximum
-  uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-  int xsum = 0;
+  // x_int = x * 2^(14 - E) without branches: two exact power-of-two products (the first 2^64 for
+  // groups below 2^-63), then adding 1.5 * 2^23 rounds to an integer (nearest, ties to even) whose
+  // low 16 bits are x_int: byte 1 = the high limb x_int >> 8 (s8), byte 0 = the low limb (u8).
+  const bool tiny = emax < 64;
+  const float s1 = tiny ? 18446744073709551616.0f : 1.0f;  // 2^64
+  const float s2 = __uint_as_float(static_cast<uint32_t>(268 - emax - (tiny ? 64 : 0)) << 23);  // 2^(141 - emax) / s1
+  uint32_t r[8], rsum = 0u;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    int neg, sig, ex;
-    bf16_parts(i & 1 ? (wv[i >> 1] >> 16) : (wv[i >> 1] & 0xFFFFu), neg, sig, ex);
-    const int xi = bf16_to_fixed(neg, sig, ex, emax);
-    xsum += xi;
-    hw[i >> 2] |= (static_cast<uint32_t>(xi >> 8) & 0xFFu) << (8 * (i & 3));
-    lw[i >> 2] |= (static_cast<uint32_t>(xi) & 0xFFu) << (8 * (i & 3));
+    const float v = __uint_as_float(i & 1 ? (wv[i >> 1] & 0xFFFF0000u) : (wv[i >> 1] << 16));
+    r[i] = __float_as_uint((v * s1) * s2 + 12582912.0f);
+    rsum += r[i];
   }
+  uint32_t hw[2], lw[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    hw[k] = __byte_perm(__byte_perm(r[4 * k], r[4 * k + 1], 0x0051u), __byte_perm(r[4 * k + 2], r[4 * k + 3], 0x0051u), 0x5410u);
+    lw[k] = __byte_perm(__byte_perm(r[4 * k], r[4 * k + 1], 0x0040u), __byte_perm(r[4 * k + 2], r[4 * k + 3], 0x0040u), 0x5410u);
+  }
+  int xsum = static_cast<int>(rsum - 8u * 0x4B400000u);  // sum of x_int (mod 2^32, exact)
   xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
   xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
   // owner of group c: lane (g = c, t = c) for c < 4, lane (g = c, t = c - 4) for c >= 4.  Step j of
