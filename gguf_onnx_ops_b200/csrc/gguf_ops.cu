@@ -451,7 +451,7 @@ int try_iq2_rows(const void* x, const void* w, void* y, int R, int N, int K, cud
 
 // Q8_0 2 <= R <= 4 * kNR on the integer tensor cores (slice_q8_i8_rows.cuh): 16 whole rows per
 // stage at pitch row bytes + 16, two or more stages.
-template <int kW, int kNR>
+template <int kW, int kNR, int kSPW = 1>
 int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s,
                          const PeerOut* po) {
   SliceArgs a = {};
@@ -476,7 +476,7 @@ int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, in
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   static std::atomic<uint64_t> done{0};
-  auto kern = slice_q8_i8_rows_kernel<kW, kNR>;
+  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
   cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row Q8_0 GEMV launch", e);
@@ -494,7 +494,7 @@ int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cuda
   const bool two = R > 4;
   switch (K) {
     case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s, po);
-    case 4096: return two ? run_slice_q8_i8_rows<16, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s, po);
+    case 4096: return two ? run_slice_q8_i8_rows<8, 2, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s, po);
     case 5120: return two ? run_slice_q8_i8_rows<20, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<20, 1>(x, w, y, R, N, K, s, po);
     default: return -1;
   }

@@ -53,10 +53,11 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
   }
 }
 
-// Warp w owns slice w of K for the whole launch; the last warp to finish a tile sums the stage's
-// reduction slot in warp order (deterministic), stores y [R, N] and refills the stage (the
-// last-arriver scheme of slice_iq2_i8_kernel).
-template <int kW, int kNR>
+// Warp w owns slices w * kSPW .. w * kSPW + kSPW - 1 of K for the whole launch; the last warp to
+// finish a tile sums the stage's reduction slot in warp order (deterministic), stores y [R, N] and
+// refills the stage (the last-arriver scheme of slice_iq2_i8_kernel).  kSPW = 2 halves the warps
+// and with them the reduction slots, which leaves room for a third stage at eight activation rows.
+template <int kW, int kNR, int kSPW = 1>
 __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
   constexpr int kRX = 4 * kNR;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -92,10 +93,11 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
     }
   pdl_wait();  // x is produced by the previous kernel
 
-  I8RowsX<kNR, false> xf;  // signed quants: no offset sums
-  i8_rows_x<kNR, false>(a.x, a.R, a.K, warp, xf);
+  I8RowsX<kNR, false> xf[kSPW];  // signed quants: no offset sums
+#pragma unroll
+  for (int j = 0; j < kSPW; ++j) i8_rows_x<kNR, false>(a.x, a.R, a.K, warp * kSPW + j, xf[j]);
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t so = static_cast<uint32_t>(warp) * 272u;
+  const uint32_t so = static_cast<uint32_t>(warp * kSPW) * 272u;
   const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
   int s = 0;
   uint32_t ph = 0;
@@ -104,7 +106,8 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
     float acc[kNR][2];
 #pragma unroll
     for (int m = 0; m < kNR; ++m) acc[m][0] = acc[m][1] = 0.f;
-    q8_rows_slice<kNR>(stages + s * a.stage_bytes, r0, r1, so, xf, acc);
+#pragma unroll
+    for (int j = 0; j < kSPW; ++j) q8_rows_slice<kNR>(stages + s * a.stage_bytes, r0, r1, so + 272u * j, xf[j], acc);
 
     float* rb = red + (s * kW + warp) * kRX * 16;
 #pragma unroll
