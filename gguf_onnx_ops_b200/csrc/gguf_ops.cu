@@ -500,6 +500,54 @@ int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cuda
   }
 }
 
+// Q8Gemv gguf=0 (split layout: u8 q + 128 [N, K], bf16 scales [N, K/32]) through the few-row Q8
+// kernel: 16 weight rows per stage at pitch K + 32 (conflict-free 8-byte quant loads), the tile's 16
+// scale rows (contiguous in the scale tensor) after them, one bulk copy each.
+template <int kW, int kNR, int kSPW = 1>
+int run_slice_q8s_rows(const void* x, const void* w, const void* scales, void* y, int R, int N, int K, cudaStream_t s) {
+  SliceArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.sc = static_cast<const uint8_t*>(scales);
+  a.x = static_cast<const bf16*>(x);
+  a.y = static_cast<bf16*>(y);
+  a.R = R;
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K;
+  a.sc_row_bytes = K / 16;  // K % 256 == 0: a multiple of 16
+  a.tiles = (N + 15) / 16;
+  a.stride = K + 32;
+  a.sc_off = 16 * a.stride;
+  a.stage_bytes = (a.sc_off + 16 * a.sc_row_bytes + 127) & ~127;
+  const int red_per_stage = kW * 4 * kNR * 16 * 4 + 4;  // reduction slot + counter
+  a.stages = std::min(4, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return -1;
+  a.off_stage = 0;
+  a.off_red = a.stages * a.stage_bytes;
+  a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW, true>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("few-row Q8Gemv gguf=0 launch", e);
+  return GGUF_OK;
+}
+
+int try_q8s_rows(const void* x, const void* w, const void* scales, void* y, int R, int N, int K, cudaStream_t s) {
+  if (g_fast.load() != 1 || R < 1 || R > 16) return -1;
+  if (R > 8) return K == 4096 ? run_slice_q8s_rows<16, 4>(x, w, scales, y, R, N, K, s) : -1;
+  const bool two = R > 4;
+  switch (K) {
+    case 2048: return two ? run_slice_q8s_rows<8, 2>(x, w, scales, y, R, N, K, s) : run_slice_q8s_rows<8, 1>(x, w, scales, y, R, N, K, s);
+    case 4096: return two ? run_slice_q8s_rows<8, 2, 2>(x, w, scales, y, R, N, K, s) : run_slice_q8s_rows<16, 1>(x, w, scales, y, R, N, K, s);
+    case 5120: return two ? run_slice_q8s_rows<20, 2>(x, w, scales, y, R, N, K, s) : run_slice_q8s_rows<20, 1>(x, w, scales, y, R, N, K, s);
+    default: return -1;
+  }
+}
+
 // NVFP4 2 <= R <= 8 on the bf16 tensor cores with the activation rows as MMA columns
 // (slice_fp4_rows.cuh): 16 whole rows per stage at pitch row bytes + 32.
 template <int kW>
@@ -1277,7 +1325,10 @@ int gguf_gemv_legacy(int layout, const void* x, const void* w, const void* scale
   auto* s = static_cast<cudaStream_t>(stream);
   const int r = static_cast<int>(R), n = static_cast<int>(N), k = static_cast<int>(K);
   switch (layout) {
-    case GGUF_LAYOUT_Q8_SPLIT:
+    case GGUF_LAYOUT_Q8_SPLIT: {
+      const int rc = try_q8s_rows(x, w, scales, y, r, n, k, s);
+      if (rc >= 0) return rc;
+    }
       return R <= 8 ? run_dense_split<kFmtQ8S, 1>(x, w, scales, gscale, y, r, n, k, s)
                     : run_dense_split<kFmtQ8S, 2>(x, w, scales, gscale, y, r, n, k, s);
     case GGUF_LAYOUT_Q4_SPLIT:

@@ -1,4 +1,5 @@
-// Few-row Q8_0 GEMV (1 <= R <= 4 * kNR) on the integer tensor cores.  A Q8_0 block is an fp16 scale
+// Few-row Q8_0 GEMV (1 <= R <= 4 * kNR) on the integer tensor cores (kSplit: the legacy split layout
+// of Q8Gemv gguf=0, u8 q + 128 with bf16 scales per 32 in a second tensor).  A Q8_0 block is an fp16 scale
 // d and 32 int8 quants, so the quants are the MMA's A operand as they are (s8, no decode step):
 // the launch is bound by HBM and by the per-block epilogue, not by a codebook.
 //
@@ -30,18 +31,42 @@ __device__ __forceinline__ void imma_s8s8_c(int (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
 
-// One 16-row x 256-column slice (8 Q8_0 blocks per row) against the kNR MMA sets; st = the stage,
-// r0 / r1 = byte offsets of rows g / g+8, so = the slice's byte offset in a row (272 * slice).
-template <int kNR>
-__device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t so,
-                                              const I8RowsX<kNR, false>& f, float (&acc)[kNR][2]) {
+// One 16-row x 256-column slice (8 blocks of 32 per row) against the kNR MMA sets; st = the stage,
+// r0 / r1 = byte offsets of rows g / g+8, sl = the slice index.  Q8_0 (kSplit false): block j at
+// 272 * sl + 34 j, fp16 d then the quants.  Split layout (Q8Gemv gguf=0, kSplit true): the quants as
+// u8 q + 128 at 256 * sl + 32 j (8-byte aligned; q = u ^ 0x80 per byte), the bf16 scales of rows g /
+// g+8 at sc0 / sc1 (stage offsets of their scale rows) + 2 (8 sl + j), read as one 16-byte load per
+// row and slice (the scale rows are 256 bytes apart, so the eight quads' reads share banks).
+template <int kNR, bool kSplit = false>
+__device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t sl, uint32_t sc0,
+                                              uint32_t sc1, const I8RowsX<kNR, false>& f, float (&acc)[kNR][2]) {
   const uint32_t t = threadIdx.x & 3;
+  uint32_t sv0[4] = {0u, 0u, 0u, 0u}, sv1[4] = {0u, 0u, 0u, 0u};
+  if constexpr (kSplit) {  // the slice's 8 bf16 scales of rows g / g+8: one 16-byte load each
+    const uint4 u0 = *reinterpret_cast<const uint4*>(st + sc0 + 16u * sl);
+    const uint4 u1 = *reinterpret_cast<const uint4*>(st + sc1 + 16u * sl);
+    sv0[0] = u0.x; sv0[1] = u0.y; sv0[2] = u0.z; sv0[3] = u0.w;
+    sv1[0] = u1.x; sv1[1] = u1.y; sv1[2] = u1.z; sv1[3] = u1.w;
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint32_t ob = so + 34u * j;  // block j: d at ob, quants at ob + 2 (4-byte aligned iff j is odd)
-    const uint2 q0 = lds8(st, r0 + ob + 2u + 8u * t, (j & 1) != 0);
-    const uint2 q1 = lds8(st, r1 + ob + 2u + 8u * t, (j & 1) != 0);
-    const float d0 = fp16_bits_to_f32(ld_u16(st, r0 + ob)), d1 = fp16_bits_to_f32(ld_u16(st, r1 + ob));
+    uint2 q0, q1;
+    float d0, d1;
+    if constexpr (kSplit) {
+      const uint32_t ob = 256u * sl + 32u * j + 8u * t;
+      q0 = *reinterpret_cast<const uint2*>(st + r0 + ob);
+      q1 = *reinterpret_cast<const uint2*>(st + r1 + ob);
+      q0 = make_uint2(q0.x ^ 0x80808080u, q0.y ^ 0x80808080u);
+      q1 = make_uint2(q1.x ^ 0x80808080u, q1.y ^ 0x80808080u);
+      d0 = __uint_as_float(j & 1 ? (sv0[j >> 1] & 0xFFFF0000u) : (sv0[j >> 1] << 16));
+      d1 = __uint_as_float(j & 1 ? (sv1[j >> 1] & 0xFFFF0000u) : (sv1[j >> 1] << 16));
+    } else {
+      const uint32_t ob = 272u * sl + 34u * j;  // block j: d at ob, quants at ob + 2 (4-byte aligned iff j is odd)
+      q0 = lds8(st, r0 + ob + 2u + 8u * t, (j & 1) != 0);
+      q1 = lds8(st, r1 + ob + 2u + 8u * t, (j & 1) != 0);
+      d0 = fp16_bits_to_f32(ld_u16(st, r0 + ob));
+      d1 = fp16_bits_to_f32(ld_u16(st, r1 + ob));
+    }
 #pragma unroll
     for (int m = 0; m < kNR; ++m) {
       int cc[4];
@@ -57,7 +82,7 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
 // finish a tile sums the stage's reduction slot in warp order (deterministic), stores y [R, N] and
 // refills the stage (the last-arriver scheme of slice_iq2_i8_kernel).  kSPW = 2 halves the warps
 // and with them the reduction slots, which leaves room for a third stage at eight activation rows.
-template <int kW, int kNR, int kSPW = 1>
+template <int kW, int kNR, int kSPW = 1, bool kSplit = false>
 __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
   constexpr int kRX = 4 * kNR;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -80,11 +105,14 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
   // stage s <- tile `tile` (the calling warp): lane 0 announces the bytes, lanes < rows copy a row each
   auto fill = [&](int s, int tile) {
     const int rv = min(16, a.N - tile * 16);
-    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes));
+    const uint32_t scb = kSplit ? static_cast<uint32_t>(rv * a.sc_row_bytes) : 0u;  // the tile's scale rows
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes) + scb);
     __syncwarp();
     if (lane < rv)
       bulk_g2s(stages + s * a.stage_bytes + lane * a.stride, a.w + (static_cast<int64_t>(tile) * 16 + lane) * a.row_bytes,
                static_cast<uint32_t>(a.row_bytes), &full[s]);
+    if (kSplit && lane == 16)
+      bulk_g2s(stages + s * a.stage_bytes + a.sc_off, a.sc + static_cast<int64_t>(tile) * 16 * a.sc_row_bytes, scb, &full[s]);
   };
   if (warp == 0)
     for (int j = 0; j < a.stages; ++j) {
@@ -97,8 +125,9 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
 #pragma unroll
   for (int j = 0; j < kSPW; ++j) i8_rows_x<kNR, false>(a.x, a.R, a.K, warp * kSPW + j, xf[j]);
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t so = static_cast<uint32_t>(warp * kSPW) * 272u;
+  const uint32_t sl0 = static_cast<uint32_t>(warp * kSPW);
   const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
+  const uint32_t sc0 = static_cast<uint32_t>(a.sc_off + g * a.sc_row_bytes), sc1 = static_cast<uint32_t>(a.sc_off + (g + 8) * a.sc_row_bytes);
   int s = 0;
   uint32_t ph = 0;
   for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
@@ -107,7 +136,8 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
 #pragma unroll
     for (int m = 0; m < kNR; ++m) acc[m][0] = acc[m][1] = 0.f;
 #pragma unroll
-    for (int j = 0; j < kSPW; ++j) q8_rows_slice<kNR>(stages + s * a.stage_bytes, r0, r1, so + 272u * j, xf[j], acc);
+    for (int j = 0; j < kSPW; ++j)
+      q8_rows_slice<kNR, kSplit>(stages + s * a.stage_bytes, r0, r1, sl0 + j, sc0, sc1, xf[j], acc);
 
     float* rb = red + (s * kW + warp) * kRX * 16;
 #pragma unroll

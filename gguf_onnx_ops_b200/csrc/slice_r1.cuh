@@ -56,6 +56,10 @@ struct SliceArgs {
   // (the row bytes plus a 16-byte pad, zero-filled past the row end) instead of one bulk copy
   CUtensorMap tmap;
   int use_tmap;
+  // slice_q8_i8_rows_kernel, split layout (Q8Gemv gguf=0): bf16 scales [N, K/32], sc_row_bytes = K/16,
+  // staged after the 16 weight rows at stage offset sc_off
+  const uint8_t* sc;
+  int sc_row_bytes, sc_off;
 };
 
 template <int F>
