@@ -503,7 +503,7 @@ int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cuda
 // Q8Gemv gguf=0 (split layout: u8 q + 128 [N, K], bf16 scales [N, K/32]) through the few-row Q8
 // kernel: 16 weight rows per stage at pitch K + 32 (conflict-free 8-byte quant loads), the tile's 16
 // scale rows (contiguous in the scale tensor) after them, one bulk copy each.
-template <int kW, int kNR, int kSPW = 1>
+template <int kW, int kNR, int kSPW = 1, int kLay = kLayQ8S>
 int run_slice_q8s_rows(const void* x, const void* w, const void* scales, void* y, int R, int N, int K, cudaStream_t s) {
   SliceArgs a = {};
   a.w = static_cast<const uint8_t*>(w);
@@ -513,10 +513,10 @@ int run_slice_q8s_rows(const void* x, const void* w, const void* scales, void* y
   a.R = R;
   a.N = N;
   a.K = K;
-  a.row_bytes = K;
+  a.row_bytes = kLay == kLayQ4S ? K / 2 : K;
   a.sc_row_bytes = K / 16;  // K % 256 == 0: a multiple of 16
   a.tiles = (N + 15) / 16;
-  a.stride = K + 32;
+  a.stride = a.row_bytes + (kLay == kLayQ4S ? 16 : 32);  // row words = 4 (Q4: 32-bit loads) / 8 (8-byte loads) mod 32
   a.sc_off = 16 * a.stride;
   a.stage_bytes = (a.sc_off + 16 * a.sc_row_bytes + 127) & ~127;
   const int red_per_stage = kW * 4 * kNR * 16 * 4 + 4;  // reduction slot + counter
@@ -529,11 +529,23 @@ int run_slice_q8s_rows(const void* x, const void* w, const void* scales, void* y
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   static std::atomic<uint64_t> done{0};
-  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW, true>;
+  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW, kLay>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
   cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row Q8Gemv gguf=0 launch", e);
   return GGUF_OK;
+}
+
+// Q4Gemv iq2=0 (split nibbles n - 8, bf16 scales per 32) on the same kernel, R <= 4 (a second MMA
+// set with the offset sums spills registers: R > 4 stays on the engine).
+int try_q4s_rows(const void* x, const void* w, const void* scales, void* y, int R, int N, int K, cudaStream_t s) {
+  if (g_fast.load() != 1 || R < 1 || R > 4) return -1;
+  switch (K) {
+    case 2048: return run_slice_q8s_rows<8, 1, 1, kLayQ4S>(x, w, scales, y, R, N, K, s);
+    case 4096: return run_slice_q8s_rows<16, 1, 1, kLayQ4S>(x, w, scales, y, R, N, K, s);
+    case 5120: return run_slice_q8s_rows<20, 1, 1, kLayQ4S>(x, w, scales, y, R, N, K, s);
+    default: return -1;
+  }
 }
 
 int try_q8s_rows(const void* x, const void* w, const void* scales, void* y, int R, int N, int K, cudaStream_t s) {
@@ -1331,7 +1343,10 @@ int gguf_gemv_legacy(int layout, const void* x, const void* w, const void* scale
     }
       return R <= 8 ? run_dense_split<kFmtQ8S, 1>(x, w, scales, gscale, y, r, n, k, s)
                     : run_dense_split<kFmtQ8S, 2>(x, w, scales, gscale, y, r, n, k, s);
-    case GGUF_LAYOUT_Q4_SPLIT:
+    case GGUF_LAYOUT_Q4_SPLIT: {
+      const int rc = try_q4s_rows(x, w, scales, y, r, n, k, s);
+      if (rc >= 0) return rc;
+    }
       return R <= 8 ? run_dense_split<kFmtQ4S, 1>(x, w, scales, gscale, y, r, n, k, s)
                     : run_dense_split<kFmtQ4S, 2>(x, w, scales, gscale, y, r, n, k, s);
     case GGUF_LAYOUT_IQ2_CODES:

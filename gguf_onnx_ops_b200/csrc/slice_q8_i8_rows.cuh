@@ -37,9 +37,18 @@ __device__ __forceinline__ void imma_s8s8_c(int (&d)[4], uint32_t a0, uint32_t a
 // u8 q + 128 at 256 * sl + 32 j (8-byte aligned; q = u ^ 0x80 per byte), the bf16 scales of rows g /
 // g+8 at sc0 / sc1 (stage offsets of their scale rows) + 2 (8 sl + j), read as one 16-byte load per
 // row and slice (the scale rows are 256 bytes apart, so the eight quads' reads share banks).
-template <int kNR, bool kSplit = false>
+//
+// kLay: 0 = Q8_0, 1 = Q8Gemv gguf=0 (split), 2 = Q4Gemv iq2=0 (split: u8 [N, K/2] nibbles n, element
+// 2i the low nibble of byte i, value n - 8, bf16 scales per 32).  Q4: lane t's 8 elements of block j
+// are bytes 4t..4t+3 at 128 sl + 16 j; the nibbles become the u8 A operand n as they are (two LOP3,
+// two byte-permutes per 8 elements) and the offset 8 sum(x_int) enters as the low-limb column's C.
+constexpr int kLayQ8 = 0, kLayQ8S = 1, kLayQ4S = 2;
+
+template <int kNR, int kLay = kLayQ8>
 __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, uint32_t r1, uint32_t sl, uint32_t sc0,
-                                              uint32_t sc1, const I8RowsX<kNR, false>& f, float (&acc)[kNR][2]) {
+                                              uint32_t sc1, const I8RowsX<kNR, kLay == kLayQ4S>& f,
+                                              float (&acc)[kNR][2]) {
+  constexpr bool kSplit = kLay != kLayQ8;
   const uint32_t t = threadIdx.x & 3;
   uint32_t sv0[4] = {0u, 0u, 0u, 0u}, sv1[4] = {0u, 0u, 0u, 0u};
   if constexpr (kSplit) {  // the slice's 8 bf16 scales of rows g / g+8: one 16-byte load each
@@ -52,7 +61,15 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
   for (int j = 0; j < 8; ++j) {
     uint2 q0, q1;
     float d0, d1;
-    if constexpr (kSplit) {
+    if constexpr (kLay == kLayQ4S) {
+      const uint32_t ob = 128u * sl + 16u * j + 4u * t;
+      const uint32_t v0 = *reinterpret_cast<const uint32_t*>(st + r0 + ob), v1 = *reinterpret_cast<const uint32_t*>(st + r1 + ob);
+      const uint32_t l0 = v0 & 0x0F0F0F0Fu, h0 = (v0 >> 4) & 0x0F0F0F0Fu, l1 = v1 & 0x0F0F0F0Fu, h1 = (v1 >> 4) & 0x0F0F0F0Fu;
+      q0 = make_uint2(__byte_perm(l0, h0, 0x5140u), __byte_perm(l0, h0, 0x7362u));  // elements 8t..8t+3, 8t+4..8t+7
+      q1 = make_uint2(__byte_perm(l1, h1, 0x5140u), __byte_perm(l1, h1, 0x7362u));
+      d0 = __uint_as_float(j & 1 ? (sv0[j >> 1] & 0xFFFF0000u) : (sv0[j >> 1] << 16));
+      d1 = __uint_as_float(j & 1 ? (sv1[j >> 1] & 0xFFFF0000u) : (sv1[j >> 1] << 16));
+    } else if constexpr (kSplit) {
       const uint32_t ob = 256u * sl + 32u * j + 8u * t;
       q0 = *reinterpret_cast<const uint2*>(st + r0 + ob);
       q1 = *reinterpret_cast<const uint2*>(st + r1 + ob);
@@ -70,7 +87,10 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
 #pragma unroll
     for (int m = 0; m < kNR; ++m) {
       int cc[4];
-      imma_s8s8_c(cc, q0.x, q1.x, q0.y, q1.y, f.b[m][j][0], f.b[m][j][1]);
+      if constexpr (kLay == kLayQ4S)
+        imma_u8s8_c(cc, q0.x, q1.x, q0.y, q1.y, f.b[m][j][0], f.b[m][j][1], 0, f.nxoff[m][j] >> 3);  // -8 sum(x_int)
+      else
+        imma_s8s8_c(cc, q0.x, q1.x, q0.y, q1.y, f.b[m][j][0], f.b[m][j][1]);
       const float p = f.xs[m][j];
       acc[m][0] = fmaf(static_cast<float>(cc[0] * 256 + cc[1]), p * d0, acc[m][0]);
       acc[m][1] = fmaf(static_cast<float>(cc[2] * 256 + cc[3]), p * d1, acc[m][1]);
@@ -82,8 +102,9 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
 // finish a tile sums the stage's reduction slot in warp order (deterministic), stores y [R, N] and
 // refills the stage (the last-arriver scheme of slice_iq2_i8_kernel).  kSPW = 2 halves the warps
 // and with them the reduction slots, which leaves room for a third stage at eight activation rows.
-template <int kW, int kNR, int kSPW = 1, bool kSplit = false>
+template <int kW, int kNR, int kSPW = 1, int kLay = kLayQ8>
 __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
+  constexpr bool kSplit = kLay != kLayQ8;
   constexpr int kRX = 4 * kNR;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
@@ -121,9 +142,9 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
     }
   pdl_wait();  // x is produced by the previous kernel
 
-  I8RowsX<kNR, false> xf[kSPW];  // signed quants: no offset sums
+  I8RowsX<kNR, kLay == kLayQ4S> xf[kSPW];  // signed quants need no offset sums, Q4 nibbles (u8) do
 #pragma unroll
-  for (int j = 0; j < kSPW; ++j) i8_rows_x<kNR, false>(a.x, a.R, a.K, warp * kSPW + j, xf[j]);
+  for (int j = 0; j < kSPW; ++j) i8_rows_x<kNR, kLay == kLayQ4S>(a.x, a.R, a.K, warp * kSPW + j, xf[j]);
   const int g = lane >> 2, t = lane & 3;
   const uint32_t sl0 = static_cast<uint32_t>(warp * kSPW);
   const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
@@ -137,7 +158,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
     for (int m = 0; m < kNR; ++m) acc[m][0] = acc[m][1] = 0.f;
 #pragma unroll
     for (int j = 0; j < kSPW; ++j)
-      q8_rows_slice<kNR, kSplit>(stages + s * a.stage_bytes, r0, r1, sl0 + j, sc0, sc1, xf[j], acc);
+      q8_rows_slice<kNR, kLay>(stages + s * a.stage_bytes, r0, r1, sl0 + j, sc0, sc1, xf[j], acc);
 
     float* rb = red + (s * kW + warp) * kRX * 16;
 #pragma unroll

@@ -90,6 +90,25 @@ def test_q8_split_few_row_kernel(cuda, R, N, K):
     assert rel(y, y_gen) < 2e-3
 
 
+@pytest.mark.parametrize("R", [1, 3, 4, 5])
+@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (61, 5120)])
+def test_q4_split_few_row_kernel(cuda, R, N, K):
+    """Q4Gemv iq2=0 through the few-row integer kernel (R <= 4; nibbles n as u8 weights, the -8 offset
+    as the MMA's C input; K = 2048 / 4096 / 5120) against the oracle and the generic engine (R = 5
+    takes the engine itself), ragged N."""
+    g = I.rng(3 * N + K + R)
+    w, sc = I.legacy_case("q4", g, N, K)
+    x = I.bf16_normal(g, (R, K), 2.0)
+    y = run_layout("q4", x, w, sc, cuda).float().cpu().numpy()
+    assert rel(y, O.gemv_ref(x, deq("q4", w, sc))) < TOL
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_layout("q4", x, w, sc, cuda).float().cpu().numpy()
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+
+
 def test_legacy_reference_shapes(cuda):
     """The harness's shapes: Nvfp4 4096x4096 R=1..8, Q8 / Q4 [N, K/32, 32|16] (tests/test_bolt_ops.py:452-470)."""
     for layout, R, N, K in (("fp4", 1, 4096, 4096), ("fp4", 8, 1024, 8192), ("q8", 2, 4096, 4096),
