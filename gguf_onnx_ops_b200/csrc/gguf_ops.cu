@@ -596,6 +596,55 @@ int run_slice_fp4_rows(const void* x, const void* w, const float* gscale, void* 
 template <int F>
 int try_slice_r1(const void* x, const void* w, const float* gscale, void* y, int N, int K, cudaStream_t s);
 
+// Nvfp4Gemv gguf=0 (split: nibbles [N, K/2], e4m3fn scales [N, K/16]) on the few-row NVFP4 kernel,
+// 2 <= R <= 8: 16 weight rows at pitch K/2 + 32 (conflict-free 8-byte nibble loads), the tile's 16
+// scale rows after them.
+template <int kW>
+int run_slice_fp4s_rows(const void* x, const void* w, const void* scales, const float* gscale, void* y, int R, int N,
+                        int K, cudaStream_t s) {
+  SliceArgs a = {};
+  a.w = static_cast<const uint8_t*>(w);
+  a.sc = static_cast<const uint8_t*>(scales);
+  a.x = static_cast<const bf16*>(x);
+  a.gscale = gscale;
+  a.y = static_cast<bf16*>(y);
+  a.R = R;
+  a.N = N;
+  a.K = K;
+  a.row_bytes = K / 2;
+  a.sc_row_bytes = K / 16;  // K % 256 == 0: a multiple of 16
+  a.tiles = (N + 15) / 16;
+  a.stride = a.row_bytes + 32;
+  a.sc_off = 16 * a.stride;
+  a.stage_bytes = (a.sc_off + 16 * a.sc_row_bytes + 127) & ~127;
+  const int lut = 512, red_per_stage = kW * 8 * 16 * 4 + 4;
+  a.stages = std::min(4, (kSmemBudgetMax - lut - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return -1;
+  a.off_stage = lut;
+  a.off_red = lut + a.stages * a.stage_bytes;
+  a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
+  const size_t smem = a.off_bar + 2 * a.stages * 8;
+  int sms = 0, rc;
+  if ((rc = current_sms(&sms))) return rc;
+  static std::atomic<uint64_t> done{0};
+  auto kern = slice_fp4_rows_kernel<kW, true>;
+  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  if (e != cudaSuccess) return cuda_fail("few-row Nvfp4Gemv gguf=0 launch", e);
+  return GGUF_OK;
+}
+
+int try_fp4s_rows(const void* x, const void* w, const void* scales, const float* gscale, void* y, int R, int N, int K,
+                  cudaStream_t s) {
+  if (g_fast.load() != 1 || R < 2 || R > 8) return -1;
+  switch (K) {
+    case 2048: return run_slice_fp4s_rows<8>(x, w, scales, gscale, y, R, N, K, s);
+    case 4096: return run_slice_fp4s_rows<16>(x, w, scales, gscale, y, R, N, K, s);
+    case 5120: return run_slice_fp4s_rows<20>(x, w, scales, gscale, y, R, N, K, s);
+    default: return -1;
+  }
+}
+
 // Dispatches 2 <= R <= 16 NVFP4 to the few-row kernel when K allows it (R > 8: two launches, rows
 // 0..7 and 8..R-1, each streaming the weights once); -1 otherwise.
 int try_fp4_rows(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
@@ -1355,7 +1404,10 @@ int gguf_gemv_legacy(int layout, const void* x, const void* w, const void* scale
     case GGUF_LAYOUT_IQ2_NATIVE:
       return R <= 8 ? run_dense_split<kFmtIQ2N, 1>(x, w, scales, gscale, y, r, n, k, s)
                     : run_dense_split<kFmtIQ2N, 2>(x, w, scales, gscale, y, r, n, k, s);
-    default:
+    default: {
+      const int rc = try_fp4s_rows(x, w, scales, gscale, y, r, n, k, s);
+      if (rc >= 0) return rc;
+    }
       return R <= 8 ? run_dense_split<kFmtFP4S, 1>(x, w, scales, gscale, y, r, n, k, s)
                     : run_dense_split<kFmtFP4S, 2>(x, w, scales, gscale, y, r, n, k, s);
   }

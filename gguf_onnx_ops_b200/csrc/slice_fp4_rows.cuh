@@ -26,7 +26,11 @@
 
 namespace gguf_b200 {
 
-template <int kW>
+// kSplit: the legacy layout of Nvfp4Gemv gguf=0 (u8 [N, K/2] nibbles with element 2i the low nibble
+// of byte i, e4m3fn scales [N, K/16] in a second tensor).  Its sub-block words pair the elements
+// (0,4) (1,5), (2,6) (3,7), ... instead, the scale table holds e4m3fn * 2^110, and a stage carries
+// the tile's 16 scale rows after its 16 weight rows (lane t's nibbles: bytes 32 b + 8 t of the slice).
+template <int kW, bool kSplit = false>
 __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid_constant__ SliceArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
@@ -44,18 +48,22 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < 256; i += kW * 32)
-    reinterpret_cast<uint16_t*>(smem)[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));
+    reinterpret_cast<uint16_t*>(smem)[i] =
+        static_cast<uint16_t>(kSplit ? e4m3fn_bf16_bits_x2p110(i) : fp4_scale_bf16_bits(i));
   __syncthreads();
   pdl_launch_dependents();
 
   // stage s <- tile `tile` (the calling warp): lane 0 announces the bytes, lanes < rows copy a row each
   auto fill = [&](int s, int tile) {
     const int rv = min(16, a.N - tile * 16);
-    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes));
+    const uint32_t scb = kSplit ? static_cast<uint32_t>(rv * a.sc_row_bytes) : 0u;  // the tile's scale rows
+    if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rv * a.row_bytes) + scb);
     __syncwarp();
     if (lane < rv)
       bulk_g2s(stages + s * a.stage_bytes + lane * a.stride, a.w + (static_cast<int64_t>(tile) * 16 + lane) * a.row_bytes,
                static_cast<uint32_t>(a.row_bytes), &full[s]);
+    if (kSplit && lane == 16)
+      bulk_g2s(stages + s * a.stage_bytes + a.sc_off, a.sc + static_cast<int64_t>(tile) * 16 * a.sc_row_bytes, scb, &full[s]);
   };
   if (warp == 0)
     for (int j = 0; j < a.stages; ++j) {
@@ -76,16 +84,29 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid
       u0 = ldg128(xp);
       u1 = ldg128(xp + 8);
     }
-    xb[b][0][0] = pair_lo(u0.x, u0.y);  // (x0, x2)
-    xb[b][0][1] = pair_lo(u1.x, u1.y);  // (x8, x10)
-    xb[b][1][0] = pair_hi(u0.x, u0.y);  // (x1, x3)
-    xb[b][1][1] = pair_hi(u1.x, u1.y);  // (x9, x11)
-    xb[b][2][0] = pair_lo(u0.z, u0.w);  // (x4, x6)
-    xb[b][2][1] = pair_lo(u1.z, u1.w);  // (x12, x14)
-    xb[b][3][0] = pair_hi(u0.z, u0.w);  // (x5, x7)
-    xb[b][3][1] = pair_hi(u1.z, u1.w);  // (x13, x15)
+    if constexpr (kSplit) {
+      xb[b][0][0] = pair_lo(u0.x, u0.z);  // (x0, x4)
+      xb[b][0][1] = pair_hi(u0.x, u0.z);  // (x1, x5)
+      xb[b][1][0] = pair_lo(u0.y, u0.w);  // (x2, x6)
+      xb[b][1][1] = pair_hi(u0.y, u0.w);  // (x3, x7)
+      xb[b][2][0] = pair_lo(u1.x, u1.z);  // (x8, x12)
+      xb[b][2][1] = pair_hi(u1.x, u1.z);  // (x9, x13)
+      xb[b][3][0] = pair_lo(u1.y, u1.w);  // (x10, x14)
+      xb[b][3][1] = pair_hi(u1.y, u1.w);  // (x11, x15)
+    } else {
+      xb[b][0][0] = pair_lo(u0.x, u0.y);  // (x0, x2)
+      xb[b][0][1] = pair_lo(u1.x, u1.y);  // (x8, x10)
+      xb[b][1][0] = pair_hi(u0.x, u0.y);  // (x1, x3)
+      xb[b][1][1] = pair_hi(u1.x, u1.y);  // (x9, x11)
+      xb[b][2][0] = pair_lo(u0.z, u0.w);  // (x4, x6)
+      xb[b][2][1] = pair_lo(u1.z, u1.w);  // (x12, x14)
+      xb[b][3][0] = pair_hi(u0.z, u0.w);  // (x5, x7)
+      xb[b][3][1] = pair_hi(u1.z, u1.w);  // (x13, x15)
+    }
   }
-  const uint32_t so = static_cast<uint32_t>(warp) * 144u;  // four 36-byte blocks per slice
+  const uint32_t so = static_cast<uint32_t>(warp) * (kSplit ? 128u : 144u);  // four blocks per slice
+  const uint32_t sc0 = static_cast<uint32_t>(a.sc_off + g * a.sc_row_bytes) + 16u * warp;   // split: the slice's
+  const uint32_t sc1 = static_cast<uint32_t>(a.sc_off + (g + 8) * a.sc_row_bytes) + 16u * warp;  // 16 scale bytes
   const uint32_t r0 = static_cast<uint32_t>(g * a.stride), r1 = static_cast<uint32_t>((g + 8) * a.stride);
   int s = 0;
   uint32_t ph = 0;
@@ -95,11 +116,21 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid
     float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const uint32_t bo0 = r0 + so + 36u * b, bo1 = r1 + so + 36u * b;  // block: 4 scale bytes, 32 nibble bytes
-      const uint32_t* w0 = reinterpret_cast<const uint32_t*>(st + bo0 + 4u + 8u * t);
-      const uint32_t* w1 = reinterpret_cast<const uint32_t*>(st + bo1 + 4u + 8u * t);
-      const uint32_t v0[2] = {w0[0], w0[1]}, v1[2] = {w1[0], w1[1]};
-      const uint32_t s0 = fp4lut[st[bo0 + t]], s1 = fp4lut[st[bo1 + t]];
+      uint32_t v0[2], v1[2], s0, s1;
+      if constexpr (kSplit) {  // nibbles: 32 bytes per block, lane t's sub-block at 8 t; scales staged apart
+        const uint2 n0 = *reinterpret_cast<const uint2*>(st + r0 + so + 32u * b + 8u * t);
+        const uint2 n1 = *reinterpret_cast<const uint2*>(st + r1 + so + 32u * b + 8u * t);
+        v0[0] = n0.x; v0[1] = n0.y; v1[0] = n1.x; v1[1] = n1.y;
+        s0 = fp4lut[st[sc0 + 4u * b + t]];
+        s1 = fp4lut[st[sc1 + 4u * b + t]];
+      } else {
+        const uint32_t bo0 = r0 + so + 36u * b, bo1 = r1 + so + 36u * b;  // block: 4 scale bytes, 32 nibble bytes
+        const uint32_t* w0 = reinterpret_cast<const uint32_t*>(st + bo0 + 4u + 8u * t);
+        const uint32_t* w1 = reinterpret_cast<const uint32_t*>(st + bo1 + 4u + 8u * t);
+        v0[0] = w0[0]; v0[1] = w0[1]; v1[0] = w1[0]; v1[1] = w1[1];
+        s0 = fp4lut[st[bo0 + t]];
+        s1 = fp4lut[st[bo1 + t]];
+      }
       const uint32_t S0 = s0 | (s0 << 16), S1 = s1 | (s1 << 16);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {

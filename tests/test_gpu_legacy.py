@@ -109,6 +109,25 @@ def test_q4_split_few_row_kernel(cuda, R, N, K):
     assert rel(y, y_gen) < 2e-3
 
 
+@pytest.mark.parametrize("R", [2, 3, 8, 9])
+@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (61, 5120)])
+def test_fp4_split_few_row_kernel(cuda, R, N, K):
+    """Nvfp4Gemv gguf=0 through the few-row NVFP4 kernel (2 <= R <= 8; R = 9 takes the engine) against
+    the oracle and the generic engine, ragged N."""
+    g = I.rng(5 * N + K + R)
+    w, sc = I.legacy_case("fp4", g, N, K)
+    x = I.bf16_normal(g, (R, K), 2.0)
+    y = run_layout("fp4", x, w, sc, cuda).float().cpu().numpy()
+    assert np.isfinite(y).all()
+    assert rel(y, O.gemv_ref(x, deq("fp4", w, sc))) < TOL
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_layout("fp4", x, w, sc, cuda).float().cpu().numpy()
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+
+
 def test_legacy_reference_shapes(cuda):
     """The harness's shapes: Nvfp4 4096x4096 R=1..8, Q8 / Q4 [N, K/32, 32|16] (tests/test_bolt_ops.py:452-470)."""
     for layout, R, N, K in (("fp4", 1, 4096, 4096), ("fp4", 8, 1024, 8192), ("q8", 2, 4096, 4096),
