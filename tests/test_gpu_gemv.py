@@ -209,6 +209,37 @@ def test_single_row_fast_path(cuda, op, N, K, xscale):
     assert_device_ok()
 
 
+@pytest.mark.parametrize("N,K,xscale", [(2408, 4096, 1.0), (2650, 2048, 1.0), (2448, 5120, 1.0),
+                                        (14336, 4096, 3000.0), (14331, 4096, 1.0)])
+def test_iq2_single_row_partial_last_round(cuda, N, K, xscale):
+    """Single-row IQ2_XXS where the tiles leave a partial last round on 148 SMs (2408 rows: 151 tiles,
+    the last of 8 rows; 14336 rows: 896 tiles = 6 x 148 + 8; 14331 rows: the last tile of 11 rows).
+    Against the oracle on every row of the last tiles and a sample of the rest, against the generic
+    engine, and bit-identical over 70 launches (fixed-order reductions, no state kept between calls)."""
+    _, w, extra = I.gemv_case("iq2_xxs", 1, N, K, seed=N + K + 5)
+    x = I.bf16_normal(I.rng(N + K), (1, K), xscale)
+    x[:, 7] = O.bf16_bits(O.bf16_to_f32(x[:, 7]) * np.float32(300.0))  # bf16 bits: one outlier column
+    y = run_gemv("iq2_xxs", x, w, extra, cuda)
+    tail = np.arange(max(0, N - 200), N)  # the split tiles are the last ones
+    rows = np.union1d(tail, np.sort(I.rng(4).choice(N, size=min(N, 300), replace=False)))
+    assert rel(y[:, rows], oracle_y("iq2_xxs", x, w, extra, rows)) < TOL
+    assert rel(y[:, tail], oracle_y("iq2_xxs", x, w, extra, tail)) < TOL
+    xt, wt = bf16_t(x, cuda), u8_t(w, cuda)
+    outs = [ops.Q4Gemv(xt, wt, iq2=3) for _ in range(70)]
+    torch.cuda.synchronize()
+    ref = outs[0].view(torch.int16)
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), ref)
+    assert np.array_equal(np_f32(outs[0]), y)
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_gemv("iq2_xxs", x, w, extra, cuda)
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+    assert_device_ok()
+
+
 @pytest.mark.parametrize("R", [2, 3, 4, 5, 8])
 @pytest.mark.parametrize("N,K,xscale", [(37, 2048, 1.0), (200, 4096, 1.0), (1000, 4096, 3000.0), (61, 5120, 1.0)])
 def test_iq2_few_row_integer_kernel(cuda, R, N, K, xscale):
