@@ -560,9 +560,10 @@ int try_q8s_rows(const void* x, const void* w, const void* scales, void* y, int 
   }
 }
 
-// NVFP4 2 <= R <= 8 on the bf16 tensor cores with the activation rows as MMA columns
-// (slice_fp4_rows.cuh): 16 whole rows per stage at pitch row bytes + 32.
-template <int kW>
+// NVFP4 2 <= R <= 8 kNB on the bf16 tensor cores with the activation rows as MMA columns
+// (slice_fp4_rows.cuh): 16 whole rows per stage at pitch row bytes + 32; with kNB = 2 the second
+// set of 8 rows is packed into 4 KB of shared memory per warp, ahead of the stages.
+template <int kW, int kNB = 1>
 int run_slice_fp4_rows(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
   SliceArgs a = {};
   a.w = static_cast<const uint8_t*>(w);
@@ -576,17 +577,18 @@ int run_slice_fp4_rows(const void* x, const void* w, const float* gscale, void* 
   a.tiles = (N + 15) / 16;
   a.stride = a.row_bytes + 32;  // row words = 8 or 24 mod 32 for K = 2048, 4096, 5120
   a.stage_bytes = (16 * a.stride + 127) & ~127;
-  const int lut = 512, red_per_stage = kW * 8 * 16 * 4 + 4;
-  a.stages = std::min(4, (kSmemBudgetMax - lut - 256) / (a.stage_bytes + red_per_stage + 16));
+  const int lut = 512, red_per_stage = kW * 8 * kNB * 16 * 4 + 4, xs2 = kNB == 2 ? kW * 16 * 32 * 8 : 0;
+  a.stages = std::min(4, (kSmemBudgetMax - lut - xs2 - 256) / (a.stage_bytes + red_per_stage + 16));
   if (a.stages < 2) return -1;
-  a.off_stage = lut;
-  a.off_red = lut + a.stages * a.stage_bytes;
+  a.off_x2 = lut;
+  a.off_stage = lut + xs2;
+  a.off_red = a.off_stage + a.stages * a.stage_bytes;
   a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
   const size_t smem = a.off_bar + 2 * a.stages * 8;
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   static std::atomic<uint64_t> done{0};
-  auto kern = slice_fp4_rows_kernel<kW>;
+  auto kern = slice_fp4_rows_kernel<kW, false, kNB>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
   cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row NVFP4 GEMV launch", e);
@@ -651,6 +653,11 @@ int try_fp4_rows(const void* x, const void* w, const float* gscale, void* y, int
   if (g_fast.load() != 1 || R < 2 || R > 16) return -1;
   if (K != 2048 && K != 4096 && K != 5120) return -1;
   if (R > 8) {
+    // one launch, each decoded weight fragment feeding both activation sets
+    const int r2 = K == 2048 ? run_slice_fp4_rows<8, 2>(x, w, gscale, y, R, N, K, s)
+                             : (K == 4096 ? run_slice_fp4_rows<16, 2>(x, w, gscale, y, R, N, K, s)
+                                          : run_slice_fp4_rows<20, 2>(x, w, gscale, y, R, N, K, s));
+    if (r2 >= 0) return r2;
     const int rc = try_fp4_rows(x, w, gscale, y, 8, N, K, s);
     if (rc != GGUF_OK) return rc;
     const bf16* x8 = static_cast<const bf16*>(x) + static_cast<int64_t>(8) * K;

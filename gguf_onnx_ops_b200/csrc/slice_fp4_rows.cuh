@@ -30,13 +30,14 @@ namespace gguf_b200 {
 // of byte i, e4m3fn scales [N, K/16] in a second tensor).  Its sub-block words pair the elements
 // (0,4) (1,5), (2,6) (3,7), ... instead, the scale table holds e4m3fn * 2^110, and a stage carries
 // the tile's 16 scale rows after its 16 weight rows (lane t's nibbles: bytes 32 b + 8 t of the slice).
-template <int kW, bool kSplit = false>
+template <int kW, bool kSplit = false, int kNB = 1>
 __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid_constant__ SliceArgs a) {
+  static_assert(kNB == 1 || (kNB == 2 && !kSplit), "two activation sets: GGUF layout only");
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   uint8_t* stages = smem + a.off_stage;
-  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [stages][kW][8 activation rows][16]
-  int* cnt = reinterpret_cast<int*>(red + a.stages * kW * 8 * 16);  // [stages]
+  float* red = reinterpret_cast<float*>(smem + a.off_red);  // [stages][kW][8 kNB activation rows][16]
+  int* cnt = reinterpret_cast<int*>(red + a.stages * kW * 8 * kNB * 16);  // [stages]
   const uint16_t* fp4lut = reinterpret_cast<const uint16_t*>(smem);  // [256] scale * 2^110, bf16 bits
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -75,35 +76,52 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid
 
   const int g = lane >> 2, t = lane & 3;
   // ---- B fragments: activation row g, elements 16t..16t+15 of the slice's four blocks ----
-  uint32_t xb[4][4][2];  // [block][MMA][b0 / b1]
+  uint32_t xb[4][4][2];  // [block][MMA][b0 / b1] of activation rows 0..7
+  // kNB = 2: the fragments of activation rows 8..15, packed once per launch into this warp's
+  // [block][MMA][lane] area of shared memory (one 8-byte load per MMA, conflict-free)
+  uint2* xs2 = reinterpret_cast<uint2*>(smem + a.off_x2) + warp * 16 * 32;
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    uint4 u0 = make_uint4(0u, 0u, 0u, 0u), u1 = u0;
-    if (g < a.R) {
-      const bf16* xp = a.x + static_cast<int64_t>(g) * a.K + warp * 256 + 64 * b + 16 * t;
-      u0 = ldg128(xp);
-      u1 = ldg128(xp + 8);
-    }
-    if constexpr (kSplit) {
-      xb[b][0][0] = pair_lo(u0.x, u0.z);  // (x0, x4)
-      xb[b][0][1] = pair_hi(u0.x, u0.z);  // (x1, x5)
-      xb[b][1][0] = pair_lo(u0.y, u0.w);  // (x2, x6)
-      xb[b][1][1] = pair_hi(u0.y, u0.w);  // (x3, x7)
-      xb[b][2][0] = pair_lo(u1.x, u1.z);  // (x8, x12)
-      xb[b][2][1] = pair_hi(u1.x, u1.z);  // (x9, x13)
-      xb[b][3][0] = pair_lo(u1.y, u1.w);  // (x10, x14)
-      xb[b][3][1] = pair_hi(u1.y, u1.w);  // (x11, x15)
-    } else {
-      xb[b][0][0] = pair_lo(u0.x, u0.y);  // (x0, x2)
-      xb[b][0][1] = pair_lo(u1.x, u1.y);  // (x8, x10)
-      xb[b][1][0] = pair_hi(u0.x, u0.y);  // (x1, x3)
-      xb[b][1][1] = pair_hi(u1.x, u1.y);  // (x9, x11)
-      xb[b][2][0] = pair_lo(u0.z, u0.w);  // (x4, x6)
-      xb[b][2][1] = pair_lo(u1.z, u1.w);  // (x12, x14)
-      xb[b][3][0] = pair_hi(u0.z, u0.w);  // (x5, x7)
-      xb[b][3][1] = pair_hi(u1.z, u1.w);  // (x13, x15)
+  for (int nb = 0; nb < kNB; ++nb) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      uint4 u0 = make_uint4(0u, 0u, 0u, 0u), u1 = u0;
+      if (8 * nb + g < a.R) {
+        const bf16* xp = a.x + static_cast<int64_t>(8 * nb + g) * a.K + warp * 256 + 64 * b + 16 * t;
+        u0 = ldg128(xp);
+        u1 = ldg128(xp + 8);
+      }
+      uint32_t f[4][2];
+      if constexpr (kSplit) {
+        f[0][0] = pair_lo(u0.x, u0.z);  // (x0, x4)
+        f[0][1] = pair_hi(u0.x, u0.z);  // (x1, x5)
+        f[1][0] = pair_lo(u0.y, u0.w);  // (x2, x6)
+        f[1][1] = pair_hi(u0.y, u0.w);  // (x3, x7)
+        f[2][0] = pair_lo(u1.x, u1.z);  // (x8, x12)
+        f[2][1] = pair_hi(u1.x, u1.z);  // (x9, x13)
+        f[3][0] = pair_lo(u1.y, u1.w);  // (x10, x14)
+        f[3][1] = pair_hi(u1.y, u1.w);  // (x11, x15)
+      } else {
+        f[0][0] = pair_lo(u0.x, u0.y);  // (x0, x2)
+        f[0][1] = pair_lo(u1.x, u1.y);  // (x8, x10)
+        f[1][0] = pair_hi(u0.x, u0.y);  // (x1, x3)
+        f[1][1] = pair_hi(u1.x, u1.y);  // (x9, x11)
+        f[2][0] = pair_lo(u0.z, u0.w);  // (x4, x6)
+        f[2][1] = pair_lo(u1.z, u1.w);  // (x12, x14)
+        f[3][0] = pair_hi(u0.z, u0.w);  // (x5, x7)
+        f[3][1] = pair_hi(u1.z, u1.w);  // (x13, x15)
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (nb == 0) {
+          xb[b][q][0] = f[q][0];
+          xb[b][q][1] = f[q][1];
+        } else {
+          xs2[(b * 4 + q) * 32 + lane] = make_uint2(f[q][0], f[q][1]);
+        }
+      }
     }
   }
+  if (kNB == 2) __syncwarp();  // each warp reads back only its own area
   const uint32_t so = static_cast<uint32_t>(warp) * (kSplit ? 128u : 144u);  // four blocks per slice
   const uint32_t sc0 = static_cast<uint32_t>(a.sc_off + g * a.sc_row_bytes) + 16u * warp;   // split: the slice's
   const uint32_t sc1 = static_cast<uint32_t>(a.sc_off + (g + 8) * a.sc_row_bytes) + 16u * warp;  // 16 scale bytes
@@ -113,6 +131,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid
   for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
     mbar_wait(&full[s], ph, kSiteFullWait);
     const uint8_t* st = stages + s * a.stage_bytes;
+    // two accumulator chains: the MMA parity (one activation set) or the set (kNB = 2)
     float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
@@ -141,25 +160,41 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_fp4_rows_kernel(const __grid
         const uint32_t a2 = hmul2_bits(((u0 & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S0);
         const uint32_t a1 = hmul2_bits(((u1 & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S1);
         const uint32_t a3 = hmul2_bits(((u1 & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S1);
-        mma_bf16_16816(c[q & 1], a0, a1, a2, a3, xb[b][q][0], xb[b][q][1], c[q & 1]);
+        if constexpr (kNB == 1) {
+          mma_bf16_16816(c[q & 1], a0, a1, a2, a3, xb[b][q][0], xb[b][q][1], c[q & 1]);
+        } else {
+          const uint2 y2 = xs2[(b * 4 + q) * 32 + lane];
+          mma_bf16_16816(c[0], a0, a1, a2, a3, xb[b][q][0], xb[b][q][1], c[0]);
+          mma_bf16_16816(c[1], a0, a1, a2, a3, y2.x, y2.y, c[1]);
+        }
       }
     }
     // lane's C: rows g / g+8 x activation rows 2t, 2t+1
-    float* rb = red + (s * kW + warp) * 8 * 16;
-    rb[(2 * t) * 16 + g] = (c[0][0] + c[1][0]) * post;
-    rb[(2 * t + 1) * 16 + g] = (c[0][1] + c[1][1]) * post;
-    rb[(2 * t) * 16 + g + 8] = (c[0][2] + c[1][2]) * post;
-    rb[(2 * t + 1) * 16 + g + 8] = (c[0][3] + c[1][3]) * post;
+    float* rb = red + (s * kW + warp) * 8 * kNB * 16;
+    if constexpr (kNB == 1) {
+      rb[(2 * t) * 16 + g] = (c[0][0] + c[1][0]) * post;
+      rb[(2 * t + 1) * 16 + g] = (c[0][1] + c[1][1]) * post;
+      rb[(2 * t) * 16 + g + 8] = (c[0][2] + c[1][2]) * post;
+      rb[(2 * t + 1) * 16 + g + 8] = (c[0][3] + c[1][3]) * post;
+    } else {
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        rb[(8 * nb + 2 * t) * 16 + g] = c[nb][0] * post;
+        rb[(8 * nb + 2 * t + 1) * 16 + g] = c[nb][1] * post;
+        rb[(8 * nb + 2 * t) * 16 + g + 8] = c[nb][2] * post;
+        rb[(8 * nb + 2 * t + 1) * 16 + g + 8] = c[nb][3] * post;
+      }
+    }
     __syncwarp();  // orders the lanes' slot writes before lane 0's release below
     int last = 0;
     if (lane == 0) last = atom_add_acq_rel_cta(&cnt[s], 1) == kW - 1;
     if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this tile are in the slot
-      const float* rs = red + s * kW * 8 * 16;
+      const float* rs = red + s * kW * 8 * kNB * 16;
 #pragma unroll
-      for (int o = lane; o < 8 * 16; o += 32) {
+      for (int o = lane; o < 8 * kNB * 16; o += 32) {
         float v[4] = {0.f, 0.f, 0.f, 0.f};  // fixed summation order: 4 strided partial sums, then a tree
 #pragma unroll
-        for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rs[w2 * 8 * 16 + o];
+        for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rs[w2 * 8 * kNB * 16 + o];
         const int xr = o >> 4, row = tile * 16 + (o & 15);
         if (xr < a.R && row < a.N) a.y[static_cast<int64_t>(xr) * a.N + row] = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
       }

@@ -60,6 +60,8 @@ struct SliceArgs {
   // staged after the 16 weight rows at stage offset sc_off
   const uint8_t* sc;
   int sc_row_bytes, sc_off;
+  // slice_fp4_rows_kernel with two activation sets: byte offset of the per-warp fragment areas
+  int off_x2;
 };
 
 template <int F>

@@ -281,11 +281,12 @@ def test_q8_few_row_integer_kernel(cuda, R, N, K, xscale):
 
 
 @pytest.mark.parametrize("R", [2, 3, 5, 8, 9, 12, 16])
-@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (333, 5120)])
+@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (333, 5120), (4000, 5120)])
 def test_nvfp4_few_row_kernel(cuda, R, N, K):
-    """The few-row NVFP4 kernel (2 <= R <= 8: activation rows as the MMA columns, scales inside the
-    exact bf16 weights; R > 8 as two launches, R = 9 with the single-row kernel for the last row)
-    against the oracle and the generic engine, every scale byte present."""
+    """The few-row NVFP4 kernel (activation rows as the MMA columns, scales inside the exact bf16
+    weights; R = 9..16 in one launch with a second set of 8 activation rows, whose fragments sit in
+    shared memory) against the oracle and the generic engine, every scale byte present; 4000 rows
+    give every CTA 2 stages' worth of tiles and a ragged last tile."""
     g = I.rng(K + 11 * R + N)
     w = I.nvfp4_weights(g, N, K, 0, 255)
     x = I.bf16_normal(g, (R, K), 2.0)
