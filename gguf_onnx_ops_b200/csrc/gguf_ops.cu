@@ -486,11 +486,13 @@ int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, in
 // Dispatches 1 <= R <= 16 Q8_0 to the few-row integer kernel when K allows it (R > 8: K = 4096
 // only); -1 otherwise.  One row uses four-row MMA columns with three empty rows: the quants need
 // no decode, so the kernel is HBM-bound at large N even so (C4 R = 1: 91 µs, 0.96 of peak, where
-// the bf16 slice kernel took 115 µs).
+// the bf16 slice kernel took 115 µs).  R > 8 runs 8 warps of two slices each: 256 threads leave
+// each thread the 255 registers that four MMA sets for two slices need (16 warps capped at 128
+// spilled), and the reduction slots stay small (C4 R = 16: 153 µs against 185 with 16 warps).
 int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s,
                 const PeerOut* po = nullptr) {
   if (g_fast.load() != 1 || R < 1 || R > 16) return -1;
-  if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<16, 4>(x, w, y, R, N, K, s, po) : -1;
+  if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<8, 4, 2>(x, w, y, R, N, K, s, po) : -1;
   const bool two = R > 4;
   switch (K) {
     case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s, po);
@@ -550,7 +552,7 @@ int try_q4s_rows(const void* x, const void* w, const void* scales, void* y, int 
 
 int try_q8s_rows(const void* x, const void* w, const void* scales, void* y, int R, int N, int K, cudaStream_t s) {
   if (g_fast.load() != 1 || R < 1 || R > 16) return -1;
-  if (R > 8) return K == 4096 ? run_slice_q8s_rows<16, 4>(x, w, scales, y, R, N, K, s) : -1;
+  if (R > 8) return K == 4096 ? run_slice_q8s_rows<8, 4, 2>(x, w, scales, y, R, N, K, s) : -1;
   const bool two = R > 4;
   switch (K) {
     case 2048: return two ? run_slice_q8s_rows<8, 2>(x, w, scales, y, R, N, K, s) : run_slice_q8s_rows<8, 1>(x, w, scales, y, R, N, K, s);
