@@ -73,10 +73,11 @@ def test_legacy_k_staging_modes(cuda, layout, K):
 
 
 @pytest.mark.parametrize("R", [1, 3, 5, 8, 12, 16])
-@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (61, 5120)])
+@pytest.mark.parametrize("N,K", [(37, 2048), (200, 4096), (61, 5120), (5000, 4096)])
 def test_q8_split_few_row_kernel(cuda, R, N, K):
     """Q8Gemv gguf=0 through the few-row integer kernel (K = 2048 / 4096 / 5120; R > 8 at K = 4096
-    only) against the oracle and the generic engine, ragged N."""
+    only, 8 warps of two slices) against the oracle and the generic engine, ragged N; 5000 rows give
+    every CTA several tiles (the staging ring wraps)."""
     g = I.rng(N + K + R)
     w, sc = I.legacy_case("q8", g, N, K)
     x = I.bf16_normal(g, (R, K), 2.0)
