@@ -649,8 +649,9 @@ int try_fp4s_rows(const void* x, const void* w, const void* scales, const float*
   }
 }
 
-// Dispatches 2 <= R <= 16 NVFP4 to the few-row kernel when K allows it (R > 8: two launches, rows
-// 0..7 and 8..R-1, each streaming the weights once); -1 otherwise.
+// Dispatches 2 <= R <= 16 NVFP4 to the few-row kernel when K allows it (R > 8: one launch with two
+// activation sets, or, where that plan does not fit shared memory, two launches for rows 0..7 and
+// 8..R-1, each streaming the weights once); -1 otherwise.
 int try_fp4_rows(const void* x, const void* w, const float* gscale, void* y, int R, int N, int K, cudaStream_t s) {
   if (g_fast.load() != 1 || R < 2 || R > 16) return -1;
   if (K != 2048 && K != 4096 && K != 5120) return -1;
