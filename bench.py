@@ -19,10 +19,11 @@ N=14336 -- as weight-stream GB/s (algorithmic bytes = the weight tensor, 15,138,
   on a bounded row sample, all host threads.
 * configs = every BASELINE config at 1 GPU (skipped with --quick or N > 1).
 
-N > 1 (torchrun): config 1 does not shard (replicas only): every rank runs the same workload on its
-own GPU; the timing is the max over ranks.  The line then also carries "sharded": the C4 LM head
-(Q8_0, N=131072) row-split over the N GPUs with the all-gather fused into the GEMV kernel, next to
-the same GEMV followed by an NCCL all-gather.
+N > 1 (torchrun): the headline is the sharded config, BASELINE config 4 (the Q8_0 LM head, R=1,
+N=131072) row-split over the N GPUs with the all-gather fused into the GEMV kernel (strong scaling,
+value = whole-tensor bytes / max-over-ranks time per call; parity against the single-GPU op checked
+in the same run).  The line also carries the same workload on one GPU, C4 at R=4/8/16, the GEMV +
+NCCL all-gather baseline, the expert-parallel C3 MoE and config 1 as independent replicas.
 ``--impl reference`` times the reference's CPU path (oracle port) on the same metric.
 """
 
@@ -56,7 +57,100 @@ def parse_args():
     ap.add_argument("--quick", action="store_true", help="headline only")
     ap.add_argument("--cpu-table", action="store_true",
                     help="print the reference CPU path's time per BASELINE config (host cores only) and exit")
+    # --profile-case: run one op a few times with eager launches (the target of the ncu captures
+    # whose summaries are in profiles/), then exit
+    ap.add_argument("--profile-case", action="store_true", help="run one op --iters times (for ncu) and exit")
+    ap.add_argument("--op", default="iq2_xxs",
+                    choices=["q8_0", "iq2_xxs", "nvfp4", "moe", "route", "embed", "norm", "q4_split", "mamba"])
+    ap.add_argument("--R", type=int, default=1)
+    ap.add_argument("--N", type=int, default=14336)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--copies", type=int, default=3)
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--fast-mode", type=int, default=1, help="gguf_set_fast_paths value (0 = generic engine)")
     return ap.parse_args()
+
+
+def profile_case(a):
+    """One op, `a.iters` eager launches on cuda:0 (weights with the BASELINE distributions, a distinct
+    weight copy per iteration when `a.copies` > 1 so that launches stream from HBM, not L2):
+
+        python bench.py --profile-case --op iq2_xxs --R 1 --N 14336 --K 4096 --iters 3
+        python bench.py --profile-case --op moe --R 1 --iters 3
+        python bench.py --profile-case --op embed --R 4096 --N 131072 --K 4096
+        python bench.py --profile-case --op norm --R 4096 --K 4096
+        python bench.py --profile-case --op q4_split --R 1 --N 14336 --K 4096
+        python bench.py --profile-case --op mamba --R 1
+    """
+    import torch
+
+    from gguf_onnx_ops_b200 import ops
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    ops.set_pdl(not a.no_pdl)
+    ops.set_fast_paths(a.fast_mode)
+    if a.op == "embed":  # Q8Embed: R ids from a [N, K] Q8_0 table
+        table = gen_weights("q8_0", a.N, a.K, seed=4, dev=dev)
+        ids = torch.randint(0, a.N, (a.R,), device=dev)
+        out = torch.empty(a.R, a.K, dtype=torch.bfloat16, device=dev)
+        for _ in range(a.iters):
+            ops.q8_0_embed_into(table, ids, out, a.N, a.K // 32 * 34, a.R)
+    elif a.op == "norm":  # SkipRmsNorm [R, K] with the sum written
+        xs = [torch.randn(a.R, a.K, device=dev).bfloat16() for _ in range(a.copies)]
+        sk = torch.randn(a.R, a.K, device=dev).bfloat16()
+        gamma = torch.rand(a.K, device=dev) + 0.5
+        y, sm = torch.empty_like(sk), torch.empty_like(sk)
+        for i in range(a.iters):
+            ops.rms_norm_into(xs[i % a.copies], sk, gamma, y, sm, a.R, a.K, 1e-5)
+    elif a.op == "q4_split":  # Q4Gemv iq2=0 (legacy split layout)
+        from gguf_onnx_ops_b200 import _lib
+
+        ws = [torch.randint(0, 256, (a.N, a.K // 2), device=dev, dtype=torch.uint8) for _ in range(a.copies)]
+        sc = (torch.rand(a.N, a.K // 32, device=dev) * 0.02).bfloat16()
+        x = torch.randn(a.R, a.K, device=dev).bfloat16()
+        y = torch.empty(a.R, a.N, dtype=torch.bfloat16, device=dev)
+        for i in range(a.iters):
+            ops.gemv_legacy_into(_lib.GGUF_LAYOUT_Q4_SPLIT, x, ws[i % a.copies], sc, None, y, a.R, a.N, a.K)
+    elif a.op == "mamba":  # MambaStep, heads 128, n_groups 8
+        heads, ng = 128, 8
+        di, cd = heads * 64, heads * 64 + 2 * ng * 128
+        proj = torch.randn(a.R, di + cd + heads, device=dev).bfloat16()
+        cs = torch.randn(1, cd, 3, device=dev).bfloat16()
+        ss = [torch.randn(1, heads, 128, 64, device=dev) * 0.1 for _ in range(a.copies)]
+        cw, cb = (torch.randn(cd, 4, device=dev) * 0.3).bfloat16(), (torch.randn(cd, device=dev) * 0.1).bfloat16()
+        hv = [torch.randn(heads, device=dev) for _ in range(3)]
+        nw = torch.rand(di, device=dev) + 0.5
+        y = torch.empty(a.R, di, dtype=torch.bfloat16, device=dev)
+        cso, sso = torch.empty_like(cs), torch.empty_like(ss[0])
+        xbc = torch.empty(a.R, cd, dtype=torch.bfloat16, device=dev)
+        ypre = torch.empty(a.R, di, device=dev)
+        for i in range(a.iters):
+            ops.mamba_step_into(proj, cs, ss[i % a.copies], cw, cb, hv[0], -hv[1].abs(), hv[2], nw, None, y, cso, sso,
+                                xbc, ypre, R=a.R, state_rows=1, heads=heads, n_groups=ng, eps=1e-5, tmin=0.001)
+    elif a.op in ("moe", "route"):
+        E, H, I, topk = 128, 1024, 1792, 6
+        w1 = gen_weights("iq2_xxs", E * I, H, seed=2, dev=dev).reshape(E, I, -1)
+        w2 = gen_weights("iq2_xxs", E * H, I, seed=3, dev=dev).reshape(E, H, -1)
+        gw = torch.randn(E, H, device=dev) * 0.02
+        bias = torch.randn(E, device=dev) * 0.01
+        x = torch.randn(a.R, H, device=dev).bfloat16()
+        z = torch.randn(a.R, H, device=dev).bfloat16()
+        for _ in range(a.iters):
+            idx, wt, _ = ops.MoeRouteGGUF(x, gw, bias, topk, 1.0)
+            if a.op == "moe":
+                ops.MoeVerify(z, idx, wt, w1, None, w2, None, topk=topk)
+    else:
+        base = gen_weights(a.op, a.N, a.K, seed=1, dev=dev)
+        ws = replicate(base, a.copies)
+        x = torch.randn(a.R, a.K, device=dev).bfloat16()
+        gs = torch.tensor([1.0 / 448.0], device=dev)
+        y = torch.empty(a.R, a.N, dtype=torch.bfloat16, device=dev)
+        for i in range(a.iters):
+            gemv_call(a.op, x, ws[i % len(ws)], y, gs, a.R, a.N, a.K)
+    torch.cuda.synchronize()
+    print("ok")
 
 
 def cpu_table():
@@ -316,11 +410,24 @@ def bench_gemv(op, R, N, K, steps, warmup, dev, target_step_ms=8.0, world=1, sam
     return out, (ws, x, ys, gs, wbytes, copies)
 
 
-def bench_rowsplit(R, steps, warmup, dev, world, rank):
+def seeded_bf16(shape, seed, dev):
+    """bf16 N(0, 1) from a seeded device generator: the same tensor on every rank."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return torch.randn(*shape, generator=g, device=dev).bfloat16()
+
+
+def bench_rowsplit(R, steps, warmup, dev, world, rank, nccl=False, e2e=False, sampler=None):
     """C4 LM head (Q8_0, N=131072, K=4096) row-split over the group: per call, each GPU streams its
     N/world rows and stores its y shard into every GPU's y inside the same kernel (NVLink peer
-    stores + epoch flags).  Baseline: the same per-GPU GEMV into a local shard followed by an NCCL
-    all-gather (both captured in CUDA graphs).  Times are the max over ranks."""
+    stores + epoch flags).  Every rank builds the same full weight matrix and keeps its shard, so
+    before timing the gathered y of one call is compared bit for bit with the single-GPU op on the
+    full matrix (same kernel per row: equal bits expected), on every rank.  Optional baseline: the
+    same per-GPU GEMV into a local shard followed by an NCCL all-gather (R = 1).  Optional e2e: x from
+    pinned host memory, one pass of calls, every y back to pinned host memory on rank 0.  Times are
+    the max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -328,28 +435,78 @@ def bench_rowsplit(R, steps, warmup, dev, world, rank):
     from gguf_onnx_ops_b200.sharded import RowSplitGemv, shard_rows
 
     N, K = 131072, 4096
+    rb = ROW_BYTES["q8_0"](K)
     row0, rows = shard_rows(N, world, rank)
-    wbytes = rows * ROW_BYTES["q8_0"](K)
-    copies = n_copies(wbytes)
+    full = gen_weights("q8_0", N, K, seed=1, dev=dev)  # the same on every rank
+    base = full[row0:row0 + rows].contiguous()
+    copies = n_copies(rows * rb)
     copies += copies & 1  # an even number of calls per pass keeps the double-buffer parity fixed
-    base = gen_weights("q8_0", rows, K, seed=1 + rank, dev=dev)
+    x = seeded_bf16((R, K), 100 + R, dev)
+    op = RowSplitGemv(_lib.GGUF_TYPE_Q8_0, base, N, row0, K, r_max=R)
+    # parity: the gathered y against the single-GPU op on the full matrix
+    y = op(x, w=base)
+    y_ref = torch.empty(R, N, dtype=torch.bfloat16, device=dev)
+    ops.q8_0_gemv_into(x, full, y_ref, R, N, K)
+    torch.cuda.synchronize()
+    bad = torch.tensor([float((y.view(torch.int16) != y_ref.view(torch.int16)).sum().item())], device=dev)
+    dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+    mismatches = int(bad.item())
+    del full, y_ref, y
     ws = replicate(base, copies)
     del base
-    x = torch.randn(R, K, device=dev).bfloat16()
-    op = RowSplitGemv(_lib.GGUF_TYPE_Q8_0, ws[0], N, row0, K, r_max=R)
+    torch.cuda.empty_cache()
 
     def fused_pass():
         for w in ws:
             op(x, w=w)
 
     g = capture(fused_pass)
-    ms = max_over_ranks(time_graph(g, steps, warmup, world), world)
+    if sampler is not None:
+        with sampler:
+            ms = max_over_ranks(time_graph(g, steps, warmup, world), world)
+    else:
+        ms = max_over_ranks(time_graph(g, steps, warmup, world), world)
     del g
     fused_us = ms * 1e3 / (steps * copies)
-    y_local = torch.empty(R, rows, dtype=torch.bfloat16, device=dev)
-    y_all = torch.empty(world * R * rows, dtype=torch.bfloat16, device=dev)
-    nccl_us, nccl_err = None, None
-    if R == 1 and N % world == 0:
+    total = N * rb
+    out = dict(world=world, R=R, fused_us_per_call=fused_us, fused_gbs=total / (fused_us * 1e-6) / 1e9,
+               rows_per_gpu=rows, copies=copies, calls=steps * copies, ms_total=ms,
+               parity="ok" if mismatches == 0 else f"mismatch: {mismatches} of {R * N} values differ (max over ranks)",
+               parity_check="gathered y of one call == single-GPU Q8Gemv on the full matrix, bit for bit, every rank")
+    if e2e:
+        # public API end to end: pinned host x -> device, one pass of row-split calls, y -> pinned host
+        xh = torch.randn(R, K).bfloat16().pin_memory()
+        yh = torch.empty(copies, R, N, dtype=torch.bfloat16).pin_memory()
+        xd = torch.empty_like(x)
+        copy_stream = torch.cuda.Stream()
+        done = [torch.cuda.Event() for _ in range(copies)]
+        copied = [torch.cuda.Event() for _ in range(copies)]
+
+        def step():
+            xd.copy_(xh, non_blocking=True)
+            for i, w in enumerate(ws):
+                if rank == 0 and i >= 2:  # call i reuses call i-2's y buffer: its copy must be done
+                    torch.cuda.current_stream().wait_event(copied[i - 2])
+                yy = op(xd, w=w)
+                if rank == 0:
+                    done[i].record()
+                    with torch.cuda.stream(copy_stream):
+                        copy_stream.wait_event(done[i])
+                        yh[i].copy_(yy, non_blocking=True)
+                        copied[i].record()
+            if rank == 0:
+                torch.cuda.current_stream().wait_stream(copy_stream)
+
+        g2 = capture(step)
+        ms2 = max_over_ranks(time_graph(g2, steps, warmup, world), world)
+        del g2
+        ms_step = ms2 / steps
+        out["e2e"] = dict(value=total * copies / (ms_step * 1e-3) / 1e9, unit="GB/s", h2d_bytes_per_step=R * K * 2,
+                          d2h_bytes_per_step=copies * R * N * 2, ms_per_step=ms_step,
+                          note="x copied from pinned host memory on every rank; every y read back on rank 0")
+    if nccl and R == 1 and N % world == 0:
+        y_local = torch.empty(R, rows, dtype=torch.bfloat16, device=dev)
+        y_all = torch.empty(world * R * rows, dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(y_all, y_local.view(-1))  # warm the communicator outside capture
         torch.cuda.synchronize()
 
@@ -362,56 +519,86 @@ def bench_rowsplit(R, steps, warmup, dev, world, rank):
             g2 = capture(nccl_pass)
             ms2 = max_over_ranks(time_graph(g2, steps, warmup, world), world)
             del g2  # graphs holding NCCL calls are released before the process group
-            nccl_us = ms2 * 1e3 / (steps * copies)
+            out["nccl_us_per_call"] = ms2 * 1e3 / (steps * copies)
+            out["nccl_gbs"] = total / (out["nccl_us_per_call"] * 1e-6) / 1e9
         except Exception as e:  # noqa: BLE001 -- the baseline is optional; report why it is missing
-            nccl_us = None
-            nccl_err = f"{type(e).__name__}: {str(e)[:160]}"
+            out["nccl_error"] = f"{type(e).__name__}: {str(e)[:160]}"
     torch.cuda.synchronize()
-    rc, site = _lib.device_status()
+    out["device_status"] = _lib.device_status()[0]
     op.close()
-    total = N * ROW_BYTES["q8_0"](K)
-    return dict(world=world, R=R, fused_us_per_call=fused_us, fused_gbs=total / (fused_us * 1e-6) / 1e9,
-                nccl_us_per_call=nccl_us, nccl_gbs=None if nccl_us is None else total / (nccl_us * 1e-6) / 1e9,
-                rows_per_gpu=rows, copies=copies, device_status=rc, **({"nccl_error": nccl_err} if nccl_err else {}))
+    del ws
+    torch.cuda.empty_cache()
+    return out
+
+
+def bench_single_c4(R, steps, warmup, dev):
+    """C4 R on this GPU alone (the 1-GPU point of the row-split curve, measured in the same run)."""
+    r, st = bench_gemv("q8_0", R, 131072, 4096, steps, warmup, dev, target_step_ms=4.0)
+    del st
+    return r["us_per_call"]
 
 
 def bench_moe_ep(R, steps, warmup, dev, world, rank):
-    """C3 MoeVerify with the 128 experts split over the group (expert parallelism, partial outputs
-    summed through peer memory inside the finalize kernel); idx from one router call (replicated).
-    Time per call = max over ranks."""
+    """C3 (MoeRouteGGUF -> MoeVerify iq2=3, E=128, I=1792, topk=6) with the experts split over the
+    group: each call runs the router (replicated) and the expert-parallel MoeVerify (partial outputs
+    summed through peer memory inside the finalize kernel).  Every rank builds the same 128 experts
+    and keeps its share, rotated over distinct copies (> 2x L2 per GPU) so that every call streams its
+    experts from HBM.  Before timing the output is compared with the single-GPU MoeVerify on all
+    experts (rel-L2 <= 5e-3, max over ranks).  Time per call = max over ranks."""
     import torch
+    import torch.distributed as dist
 
     from gguf_onnx_ops_b200 import _lib, ops
     from gguf_onnx_ops_b200.sharded import ExpertParallelMoE, shard_experts
 
     E, H, I, topk = 128, 1024, 1792, 6
     e0, el = shard_experts(E, world, rank)
-    w1 = gen_weights("iq2_xxs", el * I, H, seed=2 + rank, dev=dev).reshape(el, I, -1)
-    w2 = gen_weights("iq2_xxs", el * H, I, seed=40 + rank, dev=dev).reshape(el, H, -1)
-    torch.manual_seed(R)  # the same routing on every rank
-    gw = torch.randn(E, H, device=dev) * 0.02
-    bias = torch.randn(E, device=dev) * 0.01
-    x = torch.randn(R, H, device=dev).bfloat16()
-    z = torch.randn(R, H, device=dev).bfloat16()
-    idx, wt, _ = ops.MoeRouteGGUF(x, gw, bias, topk, 1.0)
-    op = ExpertParallelMoE(w1, w2, e0, topk, r_max=8)
+    w1 = gen_weights("iq2_xxs", E * I, H, seed=2, dev=dev).reshape(E, I, -1)
+    w2 = gen_weights("iq2_xxs", E * H, I, seed=3, dev=dev).reshape(E, H, -1)
+    w1l, w2l = w1[e0:e0 + el].contiguous(), w2[e0:e0 + el].contiguous()
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    gw = torch.randn(E, H, generator=g, device=dev) * 0.02
+    bias = torch.randn(E, generator=g, device=dev) * 0.01
+    x, z = seeded_bf16((R, H), 200 + R, dev), seeded_bf16((R, H), 300 + R, dev)
+    idx = torch.empty(R, topk, dtype=torch.int32, device=dev)
+    wt = torch.empty(R, topk, dtype=torch.float32, device=dev)
+    sc = torch.empty(R, E, dtype=torch.float32, device=dev)
+    op = ExpertParallelMoE(w1l, w2l, e0, topk, r_max=8)
     out = torch.empty(R, H, dtype=torch.bfloat16, device=dev)
+    ops.moe_route_into(x, gw, bias, idx, wt, sc, R, H, E, topk, 1.0)
+    op(z, idx, wt, out=out)
+    ref = ops.MoeVerify(z, idx, wt, w1, None, w2, None, topk=topk)[0]
+    torch.cuda.synchronize()
+    err = torch.tensor([((out.float() - ref.float()).norm() / ref.float().norm()).item()], device=dev)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    rel_err = float(err.item())
+    U = len(torch.unique(idx))
+    del w1, w2, ref
+    copies = n_copies(w1l.numel() + w2l.numel())
+    w1s, w2s = replicate(w1l, copies), replicate(w2l, copies)
+    del w1l, w2l
+    torch.cuda.empty_cache()
 
-    def one():
-        for _ in range(8):
-            op(z, idx, wt, out=out)
+    def one_pass():
+        for c in range(copies):
+            ops.moe_route_into(x, gw, bias, idx, wt, sc, R, H, E, topk, 1.0)
+            op(z, idx, wt, out=out, w1=w1s[c], w2=w2s[c])
 
-    g = capture(one)
-    ms = max_over_ranks(time_graph(g, steps, warmup, world), world)
-    del g
+    gr = capture(one_pass)
+    ms = max_over_ranks(time_graph(gr, steps, warmup, world), world)
+    del gr
     torch.cuda.synchronize()
     rc, _ = _lib.device_status()
     op.close()
-    us = ms * 1e3 / (steps * 8)
-    U = len(torch.unique(idx))
-    wbytes = U * (I * (H // 256) * 66 + H * (I // 256) * 66)
+    del w1s, w2s
+    torch.cuda.empty_cache()
+    us = ms * 1e3 / (steps * copies)
+    wbytes = E * H * 4 + E * 4 + U * (I * (H // 256) * 66 + H * (I // 256) * 66)
     return dict(world=world, R=R, us_per_call=us, gbs=wbytes / (us * 1e-6) / 1e9, unique_experts=U,
-                experts_per_gpu=el, device_status=rc, note="L2-resident weights (one expert copy per GPU)")
+                experts_per_gpu=el, copies=copies, device_status=rc,
+                parity="ok" if rel_err <= 5e-3 else f"rel-L2 {rel_err:.2e} > 5e-3", rel_l2_vs_single_gpu=rel_err,
+                note="router inside every call; expert copies rotated (> 2x L2 per GPU)")
 
 
 def bench_embed(R, steps, warmup, dev, V=131072, K=4096):
@@ -780,6 +967,12 @@ def main():
     if args.cpu_table:
         cpu_table()
         return
+    if args.profile_case:
+        import gguf_onnx_ops_b200
+
+        gguf_onnx_ops_b200.load()
+        profile_case(args)
+        return
     import torch
 
     hd = HEADLINE
@@ -787,24 +980,30 @@ def main():
         rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", args.gpus))
     else:
         rank, world, local = dist_setup(args.gpus)
-    metric = "weight-stream HBM GB/s per GEMV/MoE op call (Q4Gemv iq2=3, IQ2_XXS, R=1, K=4096, N=14336)"
+    metric = "weight-stream HBM GB/s per GEMV/MoE op call"
     config = {"workload": "BASELINE config 1: Q4Gemv iq2=3 (IQ2_XXS) R=1 K=4096 N=14336",
-              "parallelism": "replicas" if world > 1 else "single", "global_batch": hd["R"] * world,
+              "parallelism": "single", "global_batch": hd["R"],
               "l2": "distinct weight copies per pass, total > 2x L2 (126 MB)"}
 
     if args.impl == "reference":
         if rank != 0:
             return
+        # the reference's CPU path on this arm's workload: config 1 at N = 1, config 4's LM head (the
+        # sharded headline of the multi-GPU line) at N > 1
+        op, R, N, K = (hd["op"], hd["R"], hd["N"], hd["K"]) if world == 1 else ("q8_0", 1, 131072, 4096)
+        if world > 1:
+            config = {"workload": "BASELINE config 4: Q8Gemv gguf=1 R=1 K=4096 N=131072 (LM head)",
+                      "parallelism": "host CPU", "global_batch": 1}
         runs = []
         for i in range(args.warmup + args.steps):
-            cb = cpu_baseline(hd["op"], hd["R"], hd["N"], hd["K"], budget_s=max(1.0, 120.0 / (args.warmup + args.steps)))
+            cb = cpu_baseline(op, R, N, K, budget_s=max(1.0, 120.0 / (args.warmup + args.steps)))
             if i >= args.warmup:
                 runs.append(cb)
         v = statistics.median(r["value"] for r in runs)
         line = {"impl": "reference", "metric": metric, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": statistics.median(r["seconds"] for r in runs) * 1e3,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": config,
+                "higher_is_better": True, "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "config": config,
                 "cpu_baseline": {"value": v, "unit": "GB/s", "cores": runs[0]["cores"], "kind": "port",
                                  "sample": runs[0]["sample"]},
                 "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -815,6 +1014,9 @@ def main():
     import gguf_onnx_ops_b200
 
     gguf_onnx_ops_b200.load()
+    if world > 1:
+        sharded_main(args, rank, world, local, dev, metric)
+        return
     sampler = ClockSampler(local)
     res, state = bench_gemv(hd["op"], hd["R"], hd["N"], hd["K"], args.steps, args.warmup, dev, world=world,
                             sampler=sampler)
@@ -828,65 +1030,112 @@ def main():
                          "frac": res["gbs"] / peak, "traffic": traffic_per_launch(), "peak_source": src,
                          "algorithmic_bytes_per_launch": res["weight_bytes"]},
             "gpu_launches": res["calls"], "clocks": sampler.report()}
-    if rank == 0:
-        line["e2e"] = bench_e2e_gemv(hd["op"], hd["R"], hd["N"], hd["K"], args.steps, args.warmup, dev, state)
+    line["e2e"] = bench_e2e_gemv(hd["op"], hd["R"], hd["N"], hd["K"], args.steps, args.warmup, dev, state)
     del state
     torch.cuda.empty_cache()
-    if rank == 0 and world == 1:
-        line["cpu_baseline"] = cpu_baseline(hd["op"], hd["R"], hd["N"], hd["K"])
-        if not args.quick:
-            cfgs = {}
-            for name, op, R, N, K in ([("C0", "q8_0", 1, 4096, 4096)] +
-                                      [("C1", "iq2_xxs", R, 14336, 4096) for R in (1, 4, 8)] +
-                                      [("C2", "nvfp4", R, 13824, 5120) for R in (1, 8, 16)] +
-                                      [("C4", "q8_0", R, 131072, 4096) for R in (1, 4, 8, 16)]):
-                r, st = bench_gemv(op, R, N, K, max(5, args.steps // 2), args.warmup, dev)
-                del st
-                torch.cuda.empty_cache()
-                cfgs[f"{name}_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()
-                                        if k in ("us_per_call", "gbs", "weight_bytes", "copies", "rounds")}
-                cfgs[f"{name}_R{R}"]["frac_of_peak"] = round(r["gbs"] / peak, 4)
-            for R in (1, 4, 8):
-                r = bench_moe(R, max(5, args.steps // 2), args.warmup, dev)
-                r["frac_of_peak"] = r["gbs"] / peak
-                cfgs[f"C3_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()}
-                torch.cuda.empty_cache()
-            line["configs"] = cfgs
-            line["next_rows"] = {f"Q8Embed_R{R}": bench_embed(R, max(5, args.steps // 2), args.warmup, dev)
-                                 for R in (1, 8, 4096)}
+    line["cpu_baseline"] = cpu_baseline(hd["op"], hd["R"], hd["N"], hd["K"])
+    if not args.quick:
+        cfgs = {}
+        for name, op, R, N, K in ([("C0", "q8_0", 1, 4096, 4096)] +
+                                  [("C1", "iq2_xxs", R, 14336, 4096) for R in (1, 4, 8)] +
+                                  [("C2", "nvfp4", R, 13824, 5120) for R in (1, 8, 16)] +
+                                  [("C4", "q8_0", R, 131072, 4096) for R in (1, 4, 8, 16)]):
+            r, st = bench_gemv(op, R, N, K, max(5, args.steps // 2), args.warmup, dev)
+            del st
             torch.cuda.empty_cache()
-            for R in (1, 8, 4096):
-                line["next_rows"][f"SkipRmsNorm_R{R}"] = bench_norm(R, max(5, args.steps // 2), args.warmup, dev)
-            line["next_rows"]["RmsNorm_R1"] = bench_norm(1, max(5, args.steps // 2), args.warmup, dev, skip=False)
+            cfgs[f"{name}_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()
+                                    if k in ("us_per_call", "gbs", "weight_bytes", "copies", "rounds")}
+            cfgs[f"{name}_R{R}"]["frac_of_peak"] = round(r["gbs"] / peak, 4)
+        for R in (1, 4, 8):
+            r = bench_moe(R, max(5, args.steps // 2), args.warmup, dev)
+            r["frac_of_peak"] = r["gbs"] / peak
+            cfgs[f"C3_R{R}"] = {k: round(v, 4) if isinstance(v, float) else v for k, v in r.items()}
             torch.cuda.empty_cache()
-            line["next_rows"]["GGUF_load_C4_lm_head"] = bench_gguf_load(dev)
-            from gguf_onnx_ops_b200 import _lib as L
+        line["configs"] = cfgs
+        line["next_rows"] = next_rows(args, dev)
+    print(json.dumps(line), flush=True)
 
-            st2 = max(5, args.steps // 2)
-            for name, layout, R, N, K in (("Q8Gemv_gguf0", L.GGUF_LAYOUT_Q8_SPLIT, 1, 4096, 4096),
-                                          ("Q4Gemv_iq2_0", L.GGUF_LAYOUT_Q4_SPLIT, 1, 14336, 4096),
-                                          ("Q4Gemv_iq2_1", L.GGUF_LAYOUT_IQ2_CODES, 8, 14336, 4096),
-                                          ("Q4Gemv_iq2_2", L.GGUF_LAYOUT_IQ2_NATIVE, 1, 14336, 4096),
-                                          ("Nvfp4Gemv_gguf0", L.GGUF_LAYOUT_NVFP4_SPLIT, 1, 13824, 5120)):
-                line["next_rows"][f"{name}_R{R}"] = bench_legacy(layout, R, N, K, st2, args.warmup, dev)
-                torch.cuda.empty_cache()
-            line["next_rows"]["SkipRmsNorm_Q4Gemv_C1_R1"] = bench_fused_norm_gemv(st2, args.warmup, dev)
-            torch.cuda.empty_cache()
-            line["next_rows"]["MambaStep_R1"] = bench_mamba(1, st2, args.warmup, dev)
-            line["next_rows"]["MambaVerify_R8"] = bench_mamba(8, st2, args.warmup, dev, verify=True)
-            torch.cuda.empty_cache()
-    if world > 1:  # sharded LM head: the fused row-split GEMV vs GEMV + NCCL all-gather
-        line["sharded"] = {f"C4_R{R}": bench_rowsplit(R, max(5, args.steps // 2), args.warmup, dev, world, rank)
-                           for R in (1, 4)}
-        for R in (1, 8):
-            line["sharded"][f"C3_R{R}_expert_parallel"] = bench_moe_ep(R, max(5, args.steps // 2), args.warmup, dev,
-                                                                        world, rank)
+
+def next_rows(args, dev):
+    """The ops either side of the GEMVs and the legacy layouts, one GPU."""
+    import torch
+
+    from gguf_onnx_ops_b200 import _lib as L
+
+    st2 = max(5, args.steps // 2)
+    out = {f"Q8Embed_R{R}": bench_embed(R, st2, args.warmup, dev) for R in (1, 8, 4096)}
+    torch.cuda.empty_cache()
+    for R in (1, 8, 4096):
+        out[f"SkipRmsNorm_R{R}"] = bench_norm(R, st2, args.warmup, dev)
+    out["RmsNorm_R1"] = bench_norm(1, st2, args.warmup, dev, skip=False)
+    torch.cuda.empty_cache()
+    out["GGUF_load_C4_lm_head"] = bench_gguf_load(dev)
+    for name, layout, R, N, K in (("Q8Gemv_gguf0", L.GGUF_LAYOUT_Q8_SPLIT, 1, 4096, 4096),
+                                  ("Q4Gemv_iq2_0", L.GGUF_LAYOUT_Q4_SPLIT, 1, 14336, 4096),
+                                  ("Q4Gemv_iq2_1", L.GGUF_LAYOUT_IQ2_CODES, 8, 14336, 4096),
+                                  ("Q4Gemv_iq2_2", L.GGUF_LAYOUT_IQ2_NATIVE, 1, 14336, 4096),
+                                  ("Nvfp4Gemv_gguf0", L.GGUF_LAYOUT_NVFP4_SPLIT, 1, 13824, 5120)):
+        out[f"{name}_R{R}"] = bench_legacy(layout, R, N, K, st2, args.warmup, dev)
+        torch.cuda.empty_cache()
+    out["SkipRmsNorm_Q4Gemv_C1_R1"] = bench_fused_norm_gemv(st2, args.warmup, dev)
+    torch.cuda.empty_cache()
+    out["MambaStep_R1"] = bench_mamba(1, st2, args.warmup, dev)
+    out["MambaVerify_R8"] = bench_mamba(8, st2, args.warmup, dev, verify=True)
+    torch.cuda.empty_cache()
+    return out
+
+
+def sharded_main(args, rank, world, local, dev, metric):
+    """N > 1: the headline is the sharded config -- C4's LM head (Q8Gemv gguf=1, R = 1, K = 4096,
+    N = 131072) row-split over the N GPUs with the all-gather fused into the GEMV.
+    value = the whole weight tensor's bytes / the max-over-ranks time per call (strong scaling: the
+    total work is fixed).  The line also carries the same workload on one GPU (measured in this run),
+    C4 at R = 4, 8, 16, the GEMV + NCCL all-gather baseline, the expert-parallel C3 MoE, and config 1
+    as independent replicas; every sharded entry carries its parity check against the single-GPU op."""
+    import torch
+    import torch.distributed as dist
+
+    peak, src = peaks()
+    st2 = max(5, args.steps // 2)
+    sampler = ClockSampler(local)
+    one_gpu_us = bench_single_c4(1, st2, args.warmup, dev)  # every rank on its own GPU; rank 0's figure
+    torch.cuda.empty_cache()
+    barrier(world)
+    r1 = bench_rowsplit(1, args.steps, args.warmup, dev, world, rank, nccl=True, e2e=True, sampler=sampler)
+    total = 131072 * ROW_BYTES["q8_0"](4096)
+    sharded = {"C4_R1": {k: v for k, v in r1.items() if k != "e2e"}}
+    for R in (4, 8, 16):
+        sharded[f"C4_R{R}"] = bench_rowsplit(R, st2, args.warmup, dev, world, rank)
+    for R in (1, 4, 8):
+        sharded[f"C3_R{R}_expert_parallel"] = bench_moe_ep(R, st2, args.warmup, dev, world, rank)
+    rep, st = bench_gemv(HEADLINE["op"], 1, HEADLINE["N"], HEADLINE["K"], st2, args.warmup, dev, world=world)
+    del st
+    torch.cuda.empty_cache()
+    per_gpu_bytes = r1["rows_per_gpu"] * ROW_BYTES["q8_0"](4096)
+    gbs_per_gpu = per_gpu_bytes / (r1["fused_us_per_call"] * 1e-6) / 1e9
+    line = {"metric": metric, "value": r1["fused_gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r1["ms_total"] / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 4: Q8Gemv gguf=1 R=1 K=4096 N=131072 (LM head), row-split "
+                                   f"over {world} GPUs, all-gather of y fused into the GEMV (NVLink peer stores)",
+                       "parallelism": f"rowsplit{world}", "global_batch": 1,
+                       "l2": "distinct weight-shard copies per pass, > 2x L2 per GPU"},
+            "us_per_call": r1["fused_us_per_call"],
+            "one_gpu_same_workload": {"us_per_call": one_gpu_us, "gbs": total / (one_gpu_us * 1e-6) / 1e9,
+                                      "note": "C4 R=1 on one GPU (rank 0's GPU), measured in this run"},
+            "parity": r1["parity"],
+            "roofline": {"bound": "hbm", "achieved": gbs_per_gpu, "peak": peak, "unit": "GB/s",
+                         "frac": gbs_per_gpu / peak, "traffic": None, "peak_source": src,
+                         "algorithmic_bytes_per_launch": per_gpu_bytes,
+                         "note": "per GPU: its shard's bytes / the call time (peer stores and completion included)"},
+            "gpu_launches": r1["calls"], "clocks": sampler.report(), "e2e": r1.get("e2e"),
+            "sharded": sharded,
+            "replicas_C1": {"value": rep["gbs"] * world, "unit": "GB/s", "us_per_call": rep["us_per_call"],
+                            "note": "config 1 (does not shard) as independent replicas, aggregate, max over ranks"}}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -231,8 +231,13 @@ int parse(GgufFile* f) {
     ti.type = static_cast<int32_t>(type);
     ti.block_elems = ts->block;
     ti.block_bytes = ts->bytes;
+    // the byte size must fit int64 (a malformed file can claim up to 2^62 elements of a type with
+    // several bytes per element); anything larger than the file is rejected later anyway
+    int64_t nbytes = 0;
+    if (__builtin_mul_overflow(elems / ts->block, static_cast<int64_t>(ts->bytes), &nbytes))
+      return set_error(GGUF_ERR_INVALID_ARGUMENT, "GGUF: tensor " + name + " is too large");
     ti.row_bytes = ti.dims[0] / ts->block * ts->bytes;
-    ti.nbytes = elems / ts->block * ts->bytes;
+    ti.nbytes = nbytes;
     rel[i] = off;
     if (!f->tensor_index.emplace(name, static_cast<int64_t>(f->tensors.size())).second)
       return set_error(GGUF_ERR_INVALID_ARGUMENT, "GGUF: duplicate tensor name " + name);

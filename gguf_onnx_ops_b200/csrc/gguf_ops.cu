@@ -981,19 +981,29 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
 }  // namespace
 }  // namespace gguf_b200
 
+// Validation of MoeVerify iq2=3's caller-visible tensors and sizes (shared by the caller-scratch and
+// the library-scratch entry points; runs before any device call).
+static int moe_verify_check(const void* z, const int32_t* idx, const float* weights, const void* fc1_w,
+                            const void* fc2_w, const void* out, int64_t R, int64_t E, int64_t I, int64_t topk) {
+  if (!z || !idx || !weights || !fc1_w || !fc2_w || !out) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: null tensor pointer");
+  if (R < 1 || R > 8 || topk < 1 || R * topk > 128)
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: rows must be in [1,8] and rows*topk <= 128");
+  if (I <= 0 || I % 256 != 0 || I > (1 << 20) || E < 1 || E > (1 << 20))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size alignment mismatch (iq2=3 needs I % 256 == 0)");
+  if (!aligned(fc1_w, 16) || !aligned(fc2_w, 16) || !aligned(z, 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: tensors must be 16-byte aligned");
+  return GGUF_OK;
+}
+
 extern "C" int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w,
                             void* out, void* h, float* part, int32_t* meta, int64_t R, int64_t E, int64_t I, int64_t topk,
                             void* stream) {
   t_last_error.clear();
   constexpr int H = 1024;
-  if (!z || !idx || !weights || !fc1_w || !fc2_w || !out || !h || !part || !meta)
-    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: null tensor pointer");
+  if (!h || !part || !meta) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: null tensor pointer");
+  if (int rc0 = moe_verify_check(z, idx, weights, fc1_w, fc2_w, out, R, E, I, topk)) return rc0;
   const int64_t P = R * topk;
-  if (R < 1 || R > 8 || topk < 1 || P > 128) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: rows must be in [1,8] and rows*topk <= 128");
-  if (I <= 0 || I % 256 != 0 || I > (1 << 20) || E < 1 || E > (1 << 20))
-    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size alignment mismatch (iq2=3 needs I % 256 == 0)");
-  if (!aligned(fc1_w, 16) || !aligned(fc2_w, 16) || !aligned(z, 16) || !aligned(h, 16) || !aligned(part, 16))
-    return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: tensors must be 16-byte aligned");
+  if (!aligned(h, 16) || !aligned(part, 16)) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: tensors must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (g_fast.load())
     return run_moe_fused(z, idx, weights, fc1_w, fc2_w, out, h, part, meta, (int)R, (int)E, (int)I, (int)topk, s);
@@ -1191,27 +1201,16 @@ constexpr size_t kNoAllocMetaBytes = ((1 + 9 * kNoAllocMaxPairs) * 4 + 255) & ~s
 static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[kNoAllocHBytes + kNoAllocPartBytes + kNoAllocMetaBytes];
 
 namespace {
-constexpr int kMaxDevices = 64;
-std::atomic<void*> g_noalloc_ptr[kMaxDevices];
-std::mutex g_noalloc_mu;
-
-// Address of this device's copy of the scratch array, looked up once per device with that device
-// current (cudaGetSymbolAddress, which may load the module on first use).
+// Address of the scratch array in the module instance of the current context.  Looked up on every
+// call: the address belongs to a context (a driver-API context made current by the caller loads its
+// own copy of the module, and cudaDeviceReset destroys the primary context's), so caching it per
+// device ordinal could hand a kernel an address of another context.  After the first call in a
+// context the lookup only reads the runtime's symbol table; the first call may load the module, so
+// a caller that captures CUDA graphs makes one call on each device before it starts capturing.
 int noalloc_scratch(void** ptr) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail("cudaGetDevice", e);
-  if (dev < 0 || dev >= kMaxDevices) return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify (no-alloc): device ordinal out of range");
-  void* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
-    if (p == nullptr) {
-      e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
-      if (e != cudaSuccess) return cuda_fail("MoeVerify (no-alloc) scratch address", e);
-      g_noalloc_ptr[dev].store(p, std::memory_order_release);
-    }
-  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail("MoeVerify (no-alloc) scratch address", e);
   *ptr = p;
   return GGUF_OK;
 }
@@ -1224,9 +1223,11 @@ int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* idx, const flo
   if (R < 1 || topk < 1 || R * topk > kNoAllocMaxPairs || I > kNoAllocMaxInter)
     return fail(GGUF_ERR_INVALID_ARGUMENT,
                 "MoeVerify (no-alloc): needs rows*topk <= 128 and I <= 4096 (the size of the library-owned scratch)");
+  // every argument check of the caller-scratch entry point runs before the scratch lookup, so an
+  // invalid call fails with GGUF_ERR_INVALID_ARGUMENT and touches no device state
+  if (const int rc = moe_verify_check(z, idx, weights, fc1_w, fc2_w, out, R, E, I, topk)) return rc;
   void* base = nullptr;
-  const int rc = noalloc_scratch(&base);
-  if (rc != GGUF_OK) return rc;
+  if (const int rc = noalloc_scratch(&base)) return rc;
   uint8_t* b = static_cast<uint8_t*>(base);
   return gguf_moe_verify_iq2_xxs(z, idx, weights, fc1_w, fc2_w, out, b, reinterpret_cast<float*>(b + kNoAllocHBytes),
                                  reinterpret_cast<int32_t*>(b + kNoAllocHBytes + kNoAllocPartBytes), R, E, I, topk,

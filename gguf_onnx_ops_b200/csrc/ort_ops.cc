@@ -50,6 +50,22 @@ int64_t opt_int(const OrtKernelInfo* info, const char* name, int64_t dflt) {
   }
   return v;
 }
+// A required attribute (the reference reads it with KernelInfo::GetAttribute, which throws when the
+// node lacks it, and CreateKernelV2 turns that into ORT_INVALID_ARGUMENT: src/bolt_ops.cu:1873).
+bool has_int(const OrtKernelInfo* info, const char* name) {
+  int64_t v = 0;
+  OrtStatus* st = Ort::GetApi().KernelInfoGetAttribute_int64(info, name, &v);
+  if (st == nullptr) return true;
+  Ort::GetApi().ReleaseStatus(st);
+  return false;
+}
+bool has_float(const OrtKernelInfo* info, const char* name) {
+  float v = 0.f;
+  OrtStatus* st = Ort::GetApi().KernelInfoGetAttribute_float(info, name, &v);
+  if (st == nullptr) return true;
+  Ort::GetApi().ReleaseStatus(st);
+  return false;
+}
 float opt_float(const OrtKernelInfo* info, const char* name, float dflt) {
   float v = dflt;
   OrtStatus* st = Ort::GetApi().KernelInfoGetAttribute_float(info, name, &v);
@@ -68,6 +84,8 @@ struct OpDesc {
   std::vector<int> optional_in;  // indices of optional inputs
   ComputeFn compute;             // nullptr: op outside the GGUF decode path
   std::vector<int> optional_out = {};  // indices of optional outputs
+  std::vector<const char*> req_int = {};    // attributes whose absence fails kernel creation
+  std::vector<const char*> req_float = {};
 };
 
 // ---- helpers over the C++ API ----
@@ -304,20 +322,27 @@ void mamba(Ort::KernelContext& c, const Attrs& a) {
                         a.head_dim, a.d_state, a.n_groups, a.epsilon, a.time_step_min, stream(c)));
 }
 
-// Names, signatures and optional inputs of the reference's 15 ops (src/bolt_ops.cu:1886-2061).
+// Required attributes of the Mamba ops (src/bolt_ops.cu:311-316).
+const std::vector<const char*> kMambaInt = {"heads", "head_dim", "d_state", "n_groups"};
+const std::vector<const char*> kMambaFloat = {"epsilon", "time_step_min"};
+
+// Names, signatures, optional inputs and required attributes of the reference's 15 ops
+// (src/bolt_ops.cu:1886-2061; attributes read with GetAttribute at :311-316, :519-520, :669, :1333;
+// gguf / iq2 / RmsNorm's epsilon are optional there, :1319-1326, :1819-1823).
 const std::vector<OpDesc>& op_table() {
   static const std::vector<OpDesc> t = {
-      {"MambaStep", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {}, mamba<false, false>},
+      {"MambaStep", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {}, mamba<false, false>,
+       {}, kMambaInt, kMambaFloat},
       {"MambaStepGGUF", {kBF, kBF, kF32, kF32, kF32, kF32, kF32, kF32, kF32}, {kBF, kBF, kF32, kBF, kF32}, {},
-       mamba<false, true>},
+       mamba<false, true>, {}, kMambaInt, kMambaFloat},
       {"MambaVerify", {kBF, kBF, kF32, kBF, kBF, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {},
-       mamba<true, false>},
+       mamba<true, false>, {}, kMambaInt, kMambaFloat},
       {"MambaVerifyGGUF", {kBF, kBF, kF32, kF32, kF32, kF32, kF32, kF32, kF32, kI32}, {kBF, kBF, kF32, kBF, kF32}, {},
-       mamba<true, true>},
-      {"MoeRoute", {kBF, kBF, kF32}, {kI32, kF32, kF32}, {}, route_bf16},
-      {"MoeRouteGGUF", {kBF, kF32, kF32}, {kI32, kF32, kF32}, {}, route_gguf},
-      {"MoeDecode", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32}, {}, moe_decode},
-      {"MoeVerify", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32, kI32}, {4, 6}, moe_verify},
+       mamba<true, true>, {}, kMambaInt, kMambaFloat},
+      {"MoeRoute", {kBF, kBF, kF32}, {kI32, kF32, kF32}, {}, route_bf16, {}, {"topk"}, {"scale"}},
+      {"MoeRouteGGUF", {kBF, kF32, kF32}, {kI32, kF32, kF32}, {}, route_gguf, {}, {"topk"}, {"scale"}},
+      {"MoeDecode", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32}, {}, moe_decode, {}, {"topk"}},
+      {"MoeVerify", {kBF, kI32, kF32, kU8, kBF, kU8, kBF}, {kBF, kBF, kF32, kI32}, {4, 6}, moe_verify, {}, {"topk"}},
       {"Relu2", {kBF}, {kBF}, {}, relu2},
       {"Nvfp4Gemv", {kBF, kU8, kU8, kF32}, {kBF}, {2}, fp4_gemv},
       {"Q8Gemv", {kBF, kU8, kBF}, {kBF}, {2}, q8_gemv},
@@ -369,6 +394,13 @@ struct GgufOp : Ort::CustomOpBase<GgufOp, GgufKernel, true> {
   }
   OrtStatus* CreateKernelV2(const OrtApi& api, const OrtKernelInfo* info, void** kernel) const noexcept {
     try {
+      for (const char* n : d->req_int)
+        if (!has_int(info, n)) throw std::invalid_argument(std::string(d->name) + ": missing required attribute '" + n + "'");
+      for (const char* n : d->req_float)
+        if (!has_float(info, n)) throw std::invalid_argument(std::string(d->name) + ": missing required attribute '" + n + "'");
+      if (std::string(d->name).rfind("Mamba", 0) == 0 &&
+          (opt_int(info, "head_dim", 0) != 64 || opt_int(info, "d_state", 0) != 128))
+        throw std::invalid_argument("MambaStep: only head_dim=64, d_state=128 are implemented");
       auto* k = new GgufKernel{d, {}};
       k->a.gguf = opt_int(info, "gguf", 0);
       k->a.iq2 = opt_int(info, "iq2", 0);
@@ -392,8 +424,11 @@ struct GgufOp : Ort::CustomOpBase<GgufOp, GgufKernel, true> {
 
 extern "C" __attribute__((visibility("default"))) OrtStatus* ORT_API_CALL RegisterCustomOps(OrtSessionOptions* options,
                                                                                           const OrtApiBase* api_base) {
-  const OrtApi* api = api_base->GetApi(ORT_API_VERSION);
-  if (api == nullptr) return api_base->GetApi(1)->CreateStatus(ORT_FAIL, "Unsupported ORT API version");
+  // API version 22 first (the version the reference library is built against), then the headers'
+  // own version (src/bolt_ops.cu:2066-2068)
+  const OrtApi* api = api_base->GetApi(22);
+  if (api == nullptr) api = api_base->GetApi(ORT_API_VERSION);
+  if (api == nullptr) return api_base->GetApi(1)->CreateStatus(ORT_FAIL, "Unsupported ORT API");
   Ort::InitApi(api);
   try {
     static std::vector<GgufOp> ops;

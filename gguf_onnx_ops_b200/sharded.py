@@ -181,8 +181,14 @@ class ExpertParallelMoE:
         self._pr.world, self._pr.rank, self._pr.r_max = self.world, self.rank, r_max
 
     def __call__(self, z: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None = None,
-                 stream=None) -> torch.Tensor:
+                 stream=None, w1: torch.Tensor | None = None, w2: torch.Tensor | None = None) -> torch.Tensor:
+        """out = MoeVerify over the whole group; `w1` / `w2` optionally replace this rank's expert
+        tensors (same shapes and type, e.g. another copy of the same experts)."""
         R = z.shape[0]
+        w1 = self.w1 if w1 is None else w1
+        w2 = self.w2 if w2 is None else w2
+        if w1.shape != self.w1.shape or w2.shape != self.w2.shape or w1.dtype != torch.uint8 or w2.dtype != torch.uint8:
+            raise ValueError("w1 / w2 must have the shapes of this rank's expert tensors")
         if z.dtype != torch.bfloat16 or z.shape[1] != self.H or not 1 <= R <= self.r_max:
             raise ValueError("z must be bf16 [R, 1024] with R <= r_max")
         if idx.dtype != torch.int32 or weights.dtype != torch.float32 or idx.shape != (R, self.topk):
@@ -190,7 +196,7 @@ class ExpertParallelMoE:
         out = torch.empty(R, self.H, dtype=torch.bfloat16, device=z.device) if out is None else out
         s = (stream or torch.cuda.current_stream()).cuda_stream
         p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        check(load().gguf_moe_verify_iq2_xxs_ep(p(z), p(idx), p(weights), p(self.w1), p(self.w2), p(out), p(self.h),
+        check(load().gguf_moe_verify_iq2_xxs_ep(p(z), p(idx), p(weights), p(w1), p(w2), p(out), p(self.h),
                                                 p(self.part), p(self.meta), ctypes.byref(self._pr), R, self.E, self.offset,
                                                 self.I, self.topk, ctypes.c_void_p(s)))
         return out

@@ -210,8 +210,10 @@ GGUF_OPS_API int gguf_moe_verify_iq2_xxs(const void* z, const int32_t* idx, cons
  * CUDA allocator, or a decode loop that must not enter an allocator.
  * Limits: rows*topk <= 128 and I <= 4096 (larger sizes return GGUF_ERR_INVALID_ARGUMENT); the other
  * contract terms of gguf_moe_verify_iq2_xxs apply.
- * The first call on each device looks the array up (cudaGetSymbolAddress, with that device current)
- * and should come before any stream capture.  The array is shared by every call on a device: calls
+ * Every call looks the array's address up in the current context (cudaGetSymbolAddress; a driver-API
+ * context made current by the caller has its own copy of the array).  The first call in a context
+ * may load the library's device code there, so make it before any stream capture.  Argument errors
+ * are reported before that lookup.  The array is shared by every call on a device: calls
  * whose executions may overlap (different streams, unordered threads) race on it and must be ordered
  * by the caller.  Nothing in the array needs to start at zero; the per-call counters are cleared on
  * the stream by each call.

@@ -110,6 +110,8 @@ def kv_u32(key, v):
     (dict(tensors=[(b"t", [48], 8, 0)], data=b"\0" * 64), "whole blocks"),
     (dict(tensors=[(b"t", [64], 8, 0)], data=b"\0" * 67), "beyond the end"),
     (dict(tensors=[(b"t", [32], 8, 1 << 62)], data=b"\0" * 64), "beyond the end"),
+    # 2^62 F32 elements: 2^64 bytes would wrap int64 to a small size that fits the file
+    (dict(tensors=[(b"t", [1 << 31, 1 << 31], 0, 0)], data=b"\0" * 64), "too large"),
 ])
 def test_malformed_files_rejected(tmp_path, case, msg):
     q = tmp_path / "bad.gguf"

@@ -126,6 +126,42 @@ def test_lm_head_shape_r16(cuda):
     assert rel(y[:, rows], oracle_y("q8_0", x, w, extra, rows)) < TOL
 
 
+@pytest.fixture(scope="module")
+def c4_weights():
+    """BASELINE config 4's LM head (Q8_0, N = 131072, K = 4096), built once for the R sweep."""
+    _, w, extra = I.gemv_case("q8_0", 1, 131072, 4096, seed=0)
+    return w, extra
+
+
+@pytest.mark.parametrize("R", [1, 4, 8])
+def test_lm_head_config_c4(cuda, c4_weights, R):
+    """Config C4 at full size (N = 131072, K = 4096) for R = 1, 4, 8: the oracle on a 512-row sample,
+    every row against the bit-exact device dequantisation followed by an fp32 matmul."""
+    w, extra = c4_weights
+    x = I.bf16_normal(I.rng(40 + R), (R, 4096))
+    y = run_gemv("q8_0", x, w, extra, cuda)
+    rows = np.sort(I.rng(R).choice(131072, size=512, replace=False))
+    assert rel(y[:, rows], oracle_y("q8_0", x, w, extra, rows)) < TOL
+    wt = u8_t(w, cuda)
+    deq = ops.dequantize(wt, _lib.GGUF_TYPE_Q8_0, 4096)
+    full = np_f32(bf16_t(x, cuda).float() @ deq.T)
+    del deq, wt
+    assert rel(y, full) < TOL
+    assert_device_ok()
+
+
+# The reference harness's own IQ2_XXS GEMV shapes (tests/test_bolt_ops.py:478, test_q4_iq2_native):
+# K = 5376 is 21 super-blocks, an odd count between the K-specialised kernels (2048 / 4096 / 5120).
+@pytest.mark.parametrize("R,N,K", [(8, 5376, 4096), (1, 4096, 5376), (3, 1024, 4096), (8, 4096, 5376)])
+def test_harness_iq2_shapes(cuda, R, N, K):
+    g = I.rng(21 + R + N + K)
+    w = I.iq2_test_blocks(g, (N,), K)  # the harness's block builder (tests/test_bolt_ops.py:210-215)
+    x = I.bf16_normal(g, (R, K))
+    y = run_gemv("iq2_xxs", x, w, {}, cuda)
+    assert rel(y, oracle_y("iq2_xxs", x, w, {})) < TOL
+    assert_device_ok()
+
+
 @pytest.mark.parametrize("op", ["q8_0", "iq2_xxs", "nvfp4"])
 def test_chained_calls_with_pdl(cuda, op):
     """y of call i is x of call i+1 (N == K): programmatic dependent launch must still order the

@@ -42,6 +42,8 @@ def test_route_golden(cuda, golden, name):
     x, gw, b, topk, scale = route_inputs(name)
     idx, w = check_route(x, gw, b, topk, scale, cuda)
     _, _, _, near = O.route_ref(x, gw, b, topk, scale)
+    if name == "c3":  # config C3's seed has no near-tie row, so every index is compared bit for bit
+        assert not near.any()
     assert np.array_equal(idx[~near], d[f"{name}_idx"][~near])
     assert rel(w, d[f"{name}_w"]) < 1e-5
 
@@ -113,8 +115,25 @@ def test_moe_golden(cuda, golden):
 def test_moe_config_c3_routed(cuda, R):
     """Config C3 end to end: MoeRouteGGUF -> MoeVerify iq2=3, E=128, I=1792, topk=6."""
     c = I.moe_case(R)
+    _, _, _, near = O.route_ref(c["x"], c["gate_w"], c["bias"], 6, 1.0)
+    assert not near.any(), "no near-tie rows on the C3 seeds: the top-k indices are compared bit for bit"
     idx, w = check_route(c["x"], c["gate_w"], c["bias"], 6, 1.0, cuda)
     check_moe(c["z"], idx, w.astype(np.float32), c["w1"], c["w2"], 6, cuda)
+
+
+# The reference harness's own MoeVerify iq2=3 shapes (tests/test_bolt_ops.py:480-481,
+# test_moe_iq2_native): topk 9, or 6 for the 12-expert case where every expert is shared by many rows.
+@pytest.mark.parametrize("R,E,Idim", [(8, 304, 2304), (1, 240, 1536), (5, 496, 2560), (8, 12, 2048)])
+def test_moe_harness_shapes(cuda, R, E, Idim):
+    topk = 9 if E > 12 else 6
+    g = I.rng(22 + R * 7 + E)
+    z = I.bf16_normal(g, (R, 1024), 0.5)
+    idx = np.stack([g.permutation(E)[:topk] for _ in range(R)]).astype(np.int32)
+    w = g.random((R, topk)).astype(np.float32)
+    w1 = I.iq2_test_blocks(g, (E, Idim), 1024)  # the harness's block builder (tests/test_bolt_ops.py:210-215)
+    w2 = I.iq2_test_blocks(g, (E, 1024), Idim)
+    check_moe(z, idx, w, w1, w2, topk, cuda)
+    assert_status_clean()
 
 
 @pytest.mark.parametrize("R,E,Idim,topk", [(8, 12, 2048, 6), (8, 16, 256, 16), (1, 240, 1536, 9), (3, 5, 512, 5),

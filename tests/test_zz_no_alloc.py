@@ -1,9 +1,13 @@
 """gguf_moe_verify_iq2_xxs_noalloc (library-owned scratch) against gguf_moe_verify_iq2_xxs.
 
-Collected last (file name) so that it also runs after every other test has used the library on
-the same device.  Both entry points are called through the C ABI; the no-alloc one twice in a row,
-each result within the MoeVerify tolerance (rel-L2 <= 5e-3) of the caller-scratch entry point (whose
-parity with the oracle is covered by test_gpu_moe.py).
+Some callers cannot allocate device memory for MoeVerify's scratch outputs (h, part, meta): a
+cgo / JNI / FFI host that holds only the model's buffers and has no CUDA allocator, or a decode loop
+that must not enter an allocator.  The no-alloc entry point keeps that scratch in a device array of
+the library.  Collected last (file name) so that it also runs after every other test has used the
+library on the same device.  Both entry points are called through the C ABI; the no-alloc one twice
+in a row.  Both run the same deterministic kernels, so each no-alloc result must equal the
+caller-scratch result bit for bit; the caller-scratch result is also checked against the oracle
+(rel-L2 <= 5e-3, the MoeVerify tolerance).
 """
 
 import ctypes
@@ -12,6 +16,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from gguf_onnx_ops_b200 import _lib
 from oracle import inputs as I
 from tests.util import bf16_t, rel, u8_t
@@ -29,6 +34,10 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(lib):
     rc = lib.gguf_moe_verify_iq2_xxs_noalloc(None, None, None, None, None, None, 8, 128, 1792, 17, None)
     assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT
     assert b"rows*topk <= 128" in lib.gguf_last_error()
+    # the caller-visible argument checks run before the scratch lookup (no device call without a GPU)
+    rc = lib.gguf_moe_verify_iq2_xxs_noalloc(None, None, None, None, None, None, 2, 128, 1792, 6, None)
+    assert rc == _lib.GGUF_ERR_INVALID_ARGUMENT
+    assert b"null tensor pointer" in lib.gguf_last_error()
 
 
 @pytest.mark.gpu
@@ -66,7 +75,11 @@ def test_noalloc_matches_caller_scratch(cuda, lib, R, E, Iw, topk):
 
     ref = out_ref.float().cpu().numpy()
     assert np.isfinite(ref).all() and np.abs(ref).max() > 0
+    ref_bits = out_ref.cpu().view(torch.int16).numpy()
     for o in outs:
-        got = o.float().cpu().numpy()
-        assert np.isfinite(got).all()
-        assert rel(got, ref) < 5e-3
+        assert np.array_equal(o.cpu().view(torch.int16).numpy(), ref_bits)
+    used = sorted(set(idx.reshape(-1).tolist()))
+    d1 = {e: O.dequant_iq2_xxs(w1[e]) for e in used}
+    d2 = {e: O.dequant_iq2_xxs(w2[e]) for e in used}
+    oref, _, _ = O.moe_ref(z, idx, wt, d1, d2)
+    assert rel(ref, O.bf16_round(oref)) < 5e-3
