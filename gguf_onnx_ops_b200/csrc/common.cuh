@@ -154,6 +154,7 @@ struct PeerOut {
   uint32_t* flags[kMaxPeers];  // flag array of GPU p: [kMaxPeers], slot q = last epoch GPU q finished
   uint32_t* state;             // this GPU: [0] = completed epochs, [1] = CTAs of the running launch finished
   int npeer, rank, ld, row0;
+  int vec;                     // 1: every y[p] 16-byte aligned, ld and row0 multiples of 8 (16-byte stores)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -170,6 +171,28 @@ __device__ __forceinline__ void peer_store(const PeerOut& po, int col, int row, 
   const int64_t off = static_cast<int64_t>(col) * po.ld + po.row0 + row;
 #pragma unroll 1
   for (int p = 0; p < po.npeer; ++p) po.y[p][off] = v;
+}
+
+// The 16 y values of one activation row of a full 16-row tile (lane i of a 16-lane half-warp holds
+// row i's value; both halves of the warp may hold different activation rows) into every GPU's y with
+// 16-byte stores: a shuffle butterfly packs 8 consecutive values into lanes 0 and 8 of each half, which
+// then store to each peer.  All 32 lanes call it (`v` of the lanes that hold no value is ignored when
+// `ok` is false for that half); xr / row of the half's lane 0.
+__device__ __forceinline__ void peer_store_tile16(const PeerOut& po, bf16 v, bool ok, int xr, int row) {
+  const int lane = threadIdx.x & 31, li = lane & 15;
+  uint32_t w = static_cast<uint32_t>(__bfloat16_as_ushort(v));
+  w |= __shfl_down_sync(0xffffffffu, w, 1) << 16;  // even lanes: values i, i + 1
+  const uint32_t w1 = __shfl_down_sync(0xffffffffu, w, 2);
+  const uint32_t w2 = __shfl_down_sync(0xffffffffu, w, 4), w3 = __shfl_down_sync(0xffffffffu, w1, 4);
+  // lanes 0 and 8 of each half: (w, w1, w2, w3) = values li .. li + 7
+  const int src_xr = __shfl_sync(0xffffffffu, xr, lane & 16), src_row = __shfl_sync(0xffffffffu, row, lane & 16);
+  const bool src_ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, lane & 16) != 0;
+  if (src_ok && (li & 7) == 0) {
+    const int64_t off = static_cast<int64_t>(src_xr) * po.ld + po.row0 + src_row + li;
+    const uint4 q = make_uint4(w, w1, w2, w3);
+#pragma unroll 1
+    for (int p = 0; p < po.npeer; ++p) *reinterpret_cast<uint4*>(po.y[p] + off) = q;
+  }
 }
 
 // Called by one thread per CTA after the CTA's last peer_store (and a barrier over the threads that

@@ -960,6 +960,29 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     if ((rc = ensure_smem(moe_r1_i8_kernel, smem1, done1))) return rc;
     e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+  } else if (g_fast.load() == 1) {
+    // 2..8 rows: the integer decode shared by every pair of an expert (moe_pairs_kernel)
+    MoeFusedArgs b = a;
+    const int maxr = R <= 2 ? 2 : (R <= 4 ? 4 : 8);
+    b.off_stage = kI8Lut;
+    b.off_red = b.off_stage + kMoePTeams * 2 * a.stage_bytes;
+    b.off_bar = b.off_red + kMoePTeams * 2 * kMoeTeamWarps * maxr * 16 * 4;
+    b.off_grp = b.off_bar + kMoePTeams * 4 * 8;
+    b.off_zf = (b.off_grp + grp + 127) & ~127;
+    const size_t smem2 = b.off_zf + static_cast<size_t>(R) * (H / 256) * kZFragBytes;
+    if (smem2 > static_cast<size_t>(kSmemBudgetMax)) {  // large I: the bf16-decode kernel's smaller tables
+      auto kern = moe_fused_kernel;
+      if ((rc = ensure_smem(kern, smem, done))) return rc;
+      e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
+      if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
+      goto finalize;
+    }
+    static std::atomic<uint64_t> d2{0}, d4{0}, d8{0};
+    auto kern = maxr == 2 ? moe_pairs_kernel<2> : (maxr == 4 ? moe_pairs_kernel<4> : moe_pairs_kernel<8>);
+    if ((rc = ensure_smem(kern, smem2, maxr == 2 ? d2 : (maxr == 4 ? d4 : d8)))) return rc;
+    // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
+    e = launch(kern, dim3(sms), dim3(kMoePWarps * 32), smem2, s, b);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   } else {
     auto kern = moe_fused_kernel;
     if ((rc = ensure_smem(kern, smem, done))) return rc;
@@ -967,6 +990,7 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   }
+finalize:
   if (ep) {
     e = launch(moe_finalize_ep_kernel, dim3(1), dim3(kEpThreads), 0, s, static_cast<const float*>(part), weights, idx, topk,
                H, E, expert_offset, R, static_cast<bf16*>(out), *ep);
@@ -1256,6 +1280,8 @@ int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float
   po.rank = out->rank;
   po.ld = static_cast<int>(out->n_total);
   po.row0 = static_cast<int>(out->row0);
+  po.vec = out->n_total % 8 == 0 && out->row0 % 8 == 0;
+  for (int p = 0; p < out->world; ++p) po.vec = po.vec && aligned(out->y[p], 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (type) {
     case GGUF_TYPE_Q8_0:

@@ -43,6 +43,7 @@ struct MoeFusedArgs {
   int stage_bytes;    // one 16-row tile of either matrix (+ pad)
   int expert_offset;  // expert parallelism: global id of local expert 0 (idx holds global ids)
   int off_stage, off_red, off_bar, off_grp;
+  int off_zf;         // moe_pairs_kernel: the z fragments of every activation row (kZFragBytes per row and slice)
 };
 
 constexpr int kMoeDoneWaitSite = 4;
@@ -362,6 +363,284 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
         a.h[static_cast<int64_t>(p) * a.I + tile * 16 + ti] = __float2bfloat16(r * r);
       } else {
         a.part[static_cast<int64_t>(p) * a.H + tile * 16 + ti] = vb;
+      }
+    }
+    if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);
+    if (phase == 1) {  // publish: this tile of h is written (every team thread is past its store)
+      named_bar_sync(bar_id, bar_n);
+      if (leader) {
+        __threadfence();
+        atomicAdd(a.done + u, 1);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// The same MoE for 2..8 activation rows (R > 1) on the integer tensor cores.  An expert's 16-row
+// tile is decoded once (exact u8 weights 64 + s*m, the single-row decode of slice_iq2_i8.cuh) and
+// the decoded A fragments are multiplied by every pair the expert has (the rows that selected it):
+// per pair one set of block-diagonal B fragments (the pair's activation slice as two 8-bit limbs per
+// 32-element group; column 2t carries group t, column 2t + 1 group t + 4, so each lane's C cells
+// are the records it decoded) and one epilogue.  Phase 1 takes the B fragments of z from shared
+// memory, where every CTA converts the R rows of z once per launch; phase 2 converts the pair's h
+// slice (read through L2) right before its MMAs.  Work split, staging, phase order and outputs are
+// those of moe_fused_kernel; the team sums its warps' partials per (pair, row) in warp order.
+// ---------------------------------------------------------------------------------------------
+constexpr int kZFragBytes = 8 * 64 + 8 * 8;  // per (row, slice): 8 groups x (8 high + 8 low limb words), xs[8], xoff[8]
+constexpr int kMoePTeams = 4, kMoePWarps = kMoePTeams * kMoeTeamWarps;
+
+// lane (g, t) of a permuted fragment (perm_x_frag): its non-zero B column carries group t (g = 2t,
+// words bh0 / bl0) or group t + 4 (g = 2t + 1, words bh1 / bl1); lanes of quad 0 hold every group's
+// xs / xoff in their (xs0, xoff0) = group t and (xs1, xoff1) = group t + 4
+__device__ __forceinline__ void zfrag_store(const I8XFrag& f, uint8_t* dst) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  uint32_t* w = reinterpret_cast<uint32_t*>(dst);
+  if (g == 2 * t || g == 2 * t + 1) {
+    const bool lo = g == 2 * t;
+    uint32_t* gw = w + (lo ? t : t + 4) * 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      gw[j] = lo ? f.bh0[j] : f.bh1[j];
+      gw[8 + j] = lo ? f.bl0[j] : f.bl1[j];
+    }
+  }
+  if (g == 0) {
+    float* xs = reinterpret_cast<float*>(w + 128);
+    int* xo = reinterpret_cast<int*>(w + 136);
+    xs[t] = f.xs0;
+    xs[t + 4] = f.xs1;
+    xo[t] = f.xoff0;
+    xo[t + 4] = f.xoff1;
+  }
+}
+__device__ __forceinline__ void zfrag_load(const uint8_t* src, I8XFrag& f) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const bool lo = g == 2 * t, hi = g == 2 * t + 1;
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(src);
+  const uint4* gw = reinterpret_cast<const uint4*>(w + (hi ? t + 4 : t) * 16);
+  uint32_t v[16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = (lo || hi) ? gw[q] : make_uint4(0u, 0u, 0u, 0u);
+    v[4 * q] = u.x;
+    v[4 * q + 1] = u.y;
+    v[4 * q + 2] = u.z;
+    v[4 * q + 3] = u.w;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    f.bh0[j] = lo ? v[j] : 0u;
+    f.bl0[j] = lo ? v[8 + j] : 0u;
+    f.bh1[j] = hi ? v[j] : 0u;
+    f.bl1[j] = hi ? v[8 + j] : 0u;
+  }
+  const float* xs = reinterpret_cast<const float*>(w + 128);
+  const int* xo = reinterpret_cast<const int*>(w + 136);
+  f.xs0 = xs[t];
+  f.xs1 = xs[t + 4];
+  f.xoff0 = xo[t];
+  f.xoff1 = xo[t + 4];
+}
+
+// The A fragments of one 16-row x 256-column slice (records rc of rows g, g + 8 x groups t, t + 4):
+// A[e][r][h] = elements 8e + 4h .. 8e + 4h + 3 of record r as 64 + s * m bytes.
+__device__ __forceinline__ void i8_decode(const uint8_t* smem, const uint2 (&rc)[4], uint32_t (&A)[4][4][2]) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lane_off = static_cast<uint32_t>(lane & 15) * 8u, lane_off128 = lane_off | 128u;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint2 X = *reinterpret_cast<const uint2*>(smem + i8_mag_addr(rc[r].x, e, lane_off));
+      const uint2 M = *reinterpret_cast<const uint2*>(smem + i8_sgn_addr(rc[r].y, e, lane_off128));
+      A[e][r][0] = X.x - 2u * (X.x & M.x);
+      A[e][r][1] = X.y - 2u * (X.y & M.y);
+    }
+  }
+}
+// 16 MMAs of decoded A against one pair's permuted fragments and the epilogue (the permuted-column epilogue): the
+// lane's partial sums of weight rows g (acc0) and g + 8 (acc1) over its groups t, t + 4.
+__device__ __forceinline__ void i8_pair_slice(const uint32_t (&A)[4][4][2], const uint2 (&rc)[4], uint32_t dbits,
+                                              const I8XFrag& f, float& acc0, float& acc1) {
+  int ch[4] = {0, 0, 0, 0};
+  int cl[4] = {-f.xoff0, -f.xoff1, -f.xoff0, -f.xoff1};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = 2 * e + h;
+      imma_u8s8(ch, A[e][0][h], A[e][2][h], A[e][1][h], A[e][3][h], f.bh0[j], f.bh1[j]);
+      imma_u8u8(cl, A[e][0][h], A[e][2][h], A[e][1][h], A[e][3][h], f.bl0[j], f.bl1[j]);
+    }
+  }
+  const float v0 = static_cast<float>((ch[0] * 256 + cl[0]) * static_cast<int>((rc[0].y >> 27) | 1u));
+  const float v1 = static_cast<float>((ch[1] * 256 + cl[1]) * static_cast<int>((rc[1].y >> 27) | 1u));
+  const float v2 = static_cast<float>((ch[2] * 256 + cl[2]) * static_cast<int>((rc[2].y >> 27) | 1u));
+  const float v3 = static_cast<float>((ch[3] * 256 + cl[3]) * static_cast<int>((rc[3].y >> 27) | 1u));
+  const float d0 = fp16_bits_to_f32(dbits & 0xFFFFu) * 0.125f, d1 = fp16_bits_to_f32(dbits >> 16) * 0.125f;
+  acc0 = fmaf(v0, f.xs0, v1 * f.xs1) * d0;
+  acc1 = fmaf(v2, f.xs0, v3 * f.xs1) * d1;
+}
+
+template <int kMaxR>
+__global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const MoeFusedArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int team = warp / kMoeTeamWarps, tw = warp % kMoeTeamWarps;
+  const bool leader = tw == 0 && lane == 0;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
+  uint64_t* empty = full + 2;
+  uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
+  float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * kMaxR * 16;  // [2][warps][rows][16]
+  int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
+  uint8_t* zf = smem + a.off_zf;  // [R][H / 256][kZFragBytes]
+
+  if (leader) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kMoeTeamWarps);
+    }
+    fence_mbar_init();
+  }
+  i8_fill_tables<kMoePWarps * 32>(smem, threadIdx.x);
+  pdl_wait();  // idx (router) and z come from earlier kernels
+  moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
+  const int* s_uexp = s_grp + 3 * kMaxPairs;
+  const int* s_pair = s_uexp + kMaxPairs;
+  const int U = s_pair[kMaxPairs * 8];
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < 1 + 9 * a.P; i += blockDim.x) {
+      int v;
+      if (i == 0) v = U;
+      else if (i <= a.P) v = (i - 1 < U) ? s_uexp[i - 1] + a.expert_offset : -1;
+      else v = s_pair[i - 1 - a.P];
+      a.meta[i] = v;
+    }
+  pdl_launch_dependents();
+
+  const int n1 = U * a.T1, n2 = U * a.T2, nitems = n1 + n2;
+  const int teams = kMoePTeams * static_cast<int>(gridDim.x);
+  const int first = team * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
+  auto item_of = [&](int q, int& phase, int& u, int& tile) {
+    if (q < n1) {
+      phase = 1;
+      u = q / a.T1;
+      tile = q % a.T1;
+    } else {
+      phase = 2;
+      u = (q - n1) / a.T2;
+      tile = (q - n1) % a.T2;
+    }
+  };
+  auto fetch = [&](int q, uint32_t k) {
+    int phase, u, tile;
+    item_of(q, phase, u, tile);
+    const int s = static_cast<int>(k & 1u);
+    if (k >= 2u) mbar_wait(&empty[s], ((k >> 1) - 1u) & 1u, kSiteEmptyWait);
+    const int e = s_uexp[u];
+    const uint8_t* src = phase == 1 ? a.w1 + (static_cast<int64_t>(e) * a.I + tile * 16) * a.rb1
+                                    : a.w2 + (static_cast<int64_t>(e) * a.H + tile * 16) * a.rb2;
+    const uint32_t bytes = 16u * static_cast<uint32_t>(phase == 1 ? a.rb1 : a.rb2);
+    mbar_arrive_expect_tx(&full[s], bytes);
+    bulk_g2s(stage0 + s * a.stage_bytes, src, bytes, &full[s]);
+  };
+  if (leader) {
+    if (first < nitems) fetch(first, 0u);
+    if (first + teams < nitems) fetch(first + teams, 1u);
+  }
+
+  // the z fragments of every (activation row, phase-1 slice): one conversion per CTA
+  const int zunits = a.R * (a.H / 256);
+  for (int unit = warp; unit < zunits; unit += kMoePWarps) {
+    const int r = unit / (a.H / 256), sl = unit % (a.H / 256);
+    I8XFrag f;
+    perm_x_frag(ldg128(a.z + static_cast<int64_t>(r) * a.H + sl * 256 + 8 * lane), f);
+    zfrag_store(f, zf + unit * kZFragBytes);
+  }
+  __syncthreads();
+
+  const int g = lane >> 2, t = lane & 3;
+  const int bar_id = 1 + team, bar_n = kMoeTeamWarps * 32;
+  const int slices1 = a.H / 256, slices2 = a.I / 256;
+  uint32_t k = 0;
+  for (int q = first; q < nitems; q += teams, ++k) {
+    int phase, u, tile;
+    item_of(q, phase, u, tile);
+    if (phase == 2) {  // every phase-1 tile of expert u must be in h
+      if (leader) {
+        const uint64_t t0 = global_timer_ns();
+        int v;
+        for (;;) {
+          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(a.done + u) : "memory");
+          if (v >= a.T1) break;
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(kMoeDoneWaitSite);
+            break;
+          }
+          __nanosleep(128);
+        }
+      }
+      named_bar_sync(bar_id, bar_n);
+    }
+    const int s = static_cast<int>(k & 1u);
+    mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
+    const uint8_t* st = stage0 + s * a.stage_bytes;
+    float acc[kMaxR][2];
+#pragma unroll
+    for (int r = 0; r < kMaxR; ++r) acc[r][0] = acc[r][1] = 0.f;
+    const uint32_t rb = static_cast<uint32_t>(phase == 1 ? a.rb1 : a.rb2);
+    const uint32_t r0 = static_cast<uint32_t>(g) * rb, r1 = static_cast<uint32_t>(g + 8) * rb;
+    const int slices = phase == 1 ? slices1 : slices2;
+    for (int sl = tw; sl < slices; sl += kMoeTeamWarps) {
+      uint2 rc[4];
+      uint32_t dbits;
+      i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
+      uint32_t A[4][4][2];
+      i8_decode(smem, rc, A);
+#pragma unroll
+      for (int r = 0; r < kMaxR; ++r) {
+        const int p = r < a.R ? s_pair[u * 8 + r] : -1;
+        if (p < 0) continue;  // warp-uniform
+        I8XFrag f;
+        if (phase == 1) zfrag_load(zf + (r * slices1 + sl) * kZFragBytes, f);
+        else perm_x_frag(__ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(p) * a.I + sl * 256 + 8 * lane)), f);
+        float b0, b1;
+        i8_pair_slice(A, rc, dbits, f, b0, b1);
+        acc[r][0] += b0;
+        acc[r][1] += b1;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    // team reduction per (pair, row); slot (k & 1) is rewritten two items later, after a barrier
+    float* rbuf = red + s * kMoeTeamWarps * kMaxR * 16;
+#pragma unroll
+    for (int r = 0; r < kMaxR; ++r) {
+      if (r >= a.R || s_pair[u * 8 + r] < 0) continue;  // warp-uniform
+      float v0 = acc[r][0], v1 = acc[r][1];
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+      v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+      v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+      if (t == 0) {
+        rbuf[(tw * kMaxR + r) * 16 + g] = v0;
+        rbuf[(tw * kMaxR + r) * 16 + g + 8] = v1;
+      }
+    }
+    named_bar_sync(bar_id, bar_n);
+    for (int ti = tw * 32 + lane; ti < kMaxR * 16; ti += kMoeTeamWarps * 32) {
+      const int r = ti >> 4, rl = ti & 15;
+      const int p = r < a.R ? s_pair[u * 8 + r] : -1;
+      if (p < 0) continue;
+      const float v = (rbuf[(0 * kMaxR + r) * 16 + rl] + rbuf[(1 * kMaxR + r) * 16 + rl]) +
+                      (rbuf[(2 * kMaxR + r) * 16 + rl] + rbuf[(3 * kMaxR + r) * 16 + rl]);
+      const float vb = round_bf16(v);
+      if (phase == 1) {
+        const float rr = fmaxf(vb, 0.f);
+        a.h[static_cast<int64_t>(p) * a.I + tile * 16 + rl] = __float2bfloat16(rr * rr);
+      } else {
+        a.part[static_cast<int64_t>(p) * a.H + tile * 16 + rl] = vb;
       }
     }
     if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);

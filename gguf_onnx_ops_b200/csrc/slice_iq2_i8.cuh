@@ -155,6 +155,60 @@ __device__ __forceinline__ void i8_x_frag(const uint4 xv, I8XFrag& f) {
   f.xs1 = ldexpf(1.0f, e1 - 141);
 }
 
+// B fragments of one 256-element activation slice with permuted columns: column 2t of the
+// block-diagonal B carries group t and column 2t + 1 group t + 4, so the C cells lane (g, t) holds
+// (rows g, g + 8 x groups t, t + 4) are exactly the records it decodes and the sub-block scales need
+// no shuffles.  Lane (g, t)'s b0 is non-zero for g = 2t, b1 for g = 2t + 1.  Conversion as
+// i8_x_frag: x_int = x * 2^(14 - E) per 32-element group, split into a signed high and an unsigned
+// low byte.  xs0 / xoff0 belong to the lane's column 2t (group t), xs1 / xoff1 to column 2t + 1.
+__device__ __forceinline__ void perm_x_frag(const uint4 xv, I8XFrag& f) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const bool dlo = (g == 2 * t), dhi = (g == 2 * t + 1);
+  const uint32_t wv[4] = {xv.x, xv.y, xv.z, xv.w};
+  uint32_t mb = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mb = max(mb, max(wv[i] & 0x7FFFu, (wv[i] >> 16) & 0x7FFFu));
+  mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+  mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+  const int emax = max(1, static_cast<int>(mb >> 7));
+  const bool tiny = emax < 64;
+  const float s1 = tiny ? 18446744073709551616.0f : 1.0f;  // 2^64
+  const float s2 = __uint_as_float(static_cast<uint32_t>(268 - emax - (tiny ? 64 : 0)) << 23);
+  uint32_t r[8], rsum = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float v = __uint_as_float(i & 1 ? (wv[i >> 1] & 0xFFFF0000u) : (wv[i >> 1] << 16));
+    r[i] = __float_as_uint((v * s1) * s2 + 12582912.0f);
+    rsum += r[i];
+  }
+  uint32_t hw[2], lw[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    hw[k] = __byte_perm(__byte_perm(r[4 * k], r[4 * k + 1], 0x0051u), __byte_perm(r[4 * k + 2], r[4 * k + 3], 0x0051u), 0x5410u);
+    lw[k] = __byte_perm(__byte_perm(r[4 * k], r[4 * k + 1], 0x0040u), __byte_perm(r[4 * k + 2], r[4 * k + 3], 0x0040u), 0x5410u);
+  }
+  int xsum = static_cast<int>(rsum - 8u * 0x4B400000u);
+  xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+  xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+  // the group this lane's non-zero B column carries; step j of group c = word (j & 1) of lane 4c + (j >> 1)
+  const int c = dlo ? t : (dhi ? t + 4 : 0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int src = 4 * c + (j >> 1);
+    const uint32_t h = __shfl_sync(0xffffffffu, hw[j & 1], src);
+    const uint32_t l = __shfl_sync(0xffffffffu, lw[j & 1], src);
+    f.bh0[j] = dlo ? h : 0u;
+    f.bl0[j] = dlo ? l : 0u;
+    f.bh1[j] = dhi ? h : 0u;
+    f.bl1[j] = dhi ? l : 0u;
+  }
+  const int e0 = __shfl_sync(0xffffffffu, emax, 4 * t), e1 = __shfl_sync(0xffffffffu, emax, 4 * (t + 4));
+  f.xoff0 = 64 * __shfl_sync(0xffffffffu, xsum, 4 * t);
+  f.xoff1 = 64 * __shfl_sync(0xffffffffu, xsum, 4 * (t + 4));
+  f.xs0 = ldexpf(1.0f, e0 - 141);  // 2^(E - 14)
+  f.xs1 = ldexpf(1.0f, e1 - 141);
+}
+
 // The records of one slice for lane (g, t): grid bytes + sign/scale words of rows g, g+8 x groups
 // t, t+4 (rc[0..3] = [g, t], [g, t+4], [g+8, t], [g+8, t+4]) and the two super-block scales.
 // r0 / r1: byte offsets of rows g / g+8 in the stage; so: the slice's byte offset in a row (its

@@ -171,14 +171,18 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
     if (lane == 0) last = atom_add_acq_rel_cta(&cnt[s], 1) == kW - 1;
     if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this tile are in the slot
       const float* rs = red + s * kW * kRX * 16;
+      const bool vec = a.po.npeer && a.po.vec && tile * 16 + 16 <= a.N;  // full tile, aligned peer rows
 #pragma unroll
       for (int o = lane; o < kRX * 16; o += 32) {
         float v[4] = {0.f, 0.f, 0.f, 0.f};  // fixed summation order: 4 strided partial sums, then a tree
 #pragma unroll
         for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rs[w2 * kRX * 16 + o];
         const int xr = o >> 4, row = tile * 16 + (o & 15);
-        if (xr < a.R && row < a.N) {
-          const bf16 yv = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+        const bf16 yv = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+        if (vec) {  // row-split shard: 16-byte stores into every GPU's y (warp-uniform branch)
+          if (o - lane < 16 * a.R)  // the pass's first half holds an activation row < R
+            peer_store_tile16(a.po, yv, xr < a.R, xr, tile * 16);
+        } else if (xr < a.R && row < a.N) {
           if (a.po.npeer) peer_store(a.po, xr, row, yv);  // row-split shard: into every GPU's y
           else a.y[static_cast<int64_t>(xr) * a.N + row] = yv;
         }
