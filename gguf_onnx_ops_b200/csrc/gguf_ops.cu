@@ -963,13 +963,12 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   } else if (g_fast.load() == 1) {
     // 2..8 rows: the integer decode shared by every pair of an expert (moe_pairs_kernel)
     MoeFusedArgs b = a;
-    const int maxr = R <= 2 ? 2 : (R <= 4 ? 4 : 8);
     b.off_stage = kI8Lut;
     b.off_red = b.off_stage + kMoePTeams * 2 * a.stage_bytes;
-    b.off_bar = b.off_red + kMoePTeams * 2 * kMoeTeamWarps * maxr * 16 * 4;
+    b.off_bar = b.off_red + kMoePTeams * 2 * kMoeTeamWarps * 8 * 16 * 4;
     b.off_grp = b.off_bar + kMoePTeams * 4 * 8;
     b.off_zf = (b.off_grp + grp + 127) & ~127;
-    const size_t smem2 = b.off_zf + static_cast<size_t>(R) * (H / 256) * kZFragBytes;
+    const size_t smem2 = b.off_zf + static_cast<size_t>(R) * (H / 256) * kZFragBytes + kZeroBytes + kMaxPairs * 9 * 4;
     if (smem2 > static_cast<size_t>(kSmemBudgetMax)) {  // large I: the bf16-decode kernel's smaller tables
       auto kern = moe_fused_kernel;
       if ((rc = ensure_smem(kern, smem, done))) return rc;
@@ -977,9 +976,9 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
       if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
       goto finalize;
     }
-    static std::atomic<uint64_t> d2{0}, d4{0}, d8{0};
-    auto kern = maxr == 2 ? moe_pairs_kernel<2> : (maxr == 4 ? moe_pairs_kernel<4> : moe_pairs_kernel<8>);
-    if ((rc = ensure_smem(kern, smem2, maxr == 2 ? d2 : (maxr == 4 ? d4 : d8)))) return rc;
+    static std::atomic<uint64_t> dp{0};
+    auto kern = moe_pairs_kernel;
+    if ((rc = ensure_smem(kern, smem2, dp))) return rc;
     // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
     e = launch(kern, dim3(sms), dim3(kMoePWarps * 32), smem2, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);

@@ -388,11 +388,12 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
 // those of moe_fused_kernel; the team sums its warps' partials per (pair, row) in warp order.
 // ---------------------------------------------------------------------------------------------
 constexpr int kZFragBytes = 8 * 64 + 8 * 8;  // per (row, slice): 8 groups x (8 high + 8 low limb words), xs[8], xoff[8]
+constexpr int kZeroBytes = 64;                // zero limb words for lanes whose B half is empty
 constexpr int kMoePTeams = 4, kMoePWarps = kMoePTeams * kMoeTeamWarps;
 
 // lane (g, t) of a permuted fragment (perm_x_frag): its non-zero B column carries group t (g = 2t,
-// words bh0 / bl0) or group t + 4 (g = 2t + 1, words bh1 / bl1); lanes of quad 0 hold every group's
-// xs / xoff in their (xs0, xoff0) = group t and (xs1, xoff1) = group t + 4
+// words bh0 / bl0) or group t + 4 (g = 2t + 1, words bh1 / bl1); every lane holds the xs / xoff of
+// its groups t (xs0, xoff0) and t + 4 (xs1, xoff1)
 __device__ __forceinline__ void zfrag_store(const I8XFrag& f, uint8_t* dst) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   uint32_t* w = reinterpret_cast<uint32_t*>(dst);
@@ -414,29 +415,27 @@ __device__ __forceinline__ void zfrag_store(const I8XFrag& f, uint8_t* dst) {
     xo[t + 4] = f.xoff1;
   }
 }
-__device__ __forceinline__ void zfrag_load(const uint8_t* src, I8XFrag& f) {
+// Each B half comes from its group's words or from the zero block (no selects).
+__device__ __forceinline__ void zfrag_load(const uint8_t* src, const uint8_t* zero, I8XFrag& f) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const bool lo = g == 2 * t, hi = g == 2 * t + 1;
-  const uint32_t* w = reinterpret_cast<const uint32_t*>(src);
-  const uint4* gw = reinterpret_cast<const uint4*>(w + (hi ? t + 4 : t) * 16);
-  uint32_t v[16];
+  const uint4* p0 = reinterpret_cast<const uint4*>(g == 2 * t ? src + t * 64 : zero);
+  const uint4* p1 = reinterpret_cast<const uint4*>(g == 2 * t + 1 ? src + (t + 4) * 64 : zero);
+  uint4 q[8];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 u = (lo || hi) ? gw[q] : make_uint4(0u, 0u, 0u, 0u);
-    v[4 * q] = u.x;
-    v[4 * q + 1] = u.y;
-    v[4 * q + 2] = u.z;
-    v[4 * q + 3] = u.w;
+  for (int i = 0; i < 4; ++i) {
+    q[i] = p0[i];
+    q[4 + i] = p1[i];
   }
+  const uint32_t* v = reinterpret_cast<const uint32_t*>(q);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    f.bh0[j] = lo ? v[j] : 0u;
-    f.bl0[j] = lo ? v[8 + j] : 0u;
-    f.bh1[j] = hi ? v[j] : 0u;
-    f.bl1[j] = hi ? v[8 + j] : 0u;
+    f.bh0[j] = v[j];
+    f.bl0[j] = v[8 + j];
+    f.bh1[j] = v[16 + j];
+    f.bl1[j] = v[24 + j];
   }
-  const float* xs = reinterpret_cast<const float*>(w + 128);
-  const int* xo = reinterpret_cast<const int*>(w + 136);
+  const float* xs = reinterpret_cast<const float*>(src + 512);
+  const int* xo = reinterpret_cast<const int*>(src + 544);
   f.xs0 = xs[t];
   f.xs1 = xs[t + 4];
   f.xoff0 = xo[t];
@@ -459,12 +458,12 @@ __device__ __forceinline__ void i8_decode(const uint8_t* smem, const uint2 (&rc)
     }
   }
 }
-// 16 MMAs of decoded A against one pair's permuted fragments and the epilogue (the permuted-column epilogue): the
+// 16 MMAs of decoded A against one pair's permuted fragments and the permuted-column epilogue: the
 // lane's partial sums of weight rows g (acc0) and g + 8 (acc1) over its groups t, t + 4.
 __device__ __forceinline__ void i8_pair_slice(const uint32_t (&A)[4][4][2], const uint2 (&rc)[4], uint32_t dbits,
                                               const I8XFrag& f, float& acc0, float& acc1) {
   int ch[4] = {0, 0, 0, 0};
-  int cl[4] = {-f.xoff0, -f.xoff1, -f.xoff0, -f.xoff1};
+  int cl[4] = {-f.xoff0, -f.xoff1, -f.xoff0, -f.xoff1};  // the weights' +64 offset, removed in the MMA
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
 #pragma unroll
@@ -474,6 +473,8 @@ __device__ __forceinline__ void i8_pair_slice(const uint32_t (&A)[4][4][2], cons
       imma_u8u8(cl, A[e][0][h], A[e][2][h], A[e][1][h], A[e][3][h], f.bl0[j], f.bl1[j]);
     }
   }
+  // cells [row g, group t], [g, t + 4], [g + 8, t], [g + 8, t + 4] = records 0..3; (2 s + 1) * cell
+  // is exact in s32 (|cell| <= 32 * 43 * 32640, times 31 < 2^31); d * (0.5 + s) / 4 = d (2 s + 1) / 8
   const float v0 = static_cast<float>((ch[0] * 256 + cl[0]) * static_cast<int>((rc[0].y >> 27) | 1u));
   const float v1 = static_cast<float>((ch[1] * 256 + cl[1]) * static_cast<int>((rc[1].y >> 27) | 1u));
   const float v2 = static_cast<float>((ch[2] * 256 + cl[2]) * static_cast<int>((rc[2].y >> 27) | 1u));
@@ -483,7 +484,6 @@ __device__ __forceinline__ void i8_pair_slice(const uint32_t (&A)[4][4][2], cons
   acc1 = fmaf(v2, f.xs0, v3 * f.xs1) * d1;
 }
 
-template <int kMaxR>
 __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const MoeFusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -492,9 +492,12 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
   uint64_t* empty = full + 2;
   uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
-  float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * kMaxR * 16;  // [2][warps][rows][16]
+  float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 8 * 16;  // [2][warps][8 pairs][16]
   int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
-  uint8_t* zf = smem + a.off_zf;  // [R][H / 256][kZFragBytes]
+  uint8_t* zf = smem + a.off_zf;  // [R][H / 256][kZFragBytes], then kZeroBytes of zeros, then the pair lists
+  const uint8_t* zero = zf + a.R * (a.H / 256) * kZFragBytes;
+  int* s_np = reinterpret_cast<int*>(zf + a.R * (a.H / 256) * kZFragBytes + kZeroBytes);  // [kMaxPairs]
+  int* s_plist = s_np + kMaxPairs;  // [kMaxPairs][8]: pair id | activation row << 16
 
   if (leader) {
     for (int s = 0; s < 2; ++s) {
@@ -503,6 +506,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
     }
     fence_mbar_init();
   }
+  if (threadIdx.x < kZeroBytes / 4) reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(zero))[threadIdx.x] = 0u;
   i8_fill_tables<kMoePWarps * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
   moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
@@ -518,20 +522,27 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
       a.meta[i] = v;
     }
   pdl_launch_dependents();
+  // compact pair list of every unique expert (activation rows in increasing order)
+  for (int u = threadIdx.x; u < U; u += blockDim.x) {
+    int n = 0;
+    for (int r = 0; r < a.R; ++r) {
+      const int p = s_pair[u * 8 + r];
+      if (p >= 0) s_plist[u * 8 + n++] = p | (r << 16);
+    }
+    s_np[u] = n;
+  }
 
   const int n1 = U * a.T1, n2 = U * a.T2, nitems = n1 + n2;
   const int teams = kMoePTeams * static_cast<int>(gridDim.x);
   const int first = team * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x);
+  // item q -> (phase, unique expert u, tile); the quotients by T1 / T2 in fp32 (exact: q < 2^22)
+  const float inv1 = 1.0f / static_cast<float>(a.T1), inv2 = 1.0f / static_cast<float>(a.T2);
   auto item_of = [&](int q, int& phase, int& u, int& tile) {
-    if (q < n1) {
-      phase = 1;
-      u = q / a.T1;
-      tile = q % a.T1;
-    } else {
-      phase = 2;
-      u = (q - n1) / a.T2;
-      tile = (q - n1) % a.T2;
-    }
+    const bool p1 = q < n1;
+    const int qq = p1 ? q : q - n1, T = p1 ? a.T1 : a.T2;
+    u = __float2int_rz((static_cast<float>(qq) + 0.5f) * (p1 ? inv1 : inv2));
+    tile = qq - u * T;
+    phase = p1 ? 1 : 2;
   };
   auto fetch = [&](int q, uint32_t k) {
     int phase, u, tile;
@@ -551,22 +562,22 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   }
 
   // the z fragments of every (activation row, phase-1 slice): one conversion per CTA
-  const int zunits = a.R * (a.H / 256);
-  for (int unit = warp; unit < zunits; unit += kMoePWarps) {
-    const int r = unit / (a.H / 256), sl = unit % (a.H / 256);
+  const int slices1 = a.H / 256, slices2 = a.I / 256;
+  for (int unit = warp; unit < a.R * slices1; unit += kMoePWarps) {
     I8XFrag f;
-    perm_x_frag(ldg128(a.z + static_cast<int64_t>(r) * a.H + sl * 256 + 8 * lane), f);
+    perm_x_frag(ldg128(a.z + static_cast<int64_t>(unit / slices1) * a.H + (unit % slices1) * 256 + 8 * lane), f);
     zfrag_store(f, zf + unit * kZFragBytes);
   }
   __syncthreads();
 
   const int g = lane >> 2, t = lane & 3;
   const int bar_id = 1 + team, bar_n = kMoeTeamWarps * 32;
-  const int slices1 = a.H / 256, slices2 = a.I / 256;
   uint32_t k = 0;
   for (int q = first; q < nitems; q += teams, ++k) {
     int phase, u, tile;
     item_of(q, phase, u, tile);
+    const int np = s_np[u];
+    const int* pl = s_plist + u * 8;
     if (phase == 2) {  // every phase-1 tile of expert u must be in h
       if (leader) {
         const uint64_t t0 = global_timer_ns();
@@ -584,57 +595,64 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
       named_bar_sync(bar_id, bar_n);
     }
     const int s = static_cast<int>(k & 1u);
+    // this warp's partial row sums per pair: slot (k & 1) is rewritten two items later, after a barrier
+    float* rbuf = red + s * kMoeTeamWarps * 8 * 16;
+    float* mine = rbuf + tw * 8 * 16;
+    for (int i = lane; i < np * 16; i += 32) mine[i] = 0.f;
+    __syncwarp();
     mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
     const uint8_t* st = stage0 + s * a.stage_bytes;
-    float acc[kMaxR][2];
-#pragma unroll
-    for (int r = 0; r < kMaxR; ++r) acc[r][0] = acc[r][1] = 0.f;
     const uint32_t rb = static_cast<uint32_t>(phase == 1 ? a.rb1 : a.rb2);
     const uint32_t r0 = static_cast<uint32_t>(g) * rb, r1 = static_cast<uint32_t>(g + 8) * rb;
-    const int slices = phase == 1 ? slices1 : slices2;
-    for (int sl = tw; sl < slices; sl += kMoeTeamWarps) {
-      uint2 rc[4];
-      uint32_t dbits;
-      i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
-      uint32_t A[4][4][2];
-      i8_decode(smem, rc, A);
-#pragma unroll
-      for (int r = 0; r < kMaxR; ++r) {
-        const int p = r < a.R ? s_pair[u * 8 + r] : -1;
-        if (p < 0) continue;  // warp-uniform
-        I8XFrag f;
-        if (phase == 1) zfrag_load(zf + (r * slices1 + sl) * kZFragBytes, f);
-        else perm_x_frag(__ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(p) * a.I + sl * 256 + 8 * lane)), f);
-        float b0, b1;
-        i8_pair_slice(A, rc, dbits, f, b0, b1);
-        acc[r][0] += b0;
-        acc[r][1] += b1;
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    // team reduction per (pair, row); slot (k & 1) is rewritten two items later, after a barrier
-    float* rbuf = red + s * kMoeTeamWarps * kMaxR * 16;
-#pragma unroll
-    for (int r = 0; r < kMaxR; ++r) {
-      if (r >= a.R || s_pair[u * 8 + r] < 0) continue;  // warp-uniform
-      float v0 = acc[r][0], v1 = acc[r][1];
+    // one pair's MMAs on decoded A, reduced over the quad and added to the warp's slot of the pair
+    auto pair_step = [&](const uint32_t (&A)[4][4][2], const uint2 (&rc)[4], uint32_t dbits, const I8XFrag& f, int i) {
+      float v0, v1;
+      i8_pair_slice(A, rc, dbits, f, v0, v1);
       v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
       v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
       v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
       v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
       if (t == 0) {
-        rbuf[(tw * kMaxR + r) * 16 + g] = v0;
-        rbuf[(tw * kMaxR + r) * 16 + g + 8] = v1;
+        mine[i * 16 + g] += v0;
+        mine[i * 16 + g + 8] += v1;
+      }
+    };
+    if (phase == 1) {
+      for (int sl = tw; sl < slices1; sl += kMoeTeamWarps) {
+        uint2 rc[4];
+        uint32_t dbits;
+        i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
+        uint32_t A[4][4][2];
+        i8_decode(smem, rc, A);
+        for (int i = 0; i < np; ++i) {  // every pair of the expert, same decoded A
+          I8XFrag f;
+          zfrag_load(zf + ((pl[i] >> 16) * slices1 + sl) * kZFragBytes, zero, f);
+          pair_step(A, rc, dbits, f, i);
+        }
+      }
+    } else {
+      for (int sl = tw; sl < slices2; sl += kMoeTeamWarps) {
+        uint2 rc[4];
+        uint32_t dbits;
+        i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
+        uint32_t A[4][4][2];
+        i8_decode(smem, rc, A);
+        for (int i = 0; i < np; ++i) {
+          const int p = pl[i] & 0xFFFF;
+          I8XFrag f;
+          perm_x_frag(__ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(p) * a.I + sl * 256 + 8 * lane)), f);
+          pair_step(A, rc, dbits, f, i);
+        }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
     named_bar_sync(bar_id, bar_n);
-    for (int ti = tw * 32 + lane; ti < kMaxR * 16; ti += kMoeTeamWarps * 32) {
-      const int r = ti >> 4, rl = ti & 15;
-      const int p = r < a.R ? s_pair[u * 8 + r] : -1;
-      if (p < 0) continue;
-      const float v = (rbuf[(0 * kMaxR + r) * 16 + rl] + rbuf[(1 * kMaxR + r) * 16 + rl]) +
-                      (rbuf[(2 * kMaxR + r) * 16 + rl] + rbuf[(3 * kMaxR + r) * 16 + rl]);
+    for (int ti = tw * 32 + lane; ti < np * 16; ti += kMoeTeamWarps * 32) {
+      const int i = ti >> 4, rl = ti & 15;
+      const int p = pl[i] & 0xFFFF;
+      // fixed order: warps 0 + 1, then 2 + 3
+      const float v = (rbuf[ti] + rbuf[128 + ti]) + (rbuf[256 + ti] + rbuf[384 + ti]);
       const float vb = round_bf16(v);
       if (phase == 1) {
         const float rr = fmaxf(vb, 0.f);
