@@ -97,7 +97,8 @@ class GgufPeerOut(ctypes.Structure):
     """Mirror of GgufPeerOut (include/gguf_ops.h)."""
 
     _fields_ = [("y", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8), ("state", ctypes.c_void_p),
-                ("world", ctypes.c_int), ("rank", ctypes.c_int), ("n_total", ctypes.c_int64), ("row0", ctypes.c_int64)]
+                ("world", ctypes.c_int), ("rank", ctypes.c_int), ("n_total", ctypes.c_int64), ("row0", ctypes.c_int64),
+                ("ctas", ctypes.c_int32)]
 
 
 class GgufPeerReduce(ctypes.Structure):

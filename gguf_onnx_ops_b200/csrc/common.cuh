@@ -147,23 +147,27 @@ __device__ __forceinline__ uint32_t ldg32(const void* p) { return __ldg(reinterp
 constexpr int kMaxPeers = 8;
 
 // Output of one shard of a row-split GEMV: every value is stored into the full-size y of every
-// GPU of the group (peer pointers from CUDA IPC, NVLink stores), then a flag protocol makes the
+// GPU of the group (peer pointers from CUDA IPC, NVLink stores), then an arrival count makes the
 // launch complete only when every peer's shard has landed in this GPU's y.
 struct PeerOut {
   bf16* y[kMaxPeers];          // y of GPU p: [R, ld] bf16 (this shard's rows start at row0)
-  uint32_t* flags[kMaxPeers];  // flag array of GPU p: [kMaxPeers], slot q = last epoch GPU q finished
-  uint32_t* state;             // this GPU: [0] = completed epochs, [1] = CTAs of the running launch finished
+  uint32_t* flags[kMaxPeers];  // arrival counters of GPU p: [kMaxPeers], slot q = CTAs of GPU q arrived (cumulative)
+  uint32_t* state;             // this GPU: [0] = completed calls
   int npeer, rank, ld, row0;
   int vec;                     // 1: every y[p] 16-byte aligned, ld and row0 multiples of 8 (16-byte stores)
+  int ctas;                    // CTAs every GPU of the group launches per call (the same on every GPU)
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void red_relaxed_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // y[col, row] of this shard (row local to the shard) into every GPU's output.
@@ -195,30 +199,33 @@ __device__ __forceinline__ void peer_store_tile16(const PeerOut& po, bf16 v, boo
   }
 }
 
-// Called by one thread per CTA after the CTA's last peer_store (and a barrier over the threads that
-// stored).  The last CTA of the launch publishes this GPU's epoch to every peer and waits, bounded,
-// for every peer's; the launch therefore ends only once the whole y is present on this GPU.  Must
-// run after griddepcontrol.wait (the previous launch of the op updates state[0] last).
+// Called by one thread per CTA after the CTA's last peer store (and a barrier over the threads that
+// stored).  Every CTA makes its stores visible system-wide (one system-scope fence) and then counts
+// itself as arrived at every GPU of the group (slot `rank` of each peer's arrival counters; the
+// counters only grow, so nothing has to be reset between calls).  CTA 0 then waits, bounded, until
+// every GPU's slot in its own counters holds calls * ctas: every CTA of every GPU, this call
+// included, has arrived, so the whole y is present here when the launch ends.  Must run after
+// griddepcontrol.wait (CTA 0 of the previous launch updates state[0] last).  A peer can be at most
+// one call ahead (it cannot finish call e + 1 before this GPU's CTAs of call e + 1 arrive), so the
+// counts compared below are at most one call's CTAs apart and the 32-bit difference is exact.
 __device__ __forceinline__ void peer_complete(const PeerOut& po) {
   __threadfence_system();
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(po.state) + 1u;
-  const uint32_t done = atomicAdd(po.state + 1, 1u) + 1u;
-  if (done != gridDim.x) return;  // not the last CTA of this launch
-  __threadfence_system();
-  po.state[1] = 0u;  // the next launch counts from zero (it reaches this point only after griddepcontrol.wait)
-  for (int p = 0; p < po.npeer; ++p) st_release_sys(po.flags[p] + po.rank, epoch);
+  for (int p = 0; p < po.npeer; ++p) red_relaxed_sys_add(po.flags[p] + po.rank, 1u);
+  if (blockIdx.x != 0) return;
+  const uint32_t calls = *reinterpret_cast<volatile uint32_t*>(po.state) + 1u;
+  const uint32_t target = calls * static_cast<uint32_t>(po.ctas);
   const uint32_t* mine = po.flags[po.rank];
   const uint64_t t0 = global_timer_ns();
   for (int p = 0; p < po.npeer; ++p) {
-    while (static_cast<int32_t>(ld_acquire_sys(mine + p) - epoch) < 0) {
+    while (static_cast<int32_t>(ld_acquire_sys(mine + p) - target) < 0) {
       if (global_timer_ns() - t0 > kWaitLimitNs) {
         record_device_error(kSitePeerWait);
         break;
       }
-      __nanosleep(64);
+      __nanosleep(32);
     }
   }
-  *reinterpret_cast<volatile uint32_t*>(po.state) = epoch;
+  *reinterpret_cast<volatile uint32_t*>(po.state) = calls;
 }
 
 // Sum across GPUs of an f32 [R, H] partial (expert-parallel MoeVerify): every GPU stores its
@@ -236,8 +243,8 @@ struct PeerReduce {
 // Thread 0 of the (single) reducing CTA, after the CTA's stores into the peers' slots: publish and
 // wait (bounded).  Returns the epoch of this call.
 __device__ __forceinline__ uint32_t peer_reduce_sync(const PeerReduce& pr, uint32_t epoch) {
-  __threadfence_system();
-  for (int p = 0; p < pr.npeer; ++p) st_release_sys(pr.flags[p] + pr.rank, epoch);
+  __threadfence_system();  // one system-scope fence orders the slot stores before every flag below
+  for (int p = 0; p < pr.npeer; ++p) st_relaxed_sys(pr.flags[p] + pr.rank, epoch);
   const uint32_t* mine = pr.flags[pr.rank];
   const uint64_t t0 = global_timer_ns();
   for (int p = 0; p < pr.npeer; ++p) {

@@ -234,7 +234,8 @@ int run_dense(const void* x, const void* w, const float* gscale, void* y, int R,
   static std::atomic<uint64_t> done{0};
   auto kern = engine_kernel<F, NT, kKW, kModeDense>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  const int grid = std::min(a.tiles, 2 * sms);  // two CTAs per SM (engine_kernel launch bounds)
+  // two CTAs per SM (engine_kernel launch bounds); row-split: the group's CTA count
+  const int grid = a.po.npeer ? a.po.ctas : std::min(a.tiles, 2 * sms);
   cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("gemv launch", e);
   return GGUF_OK;
@@ -263,7 +264,8 @@ int run_dense_split(const void* x, const void* w, const void* sc, const float* g
   static std::atomic<uint64_t> done{0};
   auto kern = engine_kernel<F, NT, kKW, kModeDense>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  const int grid = std::min(a.tiles, 2 * sms);  // two CTAs per SM (engine_kernel launch bounds)
+  // two CTAs per SM (engine_kernel launch bounds); row-split: the group's CTA count
+  const int grid = a.po.npeer ? a.po.ctas : std::min(a.tiles, 2 * sms);
   cudaError_t e = launch(kern, dim3(grid), dim3(kThreads), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("legacy-layout gemv launch", e);
   return GGUF_OK;
@@ -299,7 +301,8 @@ int run_slice_r1(const void* x, const void* w, const float* gscale, void* y, int
   static std::atomic<uint64_t> done{0};
   auto kern = slice_r1_kernel<F, kW, kSPW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3((kW + 1) * 32), smem, s, a);
+  const int grid = a.po.npeer ? a.po.ctas : std::min(a.tiles, sms);  // row-split: the group's CTA count
+  cudaError_t e = launch(kern, dim3(grid), dim3((kW + 1) * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("single-row GEMV launch", e);
   return GGUF_OK;
 }
@@ -478,7 +481,8 @@ int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, in
   static std::atomic<uint64_t> done{0};
   auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  const int grid = a.po.npeer ? a.po.ctas : std::min(a.tiles, sms);  // row-split: the group's CTA count
+  cudaError_t e = launch(kern, dim3(grid), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row Q8_0 GEMV launch", e);
   return GGUF_OK;
 }
@@ -1281,6 +1285,10 @@ int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float
   po.row0 = static_cast<int>(out->row0);
   po.vec = out->n_total % 8 == 0 && out->row0 % 8 == 0;
   for (int p = 0; p < out->world; ++p) po.vec = po.vec && aligned(out->y[p], 16);
+  po.ctas = out->ctas;
+  if (po.ctas == 0 && current_sms(&po.ctas)) return GGUF_ERR_CUDA;
+  if (po.ctas < 1 || po.ctas > (1 << 16))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: ctas must be in [1, 65536] (0: this GPU's SM count)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (type) {
     case GGUF_TYPE_Q8_0:

@@ -329,9 +329,22 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
     } else {
       const uint32_t r0 = static_cast<uint32_t>(g * a.rb2), r1 = static_cast<uint32_t>((g + 8) * a.rb2);
       const bf16* hp = a.h + static_cast<int64_t>(p) * a.I;
-      for (int sl = tw; sl < slices2; sl += kMoeTeamWarps) {
+      // every h slice of this warp in flight at once (read through L2: written by this launch)
+      constexpr int kHPre = 2;
+      uint4 hv[kHPre];
+#pragma unroll
+      for (int i = 0; i < kHPre; ++i) {
+        const int sl = tw + i * kMoeTeamWarps;
+        hv[i] = sl < slices2 ? __ldcg(reinterpret_cast<const uint4*>(hp + sl * 256 + 8 * lane)) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      for (int sl = tw, i = 0; sl < slices2; sl += kMoeTeamWarps, ++i) {
         I8XFrag hf;
-        i8_x_frag(__ldcg(reinterpret_cast<const uint4*>(hp + sl * 256 + 8 * lane)), hf);
+        uint4 xv = hv[0];
+#pragma unroll
+        for (int j = 1; j < kHPre; ++j)
+          if (i == j) xv = hv[j];
+        if (i >= kHPre) xv = __ldcg(reinterpret_cast<const uint4*>(hp + sl * 256 + 8 * lane));
+        i8_x_frag(xv, hf);
         uint2 rc[4];
         uint32_t dbits;
         i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
@@ -632,15 +645,19 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
       }
     } else {
       for (int sl = tw; sl < slices2; sl += kMoeTeamWarps) {
+        // the first pair's h slice is in flight while the tile decodes (read through L2)
+        uint4 hv = __ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(pl[0] & 0xFFFF) * a.I + sl * 256 + 8 * lane));
         uint2 rc[4];
         uint32_t dbits;
         i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
         uint32_t A[4][4][2];
         i8_decode(smem, rc, A);
         for (int i = 0; i < np; ++i) {
-          const int p = pl[i] & 0xFFFF;
+          const uint4 cur = hv;
+          if (i + 1 < np)  // the next pair's slice while this one computes
+            hv = __ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(pl[i + 1] & 0xFFFF) * a.I + sl * 256 + 8 * lane));
           I8XFrag f;
-          perm_x_frag(__ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(p) * a.I + sl * 256 + 8 * lane)), f);
+          perm_x_frag(cur, f);
           pair_step(A, rc, dbits, f, i);
         }
       }

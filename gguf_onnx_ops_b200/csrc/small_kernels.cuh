@@ -229,16 +229,27 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restri
   const int t = blockIdx.x;
   for (int v = threadIdx.x; v < H / 4; v += blockDim.x) {
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    // the partial rows are loaded together with the expert ids (not after them): one round trip
+    constexpr int kPre = 8;
+    float4 pv[kPre];
+#pragma unroll
+    for (int k = 0; k < kPre; ++k)
+      pv[k] = k < topk ? __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(t * topk + k) * H) + v)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < topk; ++k) {
       const int p = t * topk + k;
       const int e = __ldg(idx + p);
       if (e < 0 || e >= E) continue;
       const float wk = __ldg(w + p);
-      const float4 pv = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(p) * H) + v);
-      a0 += wk * pv.x;
-      a1 += wk * pv.y;
-      a2 += wk * pv.z;
-      a3 += wk * pv.w;
+      float4 q = pv[0];
+#pragma unroll
+      for (int j = 1; j < kPre; ++j)
+        if (k == j) q = pv[j];
+      if (k >= kPre) q = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(p) * H) + v);
+      a0 += wk * q.x;
+      a1 += wk * q.y;
+      a2 += wk * q.z;
+      a3 += wk * q.w;
     }
     uint2 o;
     o.x = pack_bf16x2(a0, a1);

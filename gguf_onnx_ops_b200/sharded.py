@@ -86,8 +86,13 @@ class RowSplitGemv:
         self.flags = torch.zeros(MAX_PEERS, dtype=torch.int32, device=dev)
         self.state = torch.zeros(2, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
-        mine = [ipc_handle(self.y[0]), ipc_handle(self.y[1]), ipc_handle(self.flags)]
+        # every GPU launches the same number of CTAs per call (the smallest SM count of the group):
+        # each GPU waits until every CTA of every GPU has counted itself in its arrival counters
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        mine = [ipc_handle(self.y[0]), ipc_handle(self.y[1]), ipc_handle(self.flags), sms]
         allh = exchange(mine, group)
+        self.ctas = min(h[3] for h in allh)
+        allh = [h[:3] for h in allh]
         self._opened = []
         self._po = [_lib.GgufPeerOut(), _lib.GgufPeerOut()]
         for p, hs in enumerate(allh):
@@ -106,6 +111,7 @@ class RowSplitGemv:
             po.state = self.state.data_ptr()
             po.world, po.rank = self.world, self.rank
             po.n_total, po.row0 = n_total, row0
+            po.ctas = self.ctas
         self.calls = 0
 
     def __call__(self, x: torch.Tensor, w: torch.Tensor | None = None, stream=None) -> torch.Tensor:

@@ -228,18 +228,21 @@ GGUF_OPS_API int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* i
  * `world` holds rows [row0, row0 + rows) of W (w_shard, raw GGUF rows) and computes those outputs
  * for all R activation rows; every value is stored directly into the full y [R, n_total] of every
  * GPU of the group (peer pointers opened with gguf_ipc_open, NVLink stores), and the launch ends
- * only when every peer's shard has landed in this GPU's y (epoch flags, bounded waits reported
- * through gguf_device_status).  All GPUs of the group must issue the same sequence of calls.
+ * only when every peer's shard has landed in this GPU's y (every CTA of every GPU counts itself in
+ * every GPU's arrival counters after one system-scope fence; one CTA per GPU waits, bounded, for the
+ * whole group's count; timeouts are reported through gguf_device_status).  All GPUs of the group must issue the same sequence of calls.
  * Double buffering: a peer that finished call e may start call e+1 while this GPU still reads the
  * y of call e, so consecutive calls must alternate between two y buffers (flags and state are
  * shared by the two).
  */
 typedef struct {
   void* y[8];           /* y of GPU p (bf16 [R, n_total]); y[rank] = this GPU's own buffer */
-  uint32_t* flags[8];   /* flag array of GPU p: uint32 [8], zero-initialised, shared by all calls */
+  uint32_t* flags[8];   /* arrival counters of GPU p: uint32 [8], zero-initialised, shared by all calls */
   uint32_t* state;      /* this GPU: uint32 [2], zero-initialised, shared by all calls */
   int world, rank;
   int64_t n_total, row0;
+  int32_t ctas;         /* CTAs each GPU launches per call: the same value on every GPU of the group;
+                           0 = this GPU's SM count (only when every GPU of the group has the same) */
 } GgufPeerOut;
 
 /* type = GGUF_TYPE_*; gscale for NVFP4 only.  Contract as the single-GPU GEMV of that type, plus
