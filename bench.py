@@ -443,7 +443,6 @@ def bench_rowsplit(R, steps, warmup, dev, world, rank, nccl=False, e2e=False, sa
     full = gen_weights("q8_0", N, K, seed=1, dev=dev)  # the same on every rank
     base = full[row0:row0 + rows].contiguous()
     copies = n_copies(rows * rb)
-    copies += copies & 1  # an even number of calls per pass keeps the double-buffer parity fixed
     x = seeded_bf16((R, K), 100 + R, dev)
     op = RowSplitGemv(_lib.GGUF_TYPE_Q8_0, base, N, row0, K, r_max=R)
     # parity: the gathered y against the single-GPU op on the full matrix
@@ -492,23 +491,20 @@ def bench_rowsplit(R, steps, warmup, dev, world, rank, nccl=False, e2e=False, sa
         # public API end to end: pinned host x -> device, one pass of row-split calls, y -> pinned host
         xh = torch.randn(R, K).bfloat16().pin_memory()
         yh = torch.empty(copies, R, N, dtype=torch.bfloat16).pin_memory()
+        yd = [torch.empty(R, N, dtype=torch.bfloat16, device=dev) for _ in range(copies)]
         xd = torch.empty_like(x)
         copy_stream = torch.cuda.Stream()
         done = [torch.cuda.Event() for _ in range(copies)]
-        copied = [torch.cuda.Event() for _ in range(copies)]
 
         def step():
             xd.copy_(xh, non_blocking=True)
             for i, w in enumerate(ws):
-                if rank == 0 and i >= 2:  # call i reuses call i-2's y buffer: its copy must be done
-                    torch.cuda.current_stream().wait_event(copied[i - 2])
-                yy = op(xd, w=w)
+                yy = op(xd, w=w, out=yd[i])  # each call's y in its own buffer, read back while the next runs
                 if rank == 0:
                     done[i].record()
                     with torch.cuda.stream(copy_stream):
                         copy_stream.wait_event(done[i])
                         yh[i].copy_(yy, non_blocking=True)
-                        copied[i].record()
             if rank == 0:
                 torch.cuda.current_stream().wait_stream(copy_stream)
 

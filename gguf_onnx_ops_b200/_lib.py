@@ -96,9 +96,9 @@ class GgufUploadItem(ctypes.Structure):
 class GgufPeerOut(ctypes.Structure):
     """Mirror of GgufPeerOut (include/gguf_ops.h)."""
 
-    _fields_ = [("y", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8), ("state", ctypes.c_void_p),
+    _fields_ = [("stage", (ctypes.c_void_p * 8) * 2), ("y", ctypes.c_void_p), ("state", ctypes.c_void_p),
                 ("world", ctypes.c_int), ("rank", ctypes.c_int), ("n_total", ctypes.c_int64), ("row0", ctypes.c_int64),
-                ("ctas", ctypes.c_int32)]
+                ("ctas", ctypes.c_int32), ("r_max", ctypes.c_int32)]
 
 
 class GgufPeerReduce(ctypes.Structure):

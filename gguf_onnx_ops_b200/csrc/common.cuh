@@ -146,18 +146,45 @@ __device__ __forceinline__ uint32_t ldg32(const void* p) { return __ldg(reinterp
 // ---------------------------------------------------------------------------------------------
 constexpr int kMaxPeers = 8;
 
-// Output of one shard of a row-split GEMV: every value is stored into the full-size y of every
-// GPU of the group (peer pointers from CUDA IPC, NVLink stores), then an arrival count makes the
-// launch complete only when every peer's shard has landed in this GPU's y.
+// Output of one shard of a row-split GEMV.  Every y value travels as one 32-bit word: the bf16
+// bits in the low half and the call's tag (call number mod 2^16) in the high half, stored into the
+// staging buffer of every GPU of the group (peer pointers from CUDA IPC, NVLink stores; one buffer
+// per call parity, since a peer can be one call ahead).  A 32-bit store is seen whole or not at all,
+// so a word whose tag is this call's is this call's value: no fence and no flag is needed.  After
+// its tiles each CTA converts its slice of this GPU's staging buffer into y, waiting (bounded) for
+// words that still carry an older tag; the launch therefore ends only when the whole y is present.
 struct PeerOut {
-  bf16* y[kMaxPeers];          // y of GPU p: [R, ld] bf16 (this shard's rows start at row0)
-  uint32_t* flags[kMaxPeers];  // arrival counters of GPU p: [kMaxPeers], slot q = CTAs of GPU q arrived (cumulative)
-  uint32_t* state;             // this GPU: [0] = completed calls
+  uint32_t* stage[2][kMaxPeers];  // staging buffer of GPU p for calls of parity c: [r_max, ld] words
+  bf16* y;                        // this GPU's output: [R, ld] bf16
+  unsigned long long* state;      // this GPU: CTAs of row-split launches started so far
   int npeer, rank, ld, row0;
-  int vec;                     // 1: every y[p] 16-byte aligned, ld and row0 multiples of 8 (16-byte stores)
-  int ctas;                    // CTAs every GPU of the group launches per call (the same on every GPU)
+  int vec;                        // 1: ld and row0 multiples of 8 and every buffer 16-byte aligned
+  int ctas;                       // CTAs every GPU of the group launches per call (the same on every GPU)
 };
 
+// The call number of this launch (1, 2, ...) from this GPU's count of row-split CTAs started: every
+// call of the group launches po.ctas CTAs and each CTA counts itself once.  Thread 0 calls it before
+// the CTA's griddepcontrol.launch_dependents (and uses the result before the CTA's first barrier): a
+// dependent launch starts only once every CTA of its predecessor has passed launch_dependents, so
+// all of the previous call's counts precede this call's.
+__device__ __forceinline__ uint32_t peer_call(const PeerOut& po) {
+  const unsigned long long before = atomicAdd(po.state, 1ull);
+  return static_cast<uint32_t>(before / static_cast<unsigned long long>(po.ctas)) + 1u;
+}
+
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -166,66 +193,79 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void red_relaxed_sys_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
-// y[col, row] of this shard (row local to the shard) into every GPU's output.
-__device__ __forceinline__ void peer_store(const PeerOut& po, int col, int row, bf16 v) {
+// y[col, row] of this shard (row local to the shard) into every GPU's staging buffer.
+__device__ __forceinline__ void peer_store(const PeerOut& po, uint32_t call, int col, int row, bf16 v) {
   const int64_t off = static_cast<int64_t>(col) * po.ld + po.row0 + row;
+  const uint32_t w = static_cast<uint32_t>(__bfloat16_as_ushort(v)) | (call << 16);
+  uint32_t* const* st = po.stage[call & 1u];
 #pragma unroll 1
-  for (int p = 0; p < po.npeer; ++p) po.y[p][off] = v;
+  for (int p = 0; p < po.npeer; ++p) st[p][off] = w;
 }
 
 // The 16 y values of one activation row of a full 16-row tile (lane i of a 16-lane half-warp holds
-// row i's value; both halves of the warp may hold different activation rows) into every GPU's y with
-// 16-byte stores: a shuffle butterfly packs 8 consecutive values into lanes 0 and 8 of each half, which
-// then store to each peer.  All 32 lanes call it (`v` of the lanes that hold no value is ignored when
-// `ok` is false for that half); xr / row of the half's lane 0.
-__device__ __forceinline__ void peer_store_tile16(const PeerOut& po, bf16 v, bool ok, int xr, int row) {
+// row i's value; both halves of the warp may hold different activation rows) into every GPU's
+// staging buffer with 16-byte stores: lanes 0, 4, 8, 12 of each half gather four tagged words by
+// shuffles and store them to each peer.  All 32 lanes call it (`ok` false: the half holds no
+// activation row); xr / row of the half's lane 0.
+__device__ __forceinline__ void peer_store_tile16(const PeerOut& po, uint32_t call, bf16 v, bool ok, int xr, int row) {
   const int lane = threadIdx.x & 31, li = lane & 15;
-  uint32_t w = static_cast<uint32_t>(__bfloat16_as_ushort(v));
-  w |= __shfl_down_sync(0xffffffffu, w, 1) << 16;  // even lanes: values i, i + 1
-  const uint32_t w1 = __shfl_down_sync(0xffffffffu, w, 2);
-  const uint32_t w2 = __shfl_down_sync(0xffffffffu, w, 4), w3 = __shfl_down_sync(0xffffffffu, w1, 4);
-  // lanes 0 and 8 of each half: (w, w1, w2, w3) = values li .. li + 7
+  const uint32_t w = static_cast<uint32_t>(__bfloat16_as_ushort(v)) | (call << 16);
+  const uint32_t w1 = __shfl_down_sync(0xffffffffu, w, 1), w2 = __shfl_down_sync(0xffffffffu, w, 2);
+  const uint32_t w3 = __shfl_down_sync(0xffffffffu, w, 3);
   const int src_xr = __shfl_sync(0xffffffffu, xr, lane & 16), src_row = __shfl_sync(0xffffffffu, row, lane & 16);
   const bool src_ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, lane & 16) != 0;
-  if (src_ok && (li & 7) == 0) {
+  if (src_ok && (li & 3) == 0) {
     const int64_t off = static_cast<int64_t>(src_xr) * po.ld + po.row0 + src_row + li;
     const uint4 q = make_uint4(w, w1, w2, w3);
+    uint32_t* const* st = po.stage[call & 1u];
 #pragma unroll 1
-    for (int p = 0; p < po.npeer; ++p) *reinterpret_cast<uint4*>(po.y[p] + off) = q;
+    for (int p = 0; p < po.npeer; ++p) *reinterpret_cast<uint4*>(st[p] + off) = q;
   }
 }
 
-// Called by one thread per CTA after the CTA's last peer store (and a barrier over the threads that
-// stored).  Every CTA makes its stores visible system-wide (one system-scope fence) and then counts
-// itself as arrived at every GPU of the group (slot `rank` of each peer's arrival counters; the
-// counters only grow, so nothing has to be reset between calls).  CTA 0 then waits, bounded, until
-// every GPU's slot in its own counters holds calls * ctas: every CTA of every GPU, this call
-// included, has arrived, so the whole y is present here when the launch ends.  Must run after
-// griddepcontrol.wait (CTA 0 of the previous launch updates state[0] last).  A peer can be at most
-// one call ahead (it cannot finish call e + 1 before this GPU's CTAs of call e + 1 arrive), so the
-// counts compared below are at most one call's CTAs apart and the 32-bit difference is exact.
-__device__ __forceinline__ void peer_complete(const PeerOut& po) {
-  __threadfence_system();
-  for (int p = 0; p < po.npeer; ++p) red_relaxed_sys_add(po.flags[p] + po.rank, 1u);
-  if (blockIdx.x != 0) return;
-  const uint32_t calls = *reinterpret_cast<volatile uint32_t*>(po.state) + 1u;
-  const uint32_t target = calls * static_cast<uint32_t>(po.ctas);
-  const uint32_t* mine = po.flags[po.rank];
+// After the CTA's tiles (all of its stores issued): threads tid .. of nthr convert this CTA's slice of
+// this GPU's staging buffer ([R, ld] words, the slices split evenly over the grid) into y, re-reading
+// a word until it carries this call's tag (bounded: on timeout the site is recorded, the wait
+// stops for the rest of the slice and y holds stale values).
+__device__ __forceinline__ void peer_gather(const PeerOut& po, uint32_t call, int R, int tid, int nthr) {
+  const uint32_t* src = po.stage[call & 1u][po.rank];
+  const uint32_t tag = call & 0xFFFFu;
+  const int64_t total = static_cast<int64_t>(R) * po.ld;
   const uint64_t t0 = global_timer_ns();
-  for (int p = 0; p < po.npeer; ++p) {
-    while (static_cast<int32_t>(ld_acquire_sys(mine + p) - target) < 0) {
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        record_device_error(kSitePeerWait);
-        break;
+  bool late = false;
+  if (po.vec) {  // four words -> four bf16 per step
+    const int64_t n4 = total / 4;
+    const int64_t lo = n4 * blockIdx.x / gridDim.x, hi = n4 * (blockIdx.x + 1) / gridDim.x;
+    for (int64_t i = lo + tid; i < hi; i += nthr) {
+      uint4 q = ld_relaxed_sys_v4(src + 4 * i);
+      while (!late && ((q.x >> 16) != tag || (q.y >> 16) != tag || (q.z >> 16) != tag || (q.w >> 16) != tag)) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          late = true;
+          record_device_error(kSitePeerWait);
+          break;
+        }
+        __nanosleep(32);
+        q = ld_relaxed_sys_v4(src + 4 * i);
       }
-      __nanosleep(32);
+      *reinterpret_cast<uint2*>(po.y + 4 * i) = make_uint2((q.x & 0xFFFFu) | (q.y << 16), (q.z & 0xFFFFu) | (q.w << 16));
+    }
+  } else {
+    const int64_t lo = total * blockIdx.x / gridDim.x, hi = total * (blockIdx.x + 1) / gridDim.x;
+    for (int64_t i = lo + tid; i < hi; i += nthr) {
+      uint32_t q = ld_relaxed_sys(src + i);
+      while (!late && (q >> 16) != tag) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          late = true;
+          record_device_error(kSitePeerWait);
+          break;
+        }
+        __nanosleep(32);
+        q = ld_relaxed_sys(src + i);
+      }
+      po.y[i] = __ushort_as_bfloat16(static_cast<unsigned short>(q & 0xFFFFu));
     }
   }
-  *reinterpret_cast<volatile uint32_t*>(po.state) = calls;
 }
 
 // Sum across GPUs of an f32 [R, H] partial (expert-parallel MoeVerify): every GPU stores its

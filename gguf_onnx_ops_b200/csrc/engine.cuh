@@ -298,8 +298,10 @@ __global__ void __launch_bounds__((KW + 1) * 32, 2) engine_kernel(const __grid_c
   int nitems;
   const int* s_uexp = nullptr;
   const int* s_pair = nullptr;
+  __shared__ uint32_t s_call;  // row-split: this launch's call number (its tag)
   if constexpr (MODE == kModeDense) {
     nitems = a.tiles;
+    if (a.po.npeer && threadIdx.x == 0) s_call = peer_call(a.po);  // before launch_dependents: see peer_call
     __syncthreads();
     pdl_launch_dependents();
   } else {
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 2) engine_kernel(const __grid_c
       const int row = tile * 16 + rl;
       if (row >= a.rows || col >= a.R) continue;
       if constexpr (MODE == kModeDense) {
-        if (a.po.npeer) peer_store(a.po, col, row, __float2bfloat16(v * post));
+        if (a.po.npeer) peer_store(a.po, s_call, col, row, __float2bfloat16(v * post));
         else reinterpret_cast<bf16*>(a.y)[static_cast<int64_t>(col) * a.rows + row] = __float2bfloat16(v * post);
       } else {
         const int p = s_pair[u * 8 + col];
@@ -526,7 +528,7 @@ __global__ void __launch_bounds__((KW + 1) * 32, 2) engine_kernel(const __grid_c
     named_bar_sync(1, KW * 32);
   }
   if constexpr (MODE == kModeDense) {
-    if (a.po.npeer && threadIdx.x == 0) peer_complete(a.po);  // stores are behind the last barrier
+    if (a.po.npeer) peer_gather(a.po, s_call, a.R, threadIdx.x, KW * 32);  // the whole y, from the staging buffer
   }
 }
 

@@ -36,6 +36,7 @@ namespace {
 thread_local std::string t_last_error;
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_fast{1};  // specialised kernels (R = 1 paths); 0 forces the generic engine
+constexpr bool kQ8SmallN = true;  // Q8_0 R <= 4 at K = 4096 with at most two tiles per SM: one tile per CTA
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -100,6 +101,31 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// A cooperative launch (every CTA resident at once, grid-wide barriers allowed), with programmatic
+// dependent launch where the runtime accepts the pair, else without it.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl.load() ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess && cfg.numAttrs == 2) {
+    (void)cudaGetLastError();
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  }
+  return e;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -401,7 +427,12 @@ int run_slice_iq2_i8(const void* x, const void* w, void* y, int N, int K, cudaSt
   static std::atomic<uint64_t> done{0};
   auto kern = slice_iq2_i8_kernel<kW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
+  const int grid = std::min(a.tiles, sms);
+  // a last round of at most grid / 2 tiles runs as half tiles on twice as many CTAs
+  const int rem = a.tiles % grid;
+  a.full_items = (rem > 0 && 2 * rem <= grid) ? a.tiles - rem : a.tiles;
+  a.items = a.full_items + 2 * (a.tiles - a.full_items);
+  cudaError_t e = launch(kern, dim3(grid), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("single-row GEMV launch", e);
   return GGUF_OK;
 }
@@ -453,8 +484,9 @@ int try_iq2_rows(const void* x, const void* w, void* y, int R, int N, int K, cud
 }
 
 // Q8_0 2 <= R <= 4 * kNR on the integer tensor cores (slice_q8_i8_rows.cuh): 16 whole rows per
-// stage at pitch row bytes + 16, two or more stages.
-template <int kW, int kNR, int kSPW = 1>
+// stage at pitch row bytes + 16, two or more stages; kMinB = 2: one stage, one tile per CTA, two
+// CTAs per SM (small N).
+template <int kW, int kNR, int kSPW = 1, int kMinB = 1>
 int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s,
                          const PeerOut* po) {
   SliceArgs a = {};
@@ -470,18 +502,20 @@ int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, in
   a.stride = a.row_bytes + 16;
   a.stage_bytes = (16 * a.stride + 127) & ~127;
   const int red_per_stage = kW * 4 * kNR * 16 * 4 + 4;  // reduction slot + counter
-  a.stages = std::min(4, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
-  if (a.stages < 2) return -1;  // does not fit: the caller falls back to the engine
+  a.stages = kMinB > 1 ? 1 : std::min(4, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < (kMinB > 1 ? 1 : 2)) return -1;  // does not fit: the caller falls back to the engine
   a.off_stage = 0;
   a.off_red = a.stages * a.stage_bytes;
   a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
   const size_t smem = a.off_bar + 2 * a.stages * 8;
+  if (kMinB > 1 && smem * kMinB > static_cast<size_t>(kSmemBudgetMax)) return -1;
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   static std::atomic<uint64_t> done{0};
-  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW>;
+  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW, kLayQ8, kMinB>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  const int grid = a.po.npeer ? a.po.ctas : std::min(a.tiles, sms);  // row-split: the group's CTA count
+  // row-split: the group's CTA count; one tile per CTA: every tile
+  const int grid = a.po.npeer ? a.po.ctas : (kMinB > 1 ? a.tiles : std::min(a.tiles, sms));
   cudaError_t e = launch(kern, dim3(grid), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row Q8_0 GEMV launch", e);
   return GGUF_OK;
@@ -498,6 +532,12 @@ int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cuda
   if (g_fast.load() != 1 || R < 1 || R > 16) return -1;
   if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<8, 4, 2>(x, w, y, R, N, K, s, po) : -1;
   const bool two = R > 4;
+  if (!po && !two && K == 4096 && kQ8SmallN) {
+    int sms = 0, rc;
+    if ((rc = current_sms(&sms))) return rc;
+    // small N (C0: 256 tiles): one tile per CTA, two CTAs per SM
+    if ((N + 15) / 16 <= 2 * sms) return run_slice_q8_i8_rows<8, 1, 2, 2>(x, w, y, R, N, K, s, po);
+  }
   switch (K) {
     case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s, po);
     case 4096: return two ? run_slice_q8_i8_rows<8, 2, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s, po);
@@ -909,7 +949,8 @@ int gguf_relu2(const void* x, void* y, int64_t n, void* stream) {
 namespace gguf_b200 {
 namespace {
 // MoeVerify iq2=3 as: zero the phase counters (first 4P bytes of out, moe_zero_kernel), one fused persistent kernel
-// (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.
+// (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.  One row on one device: a single cooperative
+// launch of the fused kernel does all three.
 int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w, void* out,
                   void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s,
                   const PeerReduce* ep = nullptr, int expert_offset = 0) {
@@ -947,22 +988,42 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
-  cudaError_t e = launch(moe_zero_kernel, dim3(1), dim3(128), 0, s, static_cast<int*>(out), P);
-  if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
+  cudaError_t e;
   static std::atomic<uint64_t> done{0};
+  if (R == 1 && g_fast.load() == 1 && !ep) {
+    // one row, one device: a single cooperative launch; grid-wide barriers take the place of the
+    // per-expert counters (no zeroing kernel) and the weighted sum runs at its end (no finalize kernel)
+    MoeFusedArgs b = a;
+    b.off_stage = kI8Lut;
+    b.off_red = b.off_stage + kMoeR1Teams * 2 * a.stage_bytes;
+    b.off_bar = b.off_red + kMoeR1Teams * 2 * kMoeTeamWarps * 16 * 4;
+    b.off_grp = b.off_bar + kMoeR1Teams * 4 * 8 + kMoeR1Teams * 2 * 4;  // mbarriers, then the slot counters
+    b.wts = weights;
+    b.out = static_cast<bf16*>(out);
+    const size_t smem1 = b.off_grp + grp;
+    if (smem1 > static_cast<size_t>(kSmemBudgetMax))
+      return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
+    static std::atomic<uint64_t> donec{0};
+    if ((rc = ensure_smem(moe_r1_i8_kernel<true>, smem1, donec))) return rc;
+    e = launch_coop(moe_r1_i8_kernel<true>, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
+    if (e != cudaSuccess) return cuda_fail("MoeVerify cooperative launch", e);
+    return GGUF_OK;
+  }
+  e = launch(moe_zero_kernel, dim3(1), dim3(128), 0, s, static_cast<int*>(out), P);
+  if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
   if (R == 1 && g_fast.load() == 1) {
     // one row: the integer single-row decode; tables at offset 0 and a smaller reduction buffer
     MoeFusedArgs b = a;
     b.off_stage = kI8Lut;
     b.off_red = b.off_stage + kMoeR1Teams * 2 * a.stage_bytes;
     b.off_bar = b.off_red + kMoeR1Teams * 2 * kMoeTeamWarps * 16 * 4;
-    b.off_grp = b.off_bar + kMoeR1Teams * 4 * 8;
+    b.off_grp = b.off_bar + kMoeR1Teams * 4 * 8 + kMoeR1Teams * 2 * 4;  // mbarriers, then the slot counters
     const size_t smem1 = b.off_grp + grp;
     if (smem1 > static_cast<size_t>(kSmemBudgetMax))
       return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
     static std::atomic<uint64_t> done1{0};
-    if ((rc = ensure_smem(moe_r1_i8_kernel, smem1, done1))) return rc;
-    e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
+    if ((rc = ensure_smem(moe_r1_i8_kernel<false>, smem1, done1))) return rc;
+    e = launch(moe_r1_i8_kernel<false>, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   } else if (g_fast.load() == 1) {
     // 2..8 rows: the integer decode shared by every pair of an expert (moe_pairs_kernel)
@@ -970,7 +1031,7 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     b.off_stage = kI8Lut;
     b.off_red = b.off_stage + kMoePTeams * 2 * a.stage_bytes;
     b.off_bar = b.off_red + kMoePTeams * 2 * kMoeTeamWarps * 8 * 16 * 4;
-    b.off_grp = b.off_bar + kMoePTeams * 4 * 8;
+    b.off_grp = b.off_bar + kMoePTeams * 4 * 8 + kMoePTeams * 2 * 4;  // mbarriers, then the slot counters
     b.off_zf = (b.off_grp + grp + 127) & ~127;
     const size_t smem2 = b.off_zf + static_cast<size_t>(R) * (H / 256) * kZFragBytes + kZeroBytes + kMaxPairs * 9 * 4;
     if (smem2 > static_cast<size_t>(kSmemBudgetMax)) {  // large I: the bf16-decode kernel's smaller tables
@@ -1267,24 +1328,28 @@ int gguf_gemv_rowsplit(int type, const void* x, const void* w_shard, const float
   if (!x || !w_shard || !out) return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: null pointer");
   if (out->world < 1 || out->world > kMaxPeers || out->rank < 0 || out->rank >= out->world)
     return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 1 <= world <= 8 and 0 <= rank < world");
-  if (!out->state || rows < 1 || out->row0 < 0 || out->row0 + rows > out->n_total || !int_range(out->n_total))
-    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 0 <= row0, row0 + rows <= n_total and a state array");
-  for (int p = 0; p < out->world; ++p)
-    if (!out->y[p] || !out->flags[p]) return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: null peer buffer");
-  if (R < 1 || R > 16 || K <= 0 || !int_range(K) || !aligned(w_shard, 16) || !aligned(x, 16))
-    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 1..16 rows and 16-byte aligned x and w");
+  if (!out->state || !out->y || rows < 1 || out->row0 < 0 || out->row0 + rows > out->n_total || !int_range(out->n_total))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 0 <= row0, row0 + rows <= n_total, y and a state counter");
+  for (int c = 0; c < 2; ++c)
+    for (int p = 0; p < out->world; ++p)
+      if (!out->stage[c][p] || !aligned(out->stage[c][p], 4))
+        return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: null or misaligned staging buffer");
+  if (R < 1 || R > 16 || R > out->r_max || K <= 0 || !int_range(K) || !aligned(w_shard, 16) || !aligned(x, 16) ||
+      !aligned(out->y, 2) || !aligned(out->state, 8))
+    return fail(GGUF_ERR_INVALID_ARGUMENT, "rowsplit GEMV: needs 1..16 rows (<= r_max) and 16-byte aligned x and w");
   PeerOut po = {};
-  for (int p = 0; p < out->world; ++p) {
-    po.y[p] = static_cast<bf16*>(out->y[p]);
-    po.flags[p] = out->flags[p];
-  }
+  po.vec = out->n_total % 8 == 0 && out->row0 % 8 == 0 && aligned(out->y, 8);
+  for (int c = 0; c < 2; ++c)
+    for (int p = 0; p < out->world; ++p) {
+      po.stage[c][p] = out->stage[c][p];
+      po.vec = po.vec && aligned(out->stage[c][p], 16);
+    }
+  po.y = static_cast<bf16*>(out->y);
   po.state = out->state;
   po.npeer = out->world;
   po.rank = out->rank;
   po.ld = static_cast<int>(out->n_total);
   po.row0 = static_cast<int>(out->row0);
-  po.vec = out->n_total % 8 == 0 && out->row0 % 8 == 0;
-  for (int p = 0; p < out->world; ++p) po.vec = po.vec && aligned(out->y[p], 16);
   po.ctas = out->ctas;
   if (po.ctas == 0 && current_sms(&po.ctas)) return GGUF_ERR_CUDA;
   if (po.ctas < 1 || po.ctas > (1 << 16))

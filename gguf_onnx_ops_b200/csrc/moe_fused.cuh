@@ -23,6 +23,8 @@
 // before this kernel; `out` is only written by the finalize kernel that follows).
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "engine.cuh"
 #include "slice_iq2_i8.cuh"
 
@@ -44,7 +46,36 @@ struct MoeFusedArgs {
   int expert_offset;  // expert parallelism: global id of local expert 0 (idx holds global ids)
   int off_stage, off_red, off_bar, off_grp;
   int off_zf;         // moe_pairs_kernel: the z fragments of every activation row (kZFragBytes per row and slice)
+  const float* wts;   // cooperative moe_r1_i8_kernel: the router weights [R, topk] and the output [R, H]
+  bf16* out;
 };
+
+// out[t, n] = bf16(sum_j w[t, j] * part[t * topk + j, n]) in fp32, j ascending, pairs with an expert
+// id outside [0, E) skipped (src/bolt_ops.cu:627-662); float4 groups i = gid, gid + gstride, ...
+// of the R x H / 4 outputs (part read through L2: written by the same launch).
+__device__ __forceinline__ void moe_finalize_rows(const float* part, const float* w, const int32_t* idx, int topk, int H,
+                                                  int E, int R, bf16* out, int gid, int gstride) {
+  const int per_row = H / 4;
+  for (int i = gid; i < R * per_row; i += gstride) {
+    const int t = i / per_row, v = i % per_row;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int j = 0; j < topk; ++j) {
+      const int pr = t * topk + j;
+      const int e = __ldg(idx + pr);
+      if (e < 0 || e >= E) continue;
+      const float wk = __ldg(w + pr);
+      const float4 pv = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(pr) * H) + v);
+      a0 += wk * pv.x;
+      a1 += wk * pv.y;
+      a2 += wk * pv.z;
+      a3 += wk * pv.w;
+    }
+    uint2 o;
+    o.x = pack_bf16x2(a0, a1);
+    o.y = pack_bf16x2(a2, a3);
+    reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * H)[v] = o;
+  }
+}
 
 constexpr int kMoeDoneWaitSite = 4;
 constexpr int kMoeTeams = 4, kMoeTeamWarps = 4, kMoeWarps = kMoeTeams * kMoeTeamWarps;
@@ -224,6 +255,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
 // converting the pair's h slice (read through L2) right before each.  Work split, staging, phase
 // order and outputs are those of moe_fused_kernel.  Tables (48 KB) sit at shared offset 0.
 // ---------------------------------------------------------------------------------------------
+template <bool kCoop>
 __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const MoeFusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -231,6 +263,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
   const bool leader = tw == 0 && lane == 0;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
   uint64_t* empty = full + 2;
+  int* cnt = reinterpret_cast<int*>(smem + a.off_bar + kMoeR1Teams * 4 * 8) + team * 2;  // [2] arrivals per slot
   uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
   float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 16;  // [2][warps][16]
   int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
@@ -239,6 +272,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
     for (int s = 0; s < 2; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kMoeTeamWarps);
+      cnt[s] = 0;
     }
     fence_mbar_init();
   }
@@ -293,15 +327,15 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
   // z fragments of this warp's phase-1 slice (the single row's z, slice tw of H = 1024)
   I8XFrag zf;
   i8_x_frag(ldg128(a.z + tw * 256 + 8 * lane), zf);
-  const int bar_id = 1 + team, bar_n = kMoeTeamWarps * 32;
   const int slices2 = a.I / 256;
-  uint32_t k = 0;
-  for (int q = first; q < nitems; q += teams, ++k) {
+  // The warps of a team meet only through counters (as in moe_pairs_kernel): the last warp to
+  // count itself into an item's slot sums it, stores the row, publishes and refills the stage.
+  auto body = [&](int q, uint32_t k) {
     int phase, u, tile;
     item_of(q, phase, u, tile);
     const int p = s_pair[u * 8];  // the pair of row 0 (R = 1)
-    if (phase == 2) {  // every phase-1 tile of expert u must be in h
-      if (leader) {
+    if (!kCoop && phase == 2) {  // every phase-1 tile of expert u must be in h (each warp acquires)
+      if (lane == 0) {
         const uint64_t t0 = global_timer_ns();
         int v;
         for (;;) {
@@ -311,10 +345,10 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
             record_device_error(kMoeDoneWaitSite);
             break;
           }
-          __nanosleep(128);
+          __nanosleep(64);
         }
       }
-      named_bar_sync(bar_id, bar_n);
+      __syncwarp();
     }
     const int s = static_cast<int>(k & 1u);
     mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
@@ -354,38 +388,62 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
         acc1 += b1;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-    // team reduction of the 16 rows; slot (k & 1) is rewritten two items later, after a barrier
+    // team reduction of the 16 rows.  Slot (k & 1) is rewritten two items later, after the stage
+    // was refilled, which the last arriver of this item does after summing the slot.
     float* rb = red + s * kMoeTeamWarps * 16;
     if (t == 0) {
       rb[tw * 16 + g] = acc0;
       rb[tw * 16 + g + 8] = acc1;
     }
-    named_bar_sync(bar_id, bar_n);
-    const int ti = tw * 32 + lane;
-    if (ti < 16 && p >= 0) {
-      const float v = (rb[ti] + rb[16 + ti]) + (rb[32 + ti] + rb[48 + ti]);
-      const float vb = round_bf16(v);
-      if (phase == 1) {
-        const float r = fmaxf(vb, 0.f);
-        a.h[static_cast<int64_t>(p) * a.I + tile * 16 + ti] = __float2bfloat16(r * r);
-      } else {
-        a.part[static_cast<int64_t>(p) * a.H + tile * 16 + ti] = vb;
+    __syncwarp();  // orders the lanes' slot writes and stage reads before lane 0's arrivals below
+    int last = 0;
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      last = atom_add_acq_rel_cta(&cnt[s], 1) == kMoeTeamWarps - 1;
+    }
+    if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this item are in the slot
+      if (lane < 16 && p >= 0) {
+        const float v = (rb[lane] + rb[16 + lane]) + (rb[32 + lane] + rb[48 + lane]);
+        const float vb = round_bf16(v);
+        if (phase == 1) {
+          const float r = fmaxf(vb, 0.f);
+          a.h[static_cast<int64_t>(p) * a.I + tile * 16 + lane] = __float2bfloat16(r * r);
+        } else {
+          a.part[static_cast<int64_t>(p) * a.H + tile * 16 + lane] = vb;
+        }
+      }
+      __syncwarp();  // every lane's row stores (and slot reads) before lane 0's publish / refill
+      if (lane == 0) {
+        cnt[s] = 0;
+        if (!kCoop && phase == 1) {  // publish: this tile of h is written
+          __threadfence();
+          atomicAdd(a.done + u, 1);
+        }
+        if (q + 2 * teams < nitems) {
+          fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
+          fetch(q + 2 * teams, k + 2u);
+        }
       }
     }
-    if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);
-    if (phase == 1) {  // publish: this tile of h is written (every team thread is past its store)
-      named_bar_sync(bar_id, bar_n);
-      if (leader) {
-        __threadfence();
-        atomicAdd(a.done + u, 1);
-      }
-    }
+  };
+  if constexpr (!kCoop) {
+    uint32_t k = 0;
+    for (int q = first; q < nitems; q += teams, ++k) body(q, k);
+  } else {
+    // cooperative launch: grid-wide barriers order the phases, and the weighted sum over the top-k
+    // experts (the finalize step) runs here after the second one
+    int q = first;
+    uint32_t k = 0;
+    for (; q < n1; q += teams, ++k) body(q, k);
+    cooperative_groups::this_grid().sync();  // every h row is written (phase-2 weights already in flight)
+    for (; q < nitems; q += teams, ++k) body(q, k);
+    cooperative_groups::this_grid().sync();  // every part row is written
+    moe_finalize_rows(a.part, a.wts, a.idx, a.topk, a.H, a.E, a.R, a.out,
+                      static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x), static_cast<int>(gridDim.x * blockDim.x));
   }
 }
 
@@ -504,6 +562,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   const bool leader = tw == 0 && lane == 0;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
   uint64_t* empty = full + 2;
+  int* cnt = reinterpret_cast<int*>(smem + a.off_bar + kMoePTeams * 4 * 8) + team * 2;  // [2] arrivals per slot
   uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
   float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 8 * 16;  // [2][warps][8 pairs][16]
   int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
@@ -516,6 +575,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
     for (int s = 0; s < 2; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kMoeTeamWarps);
+      cnt[s] = 0;
     }
     fence_mbar_init();
   }
@@ -584,15 +644,17 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   __syncthreads();
 
   const int g = lane >> 2, t = lane & 3;
-  const int bar_id = 1 + team, bar_n = kMoeTeamWarps * 32;
+  // The four warps of a team meet only through counters: each warp adds its partial sums to the
+  // item's reduction slot and counts itself in (acquire-release); the last one to arrive sums the
+  // slot in warp order, stores the rows, publishes phase-1 tiles and refills the stage two items on.
   uint32_t k = 0;
   for (int q = first; q < nitems; q += teams, ++k) {
     int phase, u, tile;
     item_of(q, phase, u, tile);
     const int np = s_np[u];
     const int* pl = s_plist + u * 8;
-    if (phase == 2) {  // every phase-1 tile of expert u must be in h
-      if (leader) {
+    if (phase == 2) {  // every phase-1 tile of expert u must be in h (each warp acquires for itself)
+      if (lane == 0) {
         const uint64_t t0 = global_timer_ns();
         int v;
         for (;;) {
@@ -602,18 +664,19 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
             record_device_error(kMoeDoneWaitSite);
             break;
           }
-          __nanosleep(128);
+          __nanosleep(64);
         }
       }
-      named_bar_sync(bar_id, bar_n);
+      __syncwarp();
     }
     const int s = static_cast<int>(k & 1u);
-    // this warp's partial row sums per pair: slot (k & 1) is rewritten two items later, after a barrier
+    mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
+    // this warp's partial row sums per pair.  Slot (k & 1) was summed by the last arriver of item
+    // k - 2 before it refilled this stage, so it is free once the stage is full again.
     float* rbuf = red + s * kMoeTeamWarps * 8 * 16;
     float* mine = rbuf + tw * 8 * 16;
     for (int i = lane; i < np * 16; i += 32) mine[i] = 0.f;
     __syncwarp();
-    mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
     const uint8_t* st = stage0 + s * a.stage_bytes;
     const uint32_t rb = static_cast<uint32_t>(phase == 1 ? a.rb1 : a.rb2);
     const uint32_t r0 = static_cast<uint32_t>(g) * rb, r1 = static_cast<uint32_t>(g + 8) * rb;
@@ -662,28 +725,37 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    named_bar_sync(bar_id, bar_n);
-    for (int ti = tw * 32 + lane; ti < np * 16; ti += kMoeTeamWarps * 32) {
-      const int i = ti >> 4, rl = ti & 15;
-      const int p = pl[i] & 0xFFFF;
-      // fixed order: warps 0 + 1, then 2 + 3
-      const float v = (rbuf[ti] + rbuf[128 + ti]) + (rbuf[256 + ti] + rbuf[384 + ti]);
-      const float vb = round_bf16(v);
-      if (phase == 1) {
-        const float rr = fmaxf(vb, 0.f);
-        a.h[static_cast<int64_t>(p) * a.I + tile * 16 + rl] = __float2bfloat16(rr * rr);
-      } else {
-        a.part[static_cast<int64_t>(p) * a.H + tile * 16 + rl] = vb;
-      }
+    __syncwarp();  // orders the lanes' slot writes and stage reads before lane 0's arrivals below
+    int last = 0;
+    if (lane == 0) {
+      mbar_arrive(&empty[s]);
+      last = atom_add_acq_rel_cta(&cnt[s], 1) == kMoeTeamWarps - 1;
     }
-    if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);
-    if (phase == 1) {  // publish: this tile of h is written (every team thread is past its store)
-      named_bar_sync(bar_id, bar_n);
-      if (leader) {
-        __threadfence();
-        atomicAdd(a.done + u, 1);
+    if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this item are in the slot
+      for (int ti = lane; ti < np * 16; ti += 32) {
+        const int i = ti >> 4, rl = ti & 15;
+        const int p = pl[i] & 0xFFFF;
+        // fixed order: warps 0 + 1, then 2 + 3
+        const float v = (rbuf[ti] + rbuf[128 + ti]) + (rbuf[256 + ti] + rbuf[384 + ti]);
+        const float vb = round_bf16(v);
+        if (phase == 1) {
+          const float rr = fmaxf(vb, 0.f);
+          a.h[static_cast<int64_t>(p) * a.I + tile * 16 + rl] = __float2bfloat16(rr * rr);
+        } else {
+          a.part[static_cast<int64_t>(p) * a.H + tile * 16 + rl] = vb;
+        }
+      }
+      __syncwarp();  // every lane's row stores (and slot reads) before lane 0's publish / refill
+      if (lane == 0) {
+        cnt[s] = 0;
+        if (phase == 1) {  // publish: this tile of h is written
+          __threadfence();
+          atomicAdd(a.done + u, 1);
+        }
+        if (q + 2 * teams < nitems) {
+          fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
+          fetch(q + 2 * teams, k + 2u);
+        }
       }
     }
   }

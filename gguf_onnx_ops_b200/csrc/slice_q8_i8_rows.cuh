@@ -10,8 +10,8 @@
 // and C column pair (2t, 2t+1) of lane (g, t) is activation row t.  Epilogue per (row, block):
 // y += (256 C_hi + C_lo) * 2^(E - 13) * d, in fp32.  No offset term: the quants are signed.
 //
-// Row-split shards (a.po.npeer > 0): y goes to every GPU of the group with peer stores, and the
-// launch ends once every GPU's shard is present (peer_complete), as in slice_r1_kernel.
+// Row-split shards (a.po.npeer > 0): every y value goes to every GPU of the group as a tagged word
+// (peer_store_tile16), and the launch ends once every GPU's shard is present (peer_gather).
 //
 // Staging: a tile is 16 whole rows (K / 32 * 34 bytes each), one bulk copy per row into a stage
 // whose row pitch is the row bytes + 16, which keeps the eight quads' loads off a common bank (a
@@ -102,8 +102,11 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
 // finish a tile sums the stage's reduction slot in warp order (deterministic), stores y [R, N] and
 // refills the stage (the last-arriver scheme of slice_iq2_i8_kernel).  kSPW = 2 halves the warps
 // and with them the reduction slots, which leaves room for a third stage at eight activation rows.
-template <int kW, int kNR, int kSPW = 1, int kLay = kLayQ8>
-__global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
+// kMinB = 2: one tile per CTA (grid = tiles, one stage), two CTAs per SM, for small N: the CTAs of
+// the next call start on an SM while this call's second CTA there still runs, so their weight tiles
+// stream while this call finishes (one resident CTA per SM serialises the calls' HBM phases).
+template <int kW, int kNR, int kSPW = 1, int kLay = kLayQ8, int kMinB = 1>
+__global__ void __launch_bounds__(kW * 32, kMinB) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
   constexpr bool kSplit = kLay != kLayQ8;
   constexpr int kRX = 4 * kNR;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -112,6 +115,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
   float* red = reinterpret_cast<float*>(smem + a.off_red);  // [stages][kW][kRX][16]
   int* cnt = reinterpret_cast<int*>(red + a.stages * kW * kRX * 16);  // [stages]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ uint32_t s_call;  // row-split: this launch's call number (its tag)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < a.stages; ++s) {
@@ -119,6 +123,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
       cnt[s] = 0;
     }
     fence_mbar_init();
+    if (a.po.npeer) s_call = peer_call(a.po);  // before launch_dependents: see peer_call
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -181,9 +186,9 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
         const bf16 yv = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
         if (vec) {  // row-split shard: 16-byte stores into every GPU's y (warp-uniform branch)
           if (o - lane < 16 * a.R)  // the pass's first half holds an activation row < R
-            peer_store_tile16(a.po, yv, xr < a.R, xr, tile * 16);
+            peer_store_tile16(a.po, s_call, yv, xr < a.R, xr, tile * 16);
         } else if (xr < a.R && row < a.N) {
-          if (a.po.npeer) peer_store(a.po, xr, row, yv);  // row-split shard: into every GPU's y
+          if (a.po.npeer) peer_store(a.po, s_call, xr, row, yv);  // row-split shard: into every GPU's staging
           else a.y[static_cast<int64_t>(xr) * a.N + row] = yv;
         }
       }
@@ -200,10 +205,7 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __gr
       ph ^= 1u;
     }
   }
-  if (a.po.npeer) {  // all-gather completion: every last arriver's stores are behind the barrier
-    __syncthreads();
-    if (threadIdx.x == 0) peer_complete(a.po);
-  }
+  if (a.po.npeer) peer_gather(a.po, s_call, a.R, threadIdx.x, blockDim.x);  // the whole y, from the staging buffer
 }
 
 }  // namespace gguf_b200

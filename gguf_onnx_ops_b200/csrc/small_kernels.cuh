@@ -9,13 +9,25 @@ namespace gguf_b200 {
 // MoeRouteGGUF: one thread-block cluster of kRouteCtas CTAs per block of kRouteRows rows.
 // CTA c of a cluster computes the sigmoid scores of experts [c*E/n, (c+1)*E/n) for the cluster's
 // rows (gate row read once from HBM, rounded to bf16 in registers as src/bolt_ops.cu:441-448;
-// fp32 dot products in a fixed order), writes them to `scores`, then the cluster barrier
-// (release/acquire at cluster scope) makes every CTA's scores visible to the whole cluster and
-// warp w of CTA c selects the top-k of row (cluster row base + c*warps + w): iterative arg-max of
-// score + bias with ties to the lower expert index (src/bolt_ops.cu:459-510).
+// fp32 dot products in a fixed order), writes them to `scores` and, through distributed shared
+// memory, into CTA 0's shared copy; the cluster barrier (release/acquire at cluster scope) makes
+// every CTA's copy visible to CTA 0, whose warp w selects the top-k of row (cluster row base + w)
+// from shared memory: iterative arg-max of score + bias with ties to the lower expert index
+// (src/bolt_ops.cu:459-510).
 // ---------------------------------------------------------------------------------------------
 constexpr int kRouteCtas = 8, kRouteRows = 8, kRouteWarps = 16;
+constexpr int kRouteMaxE = 512;  // experts the router takes (the op contract)
 constexpr int kRoutePre = 4;  // 256-element chunks of a warp's first gate row fetched before the dependency wait
+
+// Shared-memory address of the same variable in CTA 0 of the cluster, and a store to it.
+__device__ __forceinline__ uint32_t map_shared_cta0(const void* p) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+  return r;
+}
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
@@ -30,9 +42,10 @@ __device__ __forceinline__ uint32_t ordered_key(float f) {
 // Top-k of one row by one warp: lane l holds experts l, l + 32, ... (kPer of them).  Each pick is an
 // arg-max of score + bias over the warp with ties to the lower expert index (src/bolt_ops.cu:459-510):
 // one warp max of the ordered keys, then one warp min of the indices holding that key.
+// sr: the row's scores in this CTA's shared memory; bv[i]: the bias of expert lane + 32 i.
 template <int kPer>
-__device__ __forceinline__ void route_select(const float* __restrict__ sr, int row, int E, int topk, float scale,
-                                             const float* __restrict__ bias, int32_t* __restrict__ idx_out,
+__device__ __forceinline__ void route_select(const float* __restrict__ sr, const float (&bv)[kPer], int row, int E,
+                                             int topk, float scale, int32_t* __restrict__ idx_out,
                                              float* __restrict__ w_out) {
   const int lane = threadIdx.x & 31;
   float sc[kPer];
@@ -40,8 +53,8 @@ __device__ __forceinline__ void route_select(const float* __restrict__ sr, int r
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int e = lane + 32 * i;
-    sc[i] = e < E ? __ldcg(sr + e) : 0.f;
-    const float v = e < E ? sc[i] + __ldg(bias + e) : 0.f;
+    sc[i] = e < E ? sr[e] : 0.f;
+    const float v = e < E ? sc[i] + bv[i] : 0.f;
     key[i] = (e < E && v == v) ? ordered_key(v) : 0u;  // 0: below every real key (absent or NaN: never picked)
   }
   int my_idx = -1;
@@ -124,6 +137,16 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
   const int nrows = min(kRouteRows, R - row0);
   const int e_lo = (rank * E) / kRouteCtas, e_hi = ((rank + 1) * E) / kRouteCtas;
   const int e_first = e_lo + warp;
+  // scores of the cluster's rows, gathered in CTA 0's shared memory for the top-k (E <= kRouteMaxE)
+  __shared__ float s_sc[kRouteRows][kRouteMaxE];
+  // bias of the experts a top-k lane owns (lane + 32 i), fetched before the dependency wait
+  constexpr int kPerMax = kRouteMaxE / 32;
+  float bv[kPerMax];
+#pragma unroll
+  for (int i = 0; i < kPerMax; ++i) {
+    const int e = lane + 32 * i;
+    bv[i] = (rank == 0 && e < E) ? __ldg(bias + e) : 0.f;
+  }
   // The gate weights do not depend on the previous kernel: this warp's first row (up to
   // kRoutePre * 256 elements) is in flight before the dependency wait.
   GateChunk<WT> pw[kRoutePre];
@@ -191,17 +214,19 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
       float v = acc[r];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0 && r < nrows) scores[static_cast<int64_t>(row0 + r) * E + e] = 1.0f / (1.0f + expf(-v));
+      if (lane == 0 && r < nrows) {
+        const float sg = 1.0f / (1.0f + expf(-v));
+        scores[static_cast<int64_t>(row0 + r) * E + e] = sg;
+        st_shared_cluster_f32(map_shared_cta0(&s_sc[r][e]), sg);  // CTA 0's copy for the top-k
+      }
     }
   }
-  cluster_sync_all();
-  const int r = rank * kRouteWarps + warp;  // kRouteCtas * kRouteWarps >= kRouteRows
-  if (r >= nrows) return;
-  const int row = row0 + r;
-  const float* sr = scores + static_cast<int64_t>(row) * E;
-  if (E <= 128) route_select<4>(sr, row, E, topk, scale, bias, idx_out, w_out);
-  else if (E <= 256) route_select<8>(sr, row, E, topk, scale, bias, idx_out, w_out);
-  else route_select<16>(sr, row, E, topk, scale, bias, idx_out, w_out);
+  cluster_sync_all();  // every CTA's remote score stores are visible in CTA 0 (release / acquire)
+  if (rank != 0 || warp >= nrows) return;
+  const int row = row0 + warp;
+  if (E <= 128) route_select<4>(s_sc[warp], reinterpret_cast<const float(&)[4]>(bv), row, E, topk, scale, idx_out, w_out);
+  else if (E <= 256) route_select<8>(s_sc[warp], reinterpret_cast<const float(&)[8]>(bv), row, E, topk, scale, idx_out, w_out);
+  else route_select<16>(s_sc[warp], bv, row, E, topk, scale, idx_out, w_out);
 }
 
 // ---------------------------------------------------------------------------------------------

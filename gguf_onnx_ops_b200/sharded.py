@@ -3,16 +3,16 @@
 The reference runs on one GPU; the two sharded patterns here are the row-split GEMV of a large
 output (the Q8 LM head) and -- through the same peer-memory machinery -- its building blocks.
 torch.distributed is the plumbing only: it exchanges CUDA IPC handles once at set-up.  The data
-path is a single kernel per call that computes this GPU's rows and stores them straight into the
-output of every GPU of the group over NVLink, then waits (bounded) for the peers' flags.
+path is a single kernel per call that computes this GPU's rows and stores them straight into a
+staging buffer of every GPU of the group over NVLink (each value tagged with the call number), then
+converts its own staging buffer into y as the tagged words arrive (bounded waits).
 
     shard = shard_rows(n_total, world, rank)          # (row0, rows) of this rank
     op = RowSplitGemv(GGUF_TYPE_Q8_0, w_full[row0:row0 + rows], n_total, row0, K, r_max=16)
     y = op(x)                                          # [R, n_total] bf16, complete on every GPU
 
 Every rank must construct the op and call it the same number of times in the same order.  The
-output alternates between two buffers (a peer may start call e+1 while this GPU still reads the y
-of call e); the returned tensor is valid until the call after next.
+returned tensor is valid until the next call.
 """
 
 from __future__ import annotations
@@ -82,53 +82,56 @@ class RowSplitGemv:
             raise ValueError("at most 8 GPUs per group")
         dev = w_shard.device
         self.r_max = r_max
-        self.y = [torch.empty(r_max, n_total, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-        self.flags = torch.zeros(MAX_PEERS, dtype=torch.int32, device=dev)
-        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        # this GPU's output, and per call parity a staging buffer that every GPU of the group writes
+        # its shard into (32-bit words: bf16 value | call number << 16)
+        self.y = torch.empty(r_max, n_total, dtype=torch.bfloat16, device=dev)
+        self.stage = [torch.zeros(r_max, n_total, dtype=torch.int32, device=dev) for _ in range(2)]
+        self.state = torch.zeros(1, dtype=torch.int64, device=dev)
         torch.cuda.synchronize(dev)
-        # every GPU launches the same number of CTAs per call (the smallest SM count of the group):
-        # each GPU waits until every CTA of every GPU has counted itself in its arrival counters
+        # every GPU launches the same number of CTAs per call (the smallest SM count of the group): a
+        # GPU numbers its calls by counting the CTAs it started
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        mine = [ipc_handle(self.y[0]), ipc_handle(self.y[1]), ipc_handle(self.flags), sms]
+        mine = [ipc_handle(self.stage[0]), ipc_handle(self.stage[1]), sms]
         allh = exchange(mine, group)
-        self.ctas = min(h[3] for h in allh)
-        allh = [h[:3] for h in allh]
+        self.ctas = min(h[2] for h in allh)
         self._opened = []
-        self._po = [_lib.GgufPeerOut(), _lib.GgufPeerOut()]
+        self._po = _lib.GgufPeerOut()
         for p, hs in enumerate(allh):
-            ptrs = []
-            for (h, off), own in zip(hs, (self.y[0], self.y[1], self.flags)):
+            for c in range(2):
                 if p == self.rank:
-                    ptrs.append(own.data_ptr())
+                    self._po.stage[c][p] = self.stage[c].data_ptr()
                 else:
+                    h, off = hs[c]
                     ptr, base = ipc_open(h, off)
                     self._opened.append(base)
-                    ptrs.append(ptr)
-            for b in range(2):
-                self._po[b].y[p] = ptrs[b]
-                self._po[b].flags[p] = ptrs[2]
-        for po in self._po:
-            po.state = self.state.data_ptr()
-            po.world, po.rank = self.world, self.rank
-            po.n_total, po.row0 = n_total, row0
-            po.ctas = self.ctas
-        self.calls = 0
+                    self._po.stage[c][p] = ptr
+        po = self._po
+        po.y = self.y.data_ptr()
+        po.state = self.state.data_ptr()
+        po.world, po.rank = self.world, self.rank
+        po.n_total, po.row0 = n_total, row0
+        po.ctas, po.r_max = self.ctas, r_max
 
-    def __call__(self, x: torch.Tensor, w: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-        """y = x @ W^T over the whole group; `w` optionally replaces the shard (same shape and type)."""
+    def __call__(self, x: torch.Tensor, w: torch.Tensor | None = None, stream=None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        """y = x @ W^T over the whole group; `w` optionally replaces the shard (same shape and type).
+        Returns `out` (bf16 [R, n_total], contiguous) or, without it, a view of this GPU's own output
+        buffer that is valid until the next call."""
         R = x.shape[0]
         if x.dtype != torch.bfloat16 or x.shape[1] != self.K or not 1 <= R <= self.r_max:
             raise ValueError("x must be bf16 [R, K] with R <= r_max")
         w = self.w if w is None else w
         if w.shape != self.w.shape or w.dtype != torch.uint8 or not w.is_contiguous():
             raise ValueError("w must have the shard's shape")
-        b = self.calls & 1
+        if out is not None and (out.dtype != torch.bfloat16 or out.shape != (R, self.n_total) or not out.is_contiguous()):
+            raise ValueError("out must be contiguous bf16 [R, n_total]")
+        y = self.y[:R] if out is None else out
+        self._po.y = y.data_ptr()
         s = (stream or torch.cuda.current_stream()).cuda_stream
         gs = ctypes.c_void_p(self.gscale.data_ptr()) if self.gscale is not None else None
         check(load().gguf_gemv_rowsplit(self.type, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w.data_ptr()), gs,
-                                        ctypes.byref(self._po[b]), R, self.rows, self.K, ctypes.c_void_p(s)))
-        self.calls += 1
-        return self.y[b][:R]
+                                        ctypes.byref(self._po), R, self.rows, self.K, ctypes.c_void_p(s)))
+        return y
 
     def close(self) -> None:
         for base in self._opened:

@@ -226,23 +226,25 @@ GGUF_OPS_API int gguf_moe_verify_iq2_xxs_noalloc(const void* z, const int32_t* i
  * Row-split (tensor-parallel) GEMV with the all-gather fused into the kernel (no counterpart in the
  * reference, which runs on one GPU; meant for LM-head-sized Q8Gemv calls).  GPU `rank` of
  * `world` holds rows [row0, row0 + rows) of W (w_shard, raw GGUF rows) and computes those outputs
- * for all R activation rows; every value is stored directly into the full y [R, n_total] of every
- * GPU of the group (peer pointers opened with gguf_ipc_open, NVLink stores), and the launch ends
- * only when every peer's shard has landed in this GPU's y (every CTA of every GPU counts itself in
- * every GPU's arrival counters after one system-scope fence; one CTA per GPU waits, bounded, for the
- * whole group's count; timeouts are reported through gguf_device_status).  All GPUs of the group must issue the same sequence of calls.
- * Double buffering: a peer that finished call e may start call e+1 while this GPU still reads the
- * y of call e, so consecutive calls must alternate between two y buffers (flags and state are
- * shared by the two).
+ * for all R activation rows.  Every value is stored into the staging buffer of every GPU of the
+ * group (peer pointers opened with gguf_ipc_open, NVLink stores) as one 32-bit word: the bf16 bits
+ * in the low half, the call number mod 2^16 in the high half.  Each GPU converts its own staging
+ * buffer into y, waiting (bounded, timeouts reported through gguf_device_status) for words that do
+ * not carry the current call's number yet; the launch ends only when the whole y [R, n_total] is
+ * on this GPU.  No fence or flag is exchanged: a 32-bit store arrives whole.  All GPUs of the group
+ * must issue the same sequence of calls; a GPU can run one call ahead of another, so there are two
+ * staging buffers, one per call parity.
  */
 typedef struct {
-  void* y[8];           /* y of GPU p (bf16 [R, n_total]); y[rank] = this GPU's own buffer */
-  uint32_t* flags[8];   /* arrival counters of GPU p: uint32 [8], zero-initialised, shared by all calls */
-  uint32_t* state;      /* this GPU: uint32 [2], zero-initialised, shared by all calls */
+  uint32_t* stage[2][8];     /* staging buffer of GPU p for calls of parity c: uint32 [r_max, n_total],
+                                zero-initialised; stage[c][rank] = this GPU's own */
+  void* y;                   /* this GPU's output: bf16 [R, n_total] (rewritten by every call) */
+  unsigned long long* state; /* this GPU: uint64 [1], zero-initialised, shared by all calls */
   int world, rank;
   int64_t n_total, row0;
-  int32_t ctas;         /* CTAs each GPU launches per call: the same value on every GPU of the group;
-                           0 = this GPU's SM count (only when every GPU of the group has the same) */
+  int32_t ctas;              /* CTAs each GPU launches per call: the same value on every GPU of the group;
+                                0 = this GPU's SM count (only when every GPU of the group has the same) */
+  int32_t r_max;             /* activation rows the staging buffers hold (R <= r_max) */
 } GgufPeerOut;
 
 /* type = GGUF_TYPE_*; gscale for NVFP4 only.  Contract as the single-GPU GEMV of that type, plus
