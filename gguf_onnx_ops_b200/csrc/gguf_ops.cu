@@ -36,7 +36,7 @@ namespace {
 thread_local std::string t_last_error;
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_fast{1};  // specialised kernels (R = 1 paths); 0 forces the generic engine
-constexpr bool kQ8SmallN = true;  // Q8_0 R <= 4 at K = 4096 with at most two tiles per SM: one tile per CTA
+constexpr bool kMoeCoopR1 = true;  // MoeVerify R = 1 on one GPU as one cooperative launch
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -427,12 +427,7 @@ int run_slice_iq2_i8(const void* x, const void* w, void* y, int N, int K, cudaSt
   static std::atomic<uint64_t> done{0};
   auto kern = slice_iq2_i8_kernel<kW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  const int grid = std::min(a.tiles, sms);
-  // a last round of at most grid / 2 tiles runs as half tiles on twice as many CTAs
-  const int rem = a.tiles % grid;
-  a.full_items = (rem > 0 && 2 * rem <= grid) ? a.tiles - rem : a.tiles;
-  a.items = a.full_items + 2 * (a.tiles - a.full_items);
-  cudaError_t e = launch(kern, dim3(grid), dim3(kW * 32), smem, s, a);
+  cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("single-row GEMV launch", e);
   return GGUF_OK;
 }
@@ -484,9 +479,8 @@ int try_iq2_rows(const void* x, const void* w, void* y, int R, int N, int K, cud
 }
 
 // Q8_0 2 <= R <= 4 * kNR on the integer tensor cores (slice_q8_i8_rows.cuh): 16 whole rows per
-// stage at pitch row bytes + 16, two or more stages; kMinB = 2: one stage, one tile per CTA, two
-// CTAs per SM (small N).
-template <int kW, int kNR, int kSPW = 1, int kMinB = 1>
+// stage at pitch row bytes + 16, two or more stages.
+template <int kW, int kNR, int kSPW = 1>
 int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, int K, cudaStream_t s,
                          const PeerOut* po) {
   SliceArgs a = {};
@@ -502,20 +496,18 @@ int run_slice_q8_i8_rows(const void* x, const void* w, void* y, int R, int N, in
   a.stride = a.row_bytes + 16;
   a.stage_bytes = (16 * a.stride + 127) & ~127;
   const int red_per_stage = kW * 4 * kNR * 16 * 4 + 4;  // reduction slot + counter
-  a.stages = kMinB > 1 ? 1 : std::min(4, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
-  if (a.stages < (kMinB > 1 ? 1 : 2)) return -1;  // does not fit: the caller falls back to the engine
+  a.stages = std::min(4, (kSmemBudgetMax - 256) / (a.stage_bytes + red_per_stage + 16));
+  if (a.stages < 2) return -1;  // does not fit: the caller falls back to the engine
   a.off_stage = 0;
   a.off_red = a.stages * a.stage_bytes;
   a.off_bar = (a.off_red + a.stages * red_per_stage + 15) & ~15;
   const size_t smem = a.off_bar + 2 * a.stages * 8;
-  if (kMinB > 1 && smem * kMinB > static_cast<size_t>(kSmemBudgetMax)) return -1;
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
   static std::atomic<uint64_t> done{0};
-  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW, kLayQ8, kMinB>;
+  auto kern = slice_q8_i8_rows_kernel<kW, kNR, kSPW>;
   if ((rc = ensure_smem(kern, smem, done))) return rc;
-  // row-split: the group's CTA count; one tile per CTA: every tile
-  const int grid = a.po.npeer ? a.po.ctas : (kMinB > 1 ? a.tiles : std::min(a.tiles, sms));
+  const int grid = a.po.npeer ? a.po.ctas : std::min(a.tiles, sms);  // row-split: the group's CTA count
   cudaError_t e = launch(kern, dim3(grid), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row Q8_0 GEMV launch", e);
   return GGUF_OK;
@@ -532,12 +524,6 @@ int try_q8_rows(const void* x, const void* w, void* y, int R, int N, int K, cuda
   if (g_fast.load() != 1 || R < 1 || R > 16) return -1;
   if (R > 8) return K == 4096 ? run_slice_q8_i8_rows<8, 4, 2>(x, w, y, R, N, K, s, po) : -1;
   const bool two = R > 4;
-  if (!po && !two && K == 4096 && kQ8SmallN) {
-    int sms = 0, rc;
-    if ((rc = current_sms(&sms))) return rc;
-    // small N (C0: 256 tiles): one tile per CTA, two CTAs per SM
-    if ((N + 15) / 16 <= 2 * sms) return run_slice_q8_i8_rows<8, 1, 2, 2>(x, w, y, R, N, K, s, po);
-  }
   switch (K) {
     case 2048: return two ? run_slice_q8_i8_rows<8, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<8, 1>(x, w, y, R, N, K, s, po);
     case 4096: return two ? run_slice_q8_i8_rows<8, 2, 2>(x, w, y, R, N, K, s, po) : run_slice_q8_i8_rows<16, 1>(x, w, y, R, N, K, s, po);
@@ -990,7 +976,7 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   if ((rc = current_sms(&sms))) return rc;
   cudaError_t e;
   static std::atomic<uint64_t> done{0};
-  if (R == 1 && g_fast.load() == 1 && !ep) {
+  if (kMoeCoopR1 && R == 1 && g_fast.load() == 1 && !ep) {
     // one row, one device: a single cooperative launch; grid-wide barriers take the place of the
     // per-expert counters (no zeroing kernel) and the weighted sum runs at its end (no finalize kernel)
     MoeFusedArgs b = a;

@@ -241,9 +241,7 @@ __device__ __forceinline__ void i8_records_any(const uint8_t* st, uint32_t r0, u
 
 // One 16-row x 256-column slice: decode (tables at shared offset 0), 16 MMAs, fp32 epilogue.  Gives
 // the lane's partial sums of rows g (acc0) and g+8 (acc1) over its C columns; the caller reduces
-// them over the quad (shuffles by 1 and 2).  kHalf = 1 / 2: only rows 0..7 / 8..15 of the tile are
-// wanted; the other half's records are not decoded (their A operands are zero).
-template <int kHalf = 0>
+// them over the quad (shuffles by 1 and 2).
 __device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[4], uint32_t dbits, const I8XFrag& f,
                                          float& acc0, float& acc1) {
   const int lane = threadIdx.x & 31, t = lane & 3;
@@ -256,10 +254,6 @@ __device__ __forceinline__ void i8_slice(const uint8_t* smem, const uint2 (&rc)[
     uint32_t A[4][2];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      if ((kHalf == 1 && r >= 2) || (kHalf == 2 && r < 2)) {  // rows of the other half
-        A[r][0] = A[r][1] = 0u;
-        continue;
-      }
       const uint2 X = *reinterpret_cast<const uint2*>(smem + i8_mag_addr(rc[r].x, e, lane_off));
       const uint2 M = *reinterpret_cast<const uint2*>(smem + i8_sgn_addr(rc[r].y, e, lane_off128));
       A[r][0] = X.x - 2u * (X.x & M.x);  // 64 + s*m per byte, no borrow between bytes
@@ -363,12 +357,10 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const __grid_c
       if (main) bulk_g2s(dst, src, main, &full[s]);
     }
   };
-  // work item -> tile (items past full_items are half tiles, two per tile)
-  auto tile_of = [&](int q) { return q < a.full_items ? q : a.full_items + ((q - a.full_items) >> 1); };
   if (warp == 0)
     for (int j = 0; j < a.stages; ++j) {
-      const int q = blockIdx.x + j * gridDim.x;
-      if (q < a.items) fill(j, tile_of(q));
+      const int tile = blockIdx.x + j * gridDim.x;
+      if (tile < a.tiles) fill(j, tile);
     }
 
   // ---------------- tables, built while the first tiles are in flight ----------------
@@ -407,26 +399,22 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const __grid_c
   // and loads the next round's, so their shared-memory latency overlaps the decode.
   uint2 rc[4];
   uint32_t dbits;
-  if (static_cast<int>(blockIdx.x) < a.items) {
+  if (static_cast<int>(blockIdx.x) < a.tiles) {
     mbar_wait(&full[0], 0u, kSiteFullWait);
     i8_records(stages, r0, r1, so, al, rc, dbits);
   }
-  for (int q = blockIdx.x; q < a.items; q += gridDim.x) {
-    const int tile = tile_of(q);
-    const int half = q < a.full_items ? 0 : 1 + ((q - a.full_items) & 1);  // 0 = whole tile
+  for (int tile = blockIdx.x; tile < a.tiles; tile += gridDim.x) {
     const int sn = s + 1 == a.stages ? 0 : s + 1;
     const uint32_t phn = sn == 0 ? ph ^ 1u : ph;
     uint2 rcn[4];
     uint32_t dbitsn = 0;
-    if (q + static_cast<int>(gridDim.x) < a.items) {
+    if (tile + static_cast<int>(gridDim.x) < a.tiles) {
       mbar_wait(&full[sn], phn, kSiteFullWait);
       i8_records(stages + sn * a.stage_bytes, r0, r1, so, al, rcn, dbitsn);
     }
 
     float acc0, acc1;
-    if (half == 0) i8_slice(smem, rc, dbits, xf, acc0, acc1);
-    else if (half == 1) i8_slice<1>(smem, rc, dbits, xf, acc0, acc1);
-    else i8_slice<2>(smem, rc, dbits, xf, acc0, acc1);
+    i8_slice(smem, rc, dbits, xf, acc0, acc1);
 
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
@@ -446,15 +434,14 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const __grid_c
 #pragma unroll
         for (int w2 = 0; w2 < kW; ++w2) v[w2 & 3] += rb[w2 * 16 + lane];
         const int row = tile * 16 + lane;
-        const bool mine = half == 0 || (lane >> 3) == half - 1;  // a half tile stores its 8 rows
-        if (row < a.N && mine) a.y[row] = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
+        if (row < a.N) a.y[row] = __float2bfloat16((v[0] + v[1]) + (v[2] + v[3]));
       }
       __syncwarp();
       if (lane == 0) cnt[s] = 0;
-      const int next = q + a.stages * static_cast<int>(gridDim.x);
-      if (next < a.items) {
+      const int next = tile + a.stages * static_cast<int>(gridDim.x);
+      if (next < a.tiles) {
         fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
-        fill(s, tile_of(next));
+        fill(s, next);
       }
     }
     s = sn;

@@ -102,11 +102,8 @@ __device__ __forceinline__ void q8_rows_slice(const uint8_t* st, uint32_t r0, ui
 // finish a tile sums the stage's reduction slot in warp order (deterministic), stores y [R, N] and
 // refills the stage (the last-arriver scheme of slice_iq2_i8_kernel).  kSPW = 2 halves the warps
 // and with them the reduction slots, which leaves room for a third stage at eight activation rows.
-// kMinB = 2: one tile per CTA (grid = tiles, one stage), two CTAs per SM, for small N: the CTAs of
-// the next call start on an SM while this call's second CTA there still runs, so their weight tiles
-// stream while this call finishes (one resident CTA per SM serialises the calls' HBM phases).
-template <int kW, int kNR, int kSPW = 1, int kLay = kLayQ8, int kMinB = 1>
-__global__ void __launch_bounds__(kW * 32, kMinB) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
+template <int kW, int kNR, int kSPW = 1, int kLay = kLayQ8>
+__global__ void __launch_bounds__(kW * 32, 1) slice_q8_i8_rows_kernel(const __grid_constant__ SliceArgs a) {
   constexpr bool kSplit = kLay != kLayQ8;
   constexpr int kRX = 4 * kNR;
   extern __shared__ __align__(128) uint8_t smem[];

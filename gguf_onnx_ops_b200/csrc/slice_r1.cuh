@@ -22,11 +22,9 @@
 //             (0x4500 | hi).  The MMA then sums (2176 + u) x = (q + 2304) x over the group; the
 //             epilogue subtracts 2304 * sum(x of the group) and scales by d.  32 MMAs per slice.
 //   NVFP4   : slice = 4 blocks = two halves of 8 sub-blocks of 16 (group = sub-block).  A nibble n
-//             gives the bf16 bit pattern of E2M1(n) * 2^-126 with (n * 0x1040) & 0x81C0 (a bf16
-//             subnormal for E2M1 0.5: the tensor cores take it exactly); the block-diagonal B keeps
-//             the sub-blocks in separate C columns (permuted: column 2t = group t, 2t + 1 = group
-//             t + 4), so the UE4M3 scales multiply the C cells in fp32, and x enters scaled by a
-//             power of two per slice that keeps every product a normal fp32 number.  16 MMAs per slice.
+//             gives the bf16 bit pattern of E2M1(n) * 2^-126 with (n * 0x1040) & 0x81C0; one
+//             bf16 multiply by the sub-block's UE4M3 scale * 2^110 makes it exact and normal
+//             (<= 6 significant bits), the epilogue multiplies by 2^16 * gscale.  16 MMAs per slice.
 //
 // Stage = one 16-row tile with the full K (per-row bulk copies into a padded stride).  The kW
 // partial sums of a tile are combined through a double-buffered shared-memory array (one named
@@ -64,10 +62,6 @@ struct SliceArgs {
   int sc_row_bytes, sc_off;
   // slice_fp4_rows_kernel with two activation sets: byte offset of the per-warp fragment areas
   int off_x2;
-  // slice_iq2_i8_kernel: work items [0, full_items) are whole tiles; items [full_items, items) are
-  // half tiles (item full_items + 2 i + h = rows 8 h .. 8 h + 7 of tile full_items + i), which split
-  // the last, partial round of tiles over twice as many CTAs
-  int full_items, items;
 };
 
 template <int F>
@@ -82,7 +76,7 @@ struct SliceFmt<kFmtQ8> {
 };
 template <>
 struct SliceFmt<kFmtFP4> {
-  static constexpr int kSliceBytes = 4 * 36, kLut = 1024;
+  static constexpr int kSliceBytes = 4 * 36, kLut = 512;
 };
 
 // 8 bytes at a 2-byte aligned offset; `al` = offset is 4-byte aligned (warp-uniform)
@@ -103,12 +97,6 @@ __device__ __forceinline__ void lds32b(const uint8_t* base, uint32_t off, uint32
     q[i] = __funnelshift_r(prev, nxt, sh);
     prev = nxt;
   }
-}
-// 2^n as fp32 for -126 <= n <= 127
-__device__ __forceinline__ float exp2_int(int n) { return __uint_as_float(static_cast<uint32_t>(n + 127) << 23); }
-// both bf16 halves of w times s1 * s2 (powers of two: exact while the result is a normal bf16)
-__device__ __forceinline__ uint32_t bf16x2_scale(uint32_t w, float s1, float s2) {
-  return pack_bf16x2((__uint_as_float(w << 16) * s1) * s2, (__uint_as_float(w & 0xFFFF0000u) * s1) * s2);
 }
 // c ^ (a & m): a masked field merged into constant bits c (c may overlap the field: XOR there)
 __device__ __forceinline__ uint32_t lop_xm(uint32_t a, uint32_t m, uint32_t c) {
@@ -167,65 +155,31 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
   // format tables, built while the first tiles are in flight
   if constexpr (F == kFmtIQ2) {  // codebook replicated 8x: conflict-free 16-byte lookups
     fill_iq2_lut_bf16<kW * 32>(smem, threadIdx.x);
-  } else if constexpr (F == kFmtFP4) {  // scale byte -> its gguf-py UE4M3 value in fp32 (exact)
-    float* sl = reinterpret_cast<float*>(smem);
-    for (int i = threadIdx.x; i < 256; i += kW * 32) sl[i] = __uint_as_float(fp4_scale_bf16_bits(i) << 16) * 0x1p-110f;
+  } else if constexpr (F == kFmtFP4) {
+    uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
+    for (int i = threadIdx.x; i < 256; i += kW * 32) sl[i] = static_cast<uint16_t>(fp4_scale_bf16_bits(i));
   }
   if constexpr (SliceFmt<F>::kLut > 0) named_bar_sync(1, kW * 32);
 
   const int g = lane >> 2, t = lane & 3;
-  // block-diagonal B: column c of the MMA carries group c (Q8_0 / IQ2); NVFP4 permutes the columns
-  // (column 2t = group t, 2t + 1 = group t + 4), so that the C cells of lane (g, t) are the
-  // (row, sub-block) cells whose records and scales the lane itself decodes
-  const bool dlo = F == kFmtFP4 ? (g == 2 * t) : (g == t), dhi = F == kFmtFP4 ? (g == 2 * t + 1) : (g == t + 4);
+  const bool dlo = (g == t), dhi = (g == t + 4);
   pdl_wait();  // x is produced by the previous kernel
 
   // ---- B fragments of this warp's slices, in MMA order ----
   uint32_t xa[kSPW][16], xb[kSPW][16];
-  float xoff[kSPW][2];  // Q8: 2304 * sum(x) of the lane's C columns (groups 2t, 2t+1); NVFP4: the slice's factors
+  float xoff[kSPW][2];  // Q8: 2304 * sum(x) of the lane's C columns (groups 2t, 2t+1)
 #pragma unroll
   for (int j = 0; j < kSPW; ++j) {
     const bf16* xs = a.x + (warp * kSPW + j) * 256;
     if constexpr (F == kFmtFP4) {
-      // The weights enter the MMA as bare E2M1 * 2^-126 patterns (bf16 subnormals for E2M1 0.5), the
-      // sub-block scales apply to the C cells.  So that every product stays a normal fp32 number, the
-      // slice's x is scaled by 2^Kx (exact: a power of two) to a maximum in [2^62, 2^63): E = biased
-      // exponent of the slice's largest |x|, Kx = 189 - E; the slice's sum is multiplied back by
-      // 2^(126 - Kx) = 2^(E - 63) as two exact factors (xoff).  Elements below 2^-188 of the slice's
-      // maximum are rounded (they would round away in the bf16 output anyway).
-      uint4 lv[2][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        lv[h][0] = lv[h][1] = lv[h][2] = lv[h][3] = make_uint4(0, 0, 0, 0);
-        if (dlo) lv[h][0] = ldg128(xs + h * 128 + 16 * t), lv[h][1] = ldg128(xs + h * 128 + 16 * t + 8);
-        if (dhi) lv[h][2] = ldg128(xs + h * 128 + 16 * (t + 4)), lv[h][3] = ldg128(xs + h * 128 + 16 * (t + 4) + 8);
-      }
-      uint32_t mb = 0;  // largest bf16 magnitude (magnitudes order like their bit patterns)
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t w4[4] = {lv[h][i].x, lv[h][i].y, lv[h][i].z, lv[h][i].w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) mb = max(mb, max(w4[q] & 0x7FFFu, (w4[q] >> 16) & 0x7FFFu));
-        }
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-      const int ex = max(1, static_cast<int>(mb >> 7)), kx = 189 - ex;
-      const float s1 = exp2_int(kx >> 1), s2 = exp2_int(kx - (kx >> 1));
-      xoff[j][0] = exp2_int((ex - 63) >> 1);
-      xoff[j][1] = exp2_int((ex - 63) - ((ex - 63) >> 1));
       // half h, group t: 16 elements; MMA order (0,2) (8,10) (1,3) (9,11) (4,6) (12,14) (5,7) (13,15)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint4 v0 = lv[h][0], v1 = lv[h][1], u0 = lv[h][2], u1 = lv[h][3];
-        uint32_t A[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          A[i] = bf16x2_scale(A[i], s1, s2);
-          B[i] = bf16x2_scale(B[i], s1, s2);
-        }
+        uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0, u0 = v0, u1 = v0;
+        if (dlo) v0 = ldg128(xs + h * 128 + 16 * t), v1 = ldg128(xs + h * 128 + 16 * t + 8);
+        if (dhi) u0 = ldg128(xs + h * 128 + 16 * (t + 4)), u1 = ldg128(xs + h * 128 + 16 * (t + 4) + 8);
+        const uint32_t A[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const uint32_t B[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
         uint32_t* oa = &xa[j][8 * h];
         uint32_t* ob = &xb[j][8 * h];
         oa[0] = pair_lo(A[0], A[1]); oa[1] = pair_lo(A[4], A[5]); oa[2] = pair_hi(A[0], A[1]); oa[3] = pair_hi(A[4], A[5]);
@@ -250,8 +204,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
         }
       }
     }
-    if constexpr (F == kFmtFP4) {
-    } else if constexpr (F == kFmtQ8) {
+    if constexpr (F == kFmtQ8) {
       float sa = 0.f, sb = 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -268,9 +221,9 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
     }
   }
   float post = 1.0f;
-  if constexpr (F == kFmtFP4) post = __ldg(a.gscale);
+  if constexpr (F == kFmtFP4) post = 65536.0f * __ldg(a.gscale);
   const uint32_t lut_lane = static_cast<uint32_t>(lane & 7) * 16u;
-  const float* fp4lut = reinterpret_cast<const float*>(smem);
+  const uint16_t* fp4lut = reinterpret_cast<const uint16_t*>(smem);
   const int q0 = (lane & ~3) | ((2 * t) & 3), q1 = (lane & ~3) | ((2 * t + 1) & 3);
   const int sel_sh = t >= 2 ? 4 : 0;
 
@@ -367,21 +320,19 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
         acc1 = fmaf(d10, (c[0][2] + c[1][2]) - xoff[j][0], acc1);
         acc1 = fmaf(d11, (c[0][3] + c[1][3]) - xoff[j][1], acc1);
       } else {  // NVFP4
-        float sc0 = 0.f, sc1 = 0.f;  // the slice's scaled sums of rows g, g+8
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          // records: group t = block 2h sub-block t, group t+4 = block 2h+1 sub-block t; with the
-          // permuted columns, record r's (row, sub-block) is C cell r of this lane
+          // records: group t = block 2h sub-block t, group t+4 = block 2h+1 sub-block t
           uint2 nb[4];
-          float S[4];
+          uint32_t S[4];
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             const uint32_t bo = (r < 2 ? r0 : r1) + so + 36u * static_cast<uint32_t>(2 * h + (r & 1));
             const uint32_t* w = reinterpret_cast<const uint32_t*>(st + bo + 4u + 8u * t);
             nb[r] = make_uint2(w[0], w[1]);
-            S[r] = fp4lut[st[bo + t]];
+            const uint32_t sv = fp4lut[st[bo + t]];
+            S[r] = sv | (sv << 16);
           }
-          float ch[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int ui = 0; ui < 2; ++ui) {
             uint32_t A[4][4];
@@ -390,22 +341,20 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
               const uint32_t v = ui ? nb[r].y : nb[r].x;
               const uint32_t v8 = v >> 8;
               // (b0, b2) low nibbles, (b0, b2) high, (b1, b3) low, (b1, b3) high -> E2M1 * 2^-126 patterns
-              A[r][0] = ((v & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
-              A[r][1] = ((v & 0x00F000F0u) * 0x104u) & 0x81C081C0u;
-              A[r][2] = ((v8 & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;
-              A[r][3] = ((v8 & 0x00F000F0u) * 0x104u) & 0x81C081C0u;
+              A[r][0] = hmul2_bits(((v & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S[r]);
+              A[r][1] = hmul2_bits(((v & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S[r]);
+              A[r][2] = hmul2_bits(((v8 & 0x000F000Fu) * 0x1040u) & 0x81C081C0u, S[r]);
+              A[r][3] = hmul2_bits(((v8 & 0x00F000F0u) * 0x104u) & 0x81C081C0u, S[r]);
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int bi = 8 * h + 4 * ui + k;
-              mma_bf16_16816(ch[k & 1], A[0][k], A[2][k], A[1][k], A[3][k], xa[j][bi], xb[j][bi], ch[k & 1]);
+              mma_bf16_16816(c[k & 1], A[0][k], A[2][k], A[1][k], A[3][k], xa[j][bi], xb[j][bi], c[k & 1]);
             }
           }
-          sc0 = fmaf(ch[0][0] + ch[1][0], S[0], fmaf(ch[0][1] + ch[1][1], S[1], sc0));
-          sc1 = fmaf(ch[0][2] + ch[1][2], S[2], fmaf(ch[0][3] + ch[1][3], S[3], sc1));
         }
-        acc0 = fmaf(sc0 * xoff[j][0], xoff[j][1], acc0);
-        acc1 = fmaf(sc1 * xoff[j][0], xoff[j][1], acc1);
+        acc0 += (c[0][0] + c[1][0]) + (c[0][1] + c[1][1]);
+        acc1 += (c[0][2] + c[1][2]) + (c[0][3] + c[1][3]);
       }
     }
     __syncwarp();

@@ -246,10 +246,11 @@ def test_single_row_fast_path(cuda, op, N, K, xscale):
 
 
 @pytest.mark.parametrize("N,K,xscale", [(2408, 4096, 1.0), (2650, 2048, 1.0), (2448, 5120, 1.0),
-                                        (14336, 4096, 3000.0), (14331, 4096, 1.0)])
+                                        (14336, 4096, 3000.0), (14331, 4096, 1.0), (3648, 4096, 1.0)])
 def test_iq2_single_row_partial_last_round(cuda, N, K, xscale):
     """Single-row IQ2_XXS where the tiles leave a partial last round on 148 SMs (2408 rows: 151 tiles,
     the last of 8 rows; 14336 rows: 896 tiles = 6 x 148 + 8; 14331 rows: the last tile of 11 rows).
+    3648 rows: 228 tiles = 148 + 80.
     Against the oracle on every row of the last tiles and a sample of the rest, against the generic
     engine, and bit-identical over 70 launches (fixed-order reductions, no state kept between calls)."""
     _, w, extra = I.gemv_case("iq2_xxs", 1, N, K, seed=N + K + 5)
