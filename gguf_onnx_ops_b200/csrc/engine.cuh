@@ -78,7 +78,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 // s_uexp[u] = expert id of group u, s_pair[u*8 + row] = pair index (row*topk + k) or -1.
 // Expert ids are taken relative to `offset` (the first expert this GPU holds under expert
 // parallelism; 0 otherwise); pairs whose relative id is outside [0, E) are ignored.  Returns U (in
-// shared memory).
+// shared memory).  s_idx must be 16-byte aligned.
 __device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int topk, int* s_idx, int offset = 0) {
   int* s_first = s_idx + kMaxPairs;
   int* s_rank = s_first + kMaxPairs;
@@ -89,30 +89,36 @@ __device__ __forceinline__ void moe_group(const int32_t* idx, int P, int E, int 
   for (int i = tid; i < kMaxPairs * 8; i += nth) s_pair[i] = -1;
   if (tid < P) s_idx[tid] = idx[tid] - offset;
   __syncthreads();
-  if (tid < P) {
+  if (tid < P) {  // first pair with the same expert: 4 ids per 16-byte load (s_idx is 16-byte aligned)
     const int my = s_idx[tid];
     int q = -1;
-    if (my >= 0 && my < E)
-      for (int j = 0; j <= tid; ++j)
-        if (s_idx[j] == my) {
-          q = j;
-          break;
-        }
+    if (my >= 0 && my < E) {
+      const int4* v4 = reinterpret_cast<const int4*>(s_idx);
+      for (int j = 0; j <= tid; j += 4) {
+        const int4 v = v4[j >> 2];  // in order: the scan stops at tid's own entry at the latest
+        if (v.x == my) { q = j; break; }
+        if (v.y == my) { q = j + 1; break; }
+        if (v.z == my) { q = j + 2; break; }
+        if (v.w == my) { q = j + 3; break; }
+      }
+    }
     s_first[tid] = q;
   }
   __syncthreads();
-  if (tid < P) {
-    if (s_first[tid] == tid) {
-      int r = 0;
-      for (int j = 0; j < tid; ++j) r += (s_first[j] == j);
-      s_rank[tid] = r;
-      s_uexp[r] = s_idx[tid];
+  if (tid < 32) {  // ranks of the first occurrences (their order = group order): ballots over the pairs
+    int base = 0;
+    for (int c = 0; c < P; c += 32) {
+      const int i = c + tid;
+      const bool head = i < P && s_first[i] == i;
+      const unsigned m = __ballot_sync(0xffffffffu, head);
+      if (head) {
+        const int r = base + __popc(m & ((1u << tid) - 1u));
+        s_rank[i] = r;
+        s_uexp[r] = s_idx[i];
+      }
+      base += __popc(m);
     }
-  }
-  if (tid == 0) {
-    int u = 0;
-    for (int j = 0; j < P; ++j) u += (s_first[j] == j);
-    *s_U = u;
+    if (tid == 0) *s_U = base;
   }
   __syncthreads();
   if (tid < P && s_first[tid] >= 0) s_pair[s_rank[s_first[tid]] * 8 + tid / topk] = tid;

@@ -36,7 +36,6 @@ namespace {
 thread_local std::string t_last_error;
 std::atomic<int> g_pdl{1};
 std::atomic<int> g_fast{1};  // specialised kernels (R = 1 paths); 0 forces the generic engine
-constexpr bool kMoeCoopR1 = true;  // MoeVerify R = 1 on one GPU as one cooperative launch
 
 int fail(int code, const std::string& msg) {
   t_last_error = msg;
@@ -101,31 +100,6 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
-// A cooperative launch (every CTA resident at once, grid-wide barriers allowed), with programmatic
-// dependent launch where the runtime accepts the pair, else without it.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_coop(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = g_pdl.load() ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
-  if (e != cudaSuccess && cfg.numAttrs == 2) {
-    (void)cudaGetLastError();
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-  }
-  return e;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -935,8 +909,7 @@ int gguf_relu2(const void* x, void* y, int64_t n, void* stream) {
 namespace gguf_b200 {
 namespace {
 // MoeVerify iq2=3 as: zero the phase counters (first 4P bytes of out, moe_zero_kernel), one fused persistent kernel
-// (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.  One row on one device: a single cooperative
-// launch of the fused kernel does all three.
+// (grouping + fc1 + fc2, moe_fused.cuh), one finalize kernel.
 int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const void* fc1_w, const void* fc2_w, void* out,
                   void* h, float* part, int32_t* meta, int R, int E, int I, int topk, cudaStream_t s,
                   const PeerReduce* ep = nullptr, int expert_offset = 0) {
@@ -968,34 +941,14 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
   a.off_stage = lut;
   a.off_red = lut + kMoeTeams * 2 * a.stage_bytes;
   a.off_bar = a.off_red + red;
-  a.off_grp = a.off_bar + kMoeTeams * 4 * 8;
+  a.off_grp = (a.off_bar + kMoeTeams * 4 * 8 + 15) & ~15;
   const size_t smem = a.off_grp + grp;
   if (smem > static_cast<size_t>(kSmemBudgetMax))
     return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
-  cudaError_t e;
   static std::atomic<uint64_t> done{0};
-  if (kMoeCoopR1 && R == 1 && g_fast.load() == 1 && !ep) {
-    // one row, one device: a single cooperative launch; grid-wide barriers take the place of the
-    // per-expert counters (no zeroing kernel) and the weighted sum runs at its end (no finalize kernel)
-    MoeFusedArgs b = a;
-    b.off_stage = kI8Lut;
-    b.off_red = b.off_stage + kMoeR1Teams * 2 * a.stage_bytes;
-    b.off_bar = b.off_red + kMoeR1Teams * 2 * kMoeTeamWarps * 16 * 4;
-    b.off_grp = b.off_bar + kMoeR1Teams * 4 * 8 + kMoeR1Teams * 2 * 4;  // mbarriers, then the slot counters
-    b.wts = weights;
-    b.out = static_cast<bf16*>(out);
-    const size_t smem1 = b.off_grp + grp;
-    if (smem1 > static_cast<size_t>(kSmemBudgetMax))
-      return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
-    static std::atomic<uint64_t> donec{0};
-    if ((rc = ensure_smem(moe_r1_i8_kernel<true>, smem1, donec))) return rc;
-    e = launch_coop(moe_r1_i8_kernel<true>, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
-    if (e != cudaSuccess) return cuda_fail("MoeVerify cooperative launch", e);
-    return GGUF_OK;
-  }
-  e = launch(moe_zero_kernel, dim3(1), dim3(128), 0, s, static_cast<int*>(out), P);
+  cudaError_t e = launch(moe_zero_kernel, dim3(1), dim3(128), 0, s, static_cast<int*>(out), P);
   if (e != cudaSuccess) return cuda_fail("MoeVerify counters", e);
   if (R == 1 && g_fast.load() == 1) {
     // one row: the integer single-row decode; tables at offset 0 and a smaller reduction buffer
@@ -1003,13 +956,13 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     b.off_stage = kI8Lut;
     b.off_red = b.off_stage + kMoeR1Teams * 2 * a.stage_bytes;
     b.off_bar = b.off_red + kMoeR1Teams * 2 * kMoeTeamWarps * 16 * 4;
-    b.off_grp = b.off_bar + kMoeR1Teams * 4 * 8 + kMoeR1Teams * 2 * 4;  // mbarriers, then the slot counters
+    b.off_grp = (b.off_bar + kMoeR1Teams * 4 * 8 + kMoeR1Teams * 3 * 4 + 15) & ~15;  // mbarriers, slot counters, ready words
     const size_t smem1 = b.off_grp + grp;
     if (smem1 > static_cast<size_t>(kSmemBudgetMax))
       return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
     static std::atomic<uint64_t> done1{0};
-    if ((rc = ensure_smem(moe_r1_i8_kernel<false>, smem1, done1))) return rc;
-    e = launch(moe_r1_i8_kernel<false>, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
+    if ((rc = ensure_smem(moe_r1_i8_kernel, smem1, done1))) return rc;
+    e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   } else if (g_fast.load() == 1) {
     // 2..8 rows: the integer decode shared by every pair of an expert (moe_pairs_kernel)
@@ -1017,7 +970,7 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     b.off_stage = kI8Lut;
     b.off_red = b.off_stage + kMoePTeams * 2 * a.stage_bytes;
     b.off_bar = b.off_red + kMoePTeams * 2 * kMoeTeamWarps * 8 * 16 * 4;
-    b.off_grp = b.off_bar + kMoePTeams * 4 * 8 + kMoePTeams * 2 * 4;  // mbarriers, then the slot counters
+    b.off_grp = (b.off_bar + kMoePTeams * 4 * 8 + kMoePTeams * 3 * 4 + 15) & ~15;  // mbarriers, slot counters, ready words
     b.off_zf = (b.off_grp + grp + 127) & ~127;
     const size_t smem2 = b.off_zf + static_cast<size_t>(R) * (H / 256) * kZFragBytes + kZeroBytes + kMaxPairs * 9 * 4;
     if (smem2 > static_cast<size_t>(kSmemBudgetMax)) {  // large I: the bf16-decode kernel's smaller tables

@@ -23,8 +23,6 @@
 // before this kernel; `out` is only written by the finalize kernel that follows).
 #pragma once
 
-#include <cooperative_groups.h>
-
 #include "engine.cuh"
 #include "slice_iq2_i8.cuh"
 
@@ -46,36 +44,7 @@ struct MoeFusedArgs {
   int expert_offset;  // expert parallelism: global id of local expert 0 (idx holds global ids)
   int off_stage, off_red, off_bar, off_grp;
   int off_zf;         // moe_pairs_kernel: the z fragments of every activation row (kZFragBytes per row and slice)
-  const float* wts;   // cooperative moe_r1_i8_kernel: the router weights [R, topk] and the output [R, H]
-  bf16* out;
 };
-
-// out[t, n] = bf16(sum_j w[t, j] * part[t * topk + j, n]) in fp32, j ascending, pairs with an expert
-// id outside [0, E) skipped (src/bolt_ops.cu:627-662); float4 groups i = gid, gid + gstride, ...
-// of the R x H / 4 outputs (part read through L2: written by the same launch).
-__device__ __forceinline__ void moe_finalize_rows(const float* part, const float* w, const int32_t* idx, int topk, int H,
-                                                  int E, int R, bf16* out, int gid, int gstride) {
-  const int per_row = H / 4;
-  for (int i = gid; i < R * per_row; i += gstride) {
-    const int t = i / per_row, v = i % per_row;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int j = 0; j < topk; ++j) {
-      const int pr = t * topk + j;
-      const int e = __ldg(idx + pr);
-      if (e < 0 || e >= E) continue;
-      const float wk = __ldg(w + pr);
-      const float4 pv = __ldcg(reinterpret_cast<const float4*>(part + static_cast<int64_t>(pr) * H) + v);
-      a0 += wk * pv.x;
-      a1 += wk * pv.y;
-      a2 += wk * pv.z;
-      a3 += wk * pv.w;
-    }
-    uint2 o;
-    o.x = pack_bf16x2(a0, a1);
-    o.y = pack_bf16x2(a2, a3);
-    reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * H)[v] = o;
-  }
-}
 
 constexpr int kMoeDoneWaitSite = 4;
 constexpr int kMoeTeams = 4, kMoeTeamWarps = 4, kMoeWarps = kMoeTeams * kMoeTeamWarps;
@@ -255,7 +224,42 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
 // converting the pair's h slice (read through L2) right before each.  Work split, staging, phase
 // order and outputs are those of moe_fused_kernel.  Tables (48 KB) sit at shared offset 0.
 // ---------------------------------------------------------------------------------------------
-template <bool kCoop>
+// Phase-2 item q of a team: every phase-1 tile of its expert must be in h.  The team's leader warp
+// polls the expert's counter in global memory (acquire, bounded) and then marks the item in the
+// team's ready word (release, CTA scope); the other warps wait on that word in shared memory, so
+// that one thread per team, not four, polls the counters the publishing warps update.  Items of a
+// team increase, so `ready > q` also covers an item the leader has already gone past.
+__device__ __forceinline__ void moe_wait_h(const int* done, int target, int* ready, int q, int tw, int lane) {
+  if (lane == 0) {
+    const uint64_t t0 = global_timer_ns();
+    if (tw == 0) {
+      int v;
+      for (;;) {
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
+        if (v >= target) break;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kMoeDoneWaitSite);
+          break;
+        }
+        __nanosleep(64);
+      }
+      asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(ready)), "r"(q + 1) : "memory");
+    } else {
+      int v;
+      for (;;) {
+        asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(ready)) : "memory");
+        if (v > q) break;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kMoeDoneWaitSite);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+  }
+  __syncwarp();
+}
+
 __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const MoeFusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -264,6 +268,8 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
   uint64_t* empty = full + 2;
   int* cnt = reinterpret_cast<int*>(smem + a.off_bar + kMoeR1Teams * 4 * 8) + team * 2;  // [2] arrivals per slot
+  // the team's phase-2 ready word: 1 + the last item whose expert the leader saw complete in h
+  int* ready = reinterpret_cast<int*>(smem + a.off_bar + kMoeR1Teams * 4 * 8) + 2 * kMoeR1Teams + team;
   uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
   float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 16;  // [2][warps][16]
   int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
@@ -274,10 +280,12 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
       mbar_init(&empty[s], kMoeTeamWarps);
       cnt[s] = 0;
     }
+    *ready = 0;
     fence_mbar_init();
   }
   i8_fill_tables<kMoeR1Warps * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
+  const uint4 zv = ldg128(a.z + tw * 256 + 8 * lane);  // this warp's phase-1 slice of z, in flight during the grouping
   moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
   const int* s_uexp = s_grp + 3 * kMaxPairs;
   const int* s_pair = s_uexp + kMaxPairs;
@@ -326,7 +334,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
   const int g = lane >> 2, t = lane & 3;
   // z fragments of this warp's phase-1 slice (the single row's z, slice tw of H = 1024)
   I8XFrag zf;
-  i8_x_frag(ldg128(a.z + tw * 256 + 8 * lane), zf);
+  i8_x_frag(zv, zf);
   const int slices2 = a.I / 256;
   // The warps of a team meet only through counters (as in moe_pairs_kernel): the last warp to
   // count itself into an item's slot sums it, stores the row, publishes and refills the stage.
@@ -334,22 +342,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
     int phase, u, tile;
     item_of(q, phase, u, tile);
     const int p = s_pair[u * 8];  // the pair of row 0 (R = 1)
-    if (!kCoop && phase == 2) {  // every phase-1 tile of expert u must be in h (each warp acquires)
-      if (lane == 0) {
-        const uint64_t t0 = global_timer_ns();
-        int v;
-        for (;;) {
-          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(a.done + u) : "memory");
-          if (v >= a.T1) break;
-          if (global_timer_ns() - t0 > kWaitLimitNs) {
-            record_device_error(kMoeDoneWaitSite);
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
-      __syncwarp();
-    }
+    if (phase == 2) moe_wait_h(a.done + u, a.T1, ready, q, tw, lane);  // every phase-1 tile of expert u is in h
     const int s = static_cast<int>(k & 1u);
     mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
     const uint8_t* st = stage0 + s * a.stage_bytes;
@@ -419,32 +412,19 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
       __syncwarp();  // every lane's row stores (and slot reads) before lane 0's publish / refill
       if (lane == 0) {
         cnt[s] = 0;
-        if (!kCoop && phase == 1) {  // publish: this tile of h is written
-          __threadfence();
-          atomicAdd(a.done + u, 1);
-        }
         if (q + 2 * teams < nitems) {
           fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
           fetch(q + 2 * teams, k + 2u);
         }
+        if (phase == 1) {  // publish: this tile of h is written
+          __threadfence();
+          atomicAdd(a.done + u, 1);
+        }
       }
     }
   };
-  if constexpr (!kCoop) {
-    uint32_t k = 0;
-    for (int q = first; q < nitems; q += teams, ++k) body(q, k);
-  } else {
-    // cooperative launch: grid-wide barriers order the phases, and the weighted sum over the top-k
-    // experts (the finalize step) runs here after the second one
-    int q = first;
-    uint32_t k = 0;
-    for (; q < n1; q += teams, ++k) body(q, k);
-    cooperative_groups::this_grid().sync();  // every h row is written (phase-2 weights already in flight)
-    for (; q < nitems; q += teams, ++k) body(q, k);
-    cooperative_groups::this_grid().sync();  // every part row is written
-    moe_finalize_rows(a.part, a.wts, a.idx, a.topk, a.H, a.E, a.R, a.out,
-                      static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x), static_cast<int>(gridDim.x * blockDim.x));
-  }
+  uint32_t k = 0;
+  for (int q = first; q < nitems; q += teams, ++k) body(q, k);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -563,6 +543,8 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
   uint64_t* empty = full + 2;
   int* cnt = reinterpret_cast<int*>(smem + a.off_bar + kMoePTeams * 4 * 8) + team * 2;  // [2] arrivals per slot
+  // the team's phase-2 ready word: 1 + the last item whose expert the leader saw complete in h
+  int* ready = reinterpret_cast<int*>(smem + a.off_bar + kMoePTeams * 4 * 8) + 2 * kMoePTeams + team;
   uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
   float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 8 * 16;  // [2][warps][8 pairs][16]
   int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
@@ -577,11 +559,22 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
       mbar_init(&empty[s], kMoeTeamWarps);
       cnt[s] = 0;
     }
+    *ready = 0;
     fence_mbar_init();
   }
   if (threadIdx.x < kZeroBytes / 4) reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(zero))[threadIdx.x] = 0u;
   i8_fill_tables<kMoePWarps * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
+  // z of this warp's (activation row, phase-1 slice) units (R * H / 256 <= 2 * kMoePWarps), in flight
+  // during the grouping
+  const int slices1 = a.H / 256, slices2 = a.I / 256;
+  uint4 zv[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int unit = warp + j * kMoePWarps;
+    zv[j] = unit < a.R * slices1 ? ldg128(a.z + static_cast<int64_t>(unit / slices1) * a.H + (unit % slices1) * 256 + 8 * lane)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+  }
   moe_group(a.idx, a.P, a.E, a.topk, s_grp, a.expert_offset);  // ends with __syncthreads
   const int* s_uexp = s_grp + 3 * kMaxPairs;
   const int* s_pair = s_uexp + kMaxPairs;
@@ -635,11 +628,14 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   }
 
   // the z fragments of every (activation row, phase-1 slice): one conversion per CTA
-  const int slices1 = a.H / 256, slices2 = a.I / 256;
-  for (int unit = warp; unit < a.R * slices1; unit += kMoePWarps) {
-    I8XFrag f;
-    perm_x_frag(ldg128(a.z + static_cast<int64_t>(unit / slices1) * a.H + (unit % slices1) * 256 + 8 * lane), f);
-    zfrag_store(f, zf + unit * kZFragBytes);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int unit = warp + j * kMoePWarps;
+    if (unit < a.R * slices1) {
+      I8XFrag f;
+      perm_x_frag(zv[j], f);
+      zfrag_store(f, zf + unit * kZFragBytes);
+    }
   }
   __syncthreads();
 
@@ -653,22 +649,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
     item_of(q, phase, u, tile);
     const int np = s_np[u];
     const int* pl = s_plist + u * 8;
-    if (phase == 2) {  // every phase-1 tile of expert u must be in h (each warp acquires for itself)
-      if (lane == 0) {
-        const uint64_t t0 = global_timer_ns();
-        int v;
-        for (;;) {
-          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(a.done + u) : "memory");
-          if (v >= a.T1) break;
-          if (global_timer_ns() - t0 > kWaitLimitNs) {
-            record_device_error(kMoeDoneWaitSite);
-            break;
-          }
-          __nanosleep(64);
-        }
-      }
-      __syncwarp();
-    }
+    if (phase == 2) moe_wait_h(a.done + u, a.T1, ready, q, tw, lane);  // every phase-1 tile of expert u is in h
     const int s = static_cast<int>(k & 1u);
     mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
     // this warp's partial row sums per pair.  Slot (k & 1) was summed by the last arriver of item
@@ -748,13 +729,13 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
       __syncwarp();  // every lane's row stores (and slot reads) before lane 0's publish / refill
       if (lane == 0) {
         cnt[s] = 0;
-        if (phase == 1) {  // publish: this tile of h is written
-          __threadfence();
-          atomicAdd(a.done + u, 1);
-        }
         if (q + 2 * teams < nitems) {
           fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
           fetch(q + 2 * teams, k + 2u);
+        }
+        if (phase == 1) {  // publish: this tile of h is written
+          __threadfence();
+          atomicAdd(a.done + u, 1);
         }
       }
     }
