@@ -83,23 +83,37 @@ int ensure_smem(Fn fn, size_t bytes, std::atomic<uint64_t>& done_mask) {
   return GGUF_OK;
 }
 
+// resident = true: a cooperative launch, for persistent kernels whose CTAs wait on one another (the
+// runtime starts every CTA at once or fails the launch, instead of leaving some CTAs queued behind
+// kernels of other streams while their peers wait for them).
+constexpr bool kMoeResident = true;
 template <typename... KArgs, typename... Args>
-cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+cudaError_t launch_ex(bool resident, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
   if (g_pdl.load()) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
+  if (resident) {
+    attr[na].id = cudaLaunchAttributeCooperative;
+    attr[na].val.cooperative = 1;
+    ++na;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  return launch_ex(false, kernel, grid, block, smem, s, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -962,21 +976,21 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
       return fail(GGUF_ERR_INVALID_ARGUMENT, "MoeVerify: inter size too large for the staging plan");
     static std::atomic<uint64_t> done1{0};
     if ((rc = ensure_smem(moe_r1_i8_kernel, smem1, done1))) return rc;
-    e = launch(moe_r1_i8_kernel, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
+    e = launch_ex(kMoeResident, moe_r1_i8_kernel, dim3(sms), dim3(kMoeR1Warps * 32), smem1, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   } else if (g_fast.load() == 1) {
     // 2..8 rows: the integer decode shared by every pair of an expert (moe_pairs_kernel)
     MoeFusedArgs b = a;
     b.off_stage = kI8Lut;
     b.off_red = b.off_stage + kMoePTeams * 2 * a.stage_bytes;
-    b.off_bar = b.off_red + kMoePTeams * 2 * kMoeTeamWarps * 8 * 16 * 4;
+    b.off_bar = b.off_red + kMoePTeams * 2 * kMoePTW * 8 * 16 * 4;
     b.off_grp = (b.off_bar + kMoePTeams * 4 * 8 + kMoePTeams * 3 * 4 + 15) & ~15;  // mbarriers, slot counters, ready words
     b.off_zf = (b.off_grp + grp + 127) & ~127;
     const size_t smem2 = b.off_zf + static_cast<size_t>(R) * (H / 256) * kZFragBytes + kZeroBytes + kMaxPairs * 9 * 4;
     if (smem2 > static_cast<size_t>(kSmemBudgetMax)) {  // large I: the bf16-decode kernel's smaller tables
       auto kern = moe_fused_kernel;
       if ((rc = ensure_smem(kern, smem, done))) return rc;
-      e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
+      e = launch_ex(kMoeResident, kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
       if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
       goto finalize;
     }
@@ -984,13 +998,13 @@ int run_moe_fused(const void* z, const int32_t* idx, const float* weights, const
     auto kern = moe_pairs_kernel;
     if ((rc = ensure_smem(kern, smem2, dp))) return rc;
     // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
-    e = launch(kern, dim3(sms), dim3(kMoePWarps * 32), smem2, s, b);
+    e = launch_ex(kMoeResident, kern, dim3(sms), dim3(kMoePWarps * 32), smem2, s, b);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   } else {
     auto kern = moe_fused_kernel;
     if ((rc = ensure_smem(kern, smem, done))) return rc;
     // persistent: at most one CTA per SM, so that every CTA is resident while others wait on it
-    e = launch(kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
+    e = launch_ex(kMoeResident, kern, dim3(sms), dim3(kMoeWarps * 32), smem, s, a);
     if (e != cudaSuccess) return cuda_fail("MoeVerify fused launch", e);
   }
 finalize:

@@ -440,7 +440,11 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
 // ---------------------------------------------------------------------------------------------
 constexpr int kZFragBytes = 8 * 64 + 8 * 8;  // per (row, slice): 8 groups x (8 high + 8 low limb words), xs[8], xoff[8]
 constexpr int kZeroBytes = 64;                // zero limb words for lanes whose B half is empty
-constexpr int kMoePTeams = 4, kMoePWarps = kMoePTeams * kMoeTeamWarps;
+// moe_pairs_kernel: seven teams of two warps per CTA (more tiles in flight per SM and fewer warps per
+// item reduction than four teams of four: C3 R = 8 58.7 against 63.4 µs)
+constexpr int kMoePTW = 2;
+constexpr int kMoePTeams = 7, kMoePWarps = kMoePTeams * kMoePTW;
+static_assert(kMoePTW == 2 || kMoePTW == 4, "moe_pairs_kernel sums two or four warp partials");
 
 // lane (g, t) of a permuted fragment (perm_x_frag): its non-zero B column carries group t (g = 2t,
 // words bh0 / bl0) or group t + 4 (g = 2t + 1, words bh1 / bl1); every lane holds the xs / xoff of
@@ -538,7 +542,7 @@ __device__ __forceinline__ void i8_pair_slice(const uint32_t (&A)[4][4][2], cons
 __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const MoeFusedArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int team = warp / kMoeTeamWarps, tw = warp % kMoeTeamWarps;
+  const int team = warp / kMoePTW, tw = warp % kMoePTW;
   const bool leader = tw == 0 && lane == 0;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bar) + team * 4;  // [2] full, then [2] empty
   uint64_t* empty = full + 2;
@@ -546,7 +550,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   // the team's phase-2 ready word: 1 + the last item whose expert the leader saw complete in h
   int* ready = reinterpret_cast<int*>(smem + a.off_bar + kMoePTeams * 4 * 8) + 2 * kMoePTeams + team;
   uint8_t* stage0 = smem + a.off_stage + team * 2 * a.stage_bytes;
-  float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoeTeamWarps * 8 * 16;  // [2][warps][8 pairs][16]
+  float* red = reinterpret_cast<float*>(smem + a.off_red) + team * 2 * kMoePTW * 8 * 16;  // [2][warps][8 pairs][16]
   int* s_grp = reinterpret_cast<int*>(smem + a.off_grp);
   uint8_t* zf = smem + a.off_zf;  // [R][H / 256][kZFragBytes], then kZeroBytes of zeros, then the pair lists
   const uint8_t* zero = zf + a.R * (a.H / 256) * kZFragBytes;
@@ -556,7 +560,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   if (leader) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kMoeTeamWarps);
+      mbar_init(&empty[s], kMoePTW);
       cnt[s] = 0;
     }
     *ready = 0;
@@ -565,12 +569,13 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
   if (threadIdx.x < kZeroBytes / 4) reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(zero))[threadIdx.x] = 0u;
   i8_fill_tables<kMoePWarps * 32>(smem, threadIdx.x);
   pdl_wait();  // idx (router) and z come from earlier kernels
-  // z of this warp's (activation row, phase-1 slice) units (R * H / 256 <= 2 * kMoePWarps), in flight
-  // during the grouping
+  // z of this warp's (activation row, phase-1 slice) units (R * H / 256 <= 8 * 4), in flight during
+  // the grouping
   const int slices1 = a.H / 256, slices2 = a.I / 256;
-  uint4 zv[2];
+  constexpr int kZU = (8 * 4 + kMoePWarps - 1) / kMoePWarps;
+  uint4 zv[kZU];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
+  for (int j = 0; j < kZU; ++j) {
     const int unit = warp + j * kMoePWarps;
     zv[j] = unit < a.R * slices1 ? ldg128(a.z + static_cast<int64_t>(unit / slices1) * a.H + (unit % slices1) * 256 + 8 * lane)
                                  : make_uint4(0u, 0u, 0u, 0u);
@@ -629,7 +634,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
 
   // the z fragments of every (activation row, phase-1 slice): one conversion per CTA
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
+  for (int j = 0; j < kZU; ++j) {
     const int unit = warp + j * kMoePWarps;
     if (unit < a.R * slices1) {
       I8XFrag f;
@@ -654,7 +659,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
     mbar_wait(&full[s], (k >> 1) & 1u, kSiteFullWait);
     // this warp's partial row sums per pair.  Slot (k & 1) was summed by the last arriver of item
     // k - 2 before it refilled this stage, so it is free once the stage is full again.
-    float* rbuf = red + s * kMoeTeamWarps * 8 * 16;
+    float* rbuf = red + s * kMoePTW * 8 * 16;
     float* mine = rbuf + tw * 8 * 16;
     for (int i = lane; i < np * 16; i += 32) mine[i] = 0.f;
     __syncwarp();
@@ -675,7 +680,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
       }
     };
     if (phase == 1) {
-      for (int sl = tw; sl < slices1; sl += kMoeTeamWarps) {
+      for (int sl = tw; sl < slices1; sl += kMoePTW) {
         uint2 rc[4];
         uint32_t dbits;
         i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);
@@ -688,7 +693,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
         }
       }
     } else {
-      for (int sl = tw; sl < slices2; sl += kMoeTeamWarps) {
+      for (int sl = tw; sl < slices2; sl += kMoePTW) {
         // the first pair's h slice is in flight while the tile decodes (read through L2)
         uint4 hv = __ldcg(reinterpret_cast<const uint4*>(a.h + static_cast<int64_t>(pl[0] & 0xFFFF) * a.I + sl * 256 + 8 * lane));
         uint2 rc[4];
@@ -710,14 +715,15 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
     int last = 0;
     if (lane == 0) {
       mbar_arrive(&empty[s]);
-      last = atom_add_acq_rel_cta(&cnt[s], 1) == kMoeTeamWarps - 1;
+      last = atom_add_acq_rel_cta(&cnt[s], 1) == kMoePTW - 1;
     }
     if (__shfl_sync(0xffffffffu, last, 0)) {  // every warp's partials of this item are in the slot
       for (int ti = lane; ti < np * 16; ti += 32) {
         const int i = ti >> 4, rl = ti & 15;
         const int p = pl[i] & 0xFFFF;
-        // fixed order: warps 0 + 1, then 2 + 3
-        const float v = (rbuf[ti] + rbuf[128 + ti]) + (rbuf[256 + ti] + rbuf[384 + ti]);
+        // fixed order: warps 0 + 1 (then 2 + 3 with four-warp teams)
+        const float v = kMoePTW == 4 ? (rbuf[ti] + rbuf[128 + ti]) + (rbuf[256 + ti] + rbuf[384 + ti])
+                                     : rbuf[ti] + rbuf[128 + ti];
         const float vb = round_bf16(v);
         if (phase == 1) {
           const float rr = fmaxf(vb, 0.f);
