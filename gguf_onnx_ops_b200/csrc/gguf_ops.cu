@@ -881,9 +881,24 @@ int run_route(const char* op, const void* x, const WT* gate_w, const float* bias
   if (!aligned(x, 16) || !aligned(gate_w, 16))
     return fail(GGUF_ERR_INVALID_ARGUMENT, std::string(op) + ": x and gate_w must be 16-byte aligned");
   const int clusters = static_cast<int>((R + kRouteRows - 1) / kRouteRows);
-  cudaError_t e = launch(route_kernel<WT>, dim3(clusters * kRouteCtas), dim3(kRouteWarps * 32), 0,
-                         static_cast<cudaStream_t>(stream), static_cast<const bf16*>(x), gate_w, bias, (int)R, (int)K,
-                         (int)E, (int)topk, scale, idx, weights, scores);
+  // the cluster's x rows staged in shared memory when they fit in 64 KB (K <= 4096)
+  const size_t xs = static_cast<size_t>(kRouteRows) * K * 2;
+  const bool staged = xs <= 64 * 1024;
+  cudaError_t e;
+  if (staged) {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load() & bit)) {
+      e = cudaFuncSetAttribute(route_kernel<WT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      if (e != cudaSuccess) return cuda_fail("cudaFuncSetAttribute", e);
+      done.fetch_or(bit);
+    }
+  }
+  e = launch(staged ? route_kernel<WT, true> : route_kernel<WT, false>, dim3(clusters * kRouteCtas),
+             dim3(kRouteWarps * 32), staged ? xs : 0, static_cast<cudaStream_t>(stream), static_cast<const bf16*>(x), gate_w,
+             bias, (int)R, (int)K, (int)E, (int)topk, scale, idx, weights, scores);
   if (e != cudaSuccess) return cuda_fail((std::string(op) + " launch").c_str(), e);
   return GGUF_OK;
 }

@@ -126,7 +126,10 @@ struct GateChunk<bf16> {
   }
 };
 
-template <typename WT>
+// kStaged: the cluster's x rows are copied once into shared memory (dynamic, kRouteRows x K bf16)
+// right after the dependency wait, one load round trip for all rows, and every warp reads its
+// chunks from there; otherwise each warp loads its rows' chunks through L1 row by row.
+template <typename WT, bool kStaged>
 __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps * 32)
     route_kernel(const bf16* __restrict__ x, const WT* __restrict__ gw, const float* __restrict__ bias, int R, int K,
                  int E, int topk, float scale, int32_t* __restrict__ idx_out, float* __restrict__ w_out,
@@ -158,6 +161,15 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
   }
   pdl_wait();
   pdl_launch_dependents();
+  extern __shared__ __align__(16) uint8_t route_xs[];
+  const bf16* xr = x + static_cast<int64_t>(row0) * K;  // the cluster's first row (global, or staged)
+  if constexpr (kStaged) {
+    const uint4* src = reinterpret_cast<const uint4*>(xr);
+    uint4* dst = reinterpret_cast<uint4*>(route_xs);
+    for (int i = threadIdx.x; i < nrows * (K / 8); i += kRouteWarps * 32) dst[i] = ldg128(src + i);
+    __syncthreads();
+    xr = reinterpret_cast<const bf16*>(route_xs);
+  }
   for (int e = e_first; e < e_hi; e += kRouteWarps) {
     const WT* wr = gw + static_cast<int64_t>(e) * K;
     float acc[kRouteRows];
@@ -170,7 +182,8 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
 #pragma unroll
       for (int r = 0; r < kRouteRows; ++r) {
         if (r < nrows) {
-          const uint4 xv = ldg128(x + static_cast<int64_t>(row0 + r) * K + k);
+          const uint4 xv = kStaged ? *reinterpret_cast<const uint4*>(xr + static_cast<int64_t>(r) * K + k)
+                                   : ldg128(xr + static_cast<int64_t>(r) * K + k);
           const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -192,8 +205,9 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
         uint4 xv[kRoutePre];
 #pragma unroll
         for (int c = 0; c < kRoutePre; ++c)
-          xv[c] = c * 256 + lane * 8 < K ? ldg128(x + static_cast<int64_t>(row0 + r) * K + c * 256 + lane * 8)
-                                         : make_uint4(0u, 0u, 0u, 0u);
+          xv[c] = c * 256 + lane * 8 >= K ? make_uint4(0u, 0u, 0u, 0u)
+                  : kStaged ? *reinterpret_cast<const uint4*>(xr + static_cast<int64_t>(r) * K + c * 256 + lane * 8)
+                            : ldg128(xr + static_cast<int64_t>(r) * K + c * 256 + lane * 8);
 #pragma unroll
         for (int c = 0; c < kRoutePre; ++c) {
           if (c * 256 + lane * 8 >= K) break;
