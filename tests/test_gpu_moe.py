@@ -50,8 +50,10 @@ def test_route_golden(cuda, golden, name):
 
 @pytest.mark.parametrize("R,E,K,topk,scale", [(1, 128, 1024, 6, 1.0), (4, 128, 1024, 6, 1.0), (8, 128, 1024, 6, 1.0),
                                               (3, 240, 4096, 9, 5.0), (8, 496, 2048, 9, 2.5), (21, 128, 1024, 6, 1.0),
-                                              (5, 512, 256, 32, 1.0), (2, 7, 256, 1, 1.0), (9, 13, 512, 13, 0.5)])
+                                              (5, 512, 256, 32, 1.0), (2, 7, 256, 1, 1.0), (9, 13, 512, 13, 0.5),
+                                              (3, 128, 8192, 6, 1.0), (10, 64, 5120, 4, 1.0)])
 def test_route_shapes(cuda, R, E, K, topk, scale):
+    """Router shapes, including K > 4096 (x rows read through L1 instead of staged in shared memory)."""
     g = I.rng(R * 1000 + E)
     x = I.bf16_normal(g, (R, K))
     gw = (g.standard_normal((E, K)) * 0.02).astype(np.float32)
