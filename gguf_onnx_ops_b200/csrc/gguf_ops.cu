@@ -84,8 +84,8 @@ int ensure_smem(Fn fn, size_t bytes, std::atomic<uint64_t>& done_mask) {
 }
 
 // resident = true: a cooperative launch, for persistent kernels whose CTAs wait on one another (the
-// runtime starts every CTA at once or fails the launch, instead of leaving some CTAs queued behind
-// kernels of other streams while their peers wait for them).
+// runtime starts all CTAs together, or fails the launch if they cannot all be resident at once,
+// instead of starting some while others stay queued behind kernels of other streams).
 constexpr bool kMoeResident = true;
 template <typename... KArgs, typename... Args>
 cudaError_t launch_ex(bool resident, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
