@@ -46,6 +46,13 @@ struct MoeFusedArgs {
   int off_zf;         // moe_pairs_kernel: the z fragments of every activation row (kZFragBytes per row and slice)
 };
 
+// Publishes a finished fc1 tile: +1 on the expert's counter with release semantics at GPU scope
+// (the caller's warp's, or after a barrier its CTA's, h stores are visible to whoever acquires the
+// new count), without a separate full fence.
+__device__ __forceinline__ void moe_publish(int* counter) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(counter) : "memory");
+}
+
 constexpr int kMoeDoneWaitSite = 4;
 constexpr int kMoeTeams = 4, kMoeTeamWarps = 4, kMoeWarps = kMoeTeams * kMoeTeamWarps;
 // The single-row kernel runs five teams per CTA (20 warps): 5 x 148 teams cover a decode step's
@@ -207,10 +214,7 @@ __global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_fused_kernel(const MoeF
     if (leader && q + 2 * teams < nitems) fetch(q + 2 * teams, k + 2u);
     if (phase == 1) {  // publish: this tile of h is written (every team thread is past its store)
       named_bar_sync(bar_id, bar_n);
-      if (leader) {
-        __threadfence();
-        atomicAdd(a.done + u, 1);
-      }
+      if (leader) moe_publish(a.done + u);
     }
   }
 }
@@ -416,10 +420,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
           fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
           fetch(q + 2 * teams, k + 2u);
         }
-        if (phase == 1) {  // publish: this tile of h is written
-          __threadfence();
-          atomicAdd(a.done + u, 1);
-        }
+        if (phase == 1) moe_publish(a.done + u);  // this tile of h is written
       }
     }
   };
@@ -739,10 +740,7 @@ __global__ void __launch_bounds__(kMoePWarps * 32, 1) moe_pairs_kernel(const Moe
           fence_proxy_async_smem();  // the warps' generic reads of the stage before the copy engine's writes
           fetch(q + 2 * teams, k + 2u);
         }
-        if (phase == 1) {  // publish: this tile of h is written
-          __threadfence();
-          atomicAdd(a.done + u, 1);
-        }
+        if (phase == 1) moe_publish(a.done + u);  // this tile of h is written
       }
     }
   }
