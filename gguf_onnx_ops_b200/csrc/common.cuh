@@ -23,7 +23,7 @@ enum DeviceErrorSite : int {
   kSiteFullWait = 1,     // consumer waited too long for a weight stage
   kSiteEmptyWait = 2,    // producer waited too long for a free stage
   kSiteDrainWait = 3,    // producer waited too long for its last copies at exit
-  kSitePeerWait = 5,     // a sharded op waited too long for a peer GPU's completion flag
+  kSitePeerWait = 5,     // a sharded op waited too long for a peer GPU (its row-split words or EP partials)
   kSiteBadStateRow = 6,  // MambaVerify: the device-side state row was outside [0, state_rows) (row 0 used)
 };
 
