@@ -73,6 +73,9 @@ struct EngineArgs {
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 // Unique-expert grouping of idx (first-occurrence order, as src/bolt_ops.cu:1233-1261):
 // s_uexp[u] = expert id of group u, s_pair[u*8 + row] = pair index (row*topk + k) or -1.

@@ -357,8 +357,11 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const __grid_c
       if (main) bulk_g2s(dst, src, main, &full[s]);
     }
   };
+  // Two stages are requested before the dependency wait, the rest once every warp has issued its load
+  // of x: behind all eight stages' bulk copies that load returned late (C1: 10.22 -> 9.83 µs).
+  const int pre = min(a.stages, 2);
   if (warp == 0)
-    for (int j = 0; j < a.stages; ++j) {
+    for (int j = 0; j < pre; ++j) {
       const int tile = blockIdx.x + j * gridDim.x;
       if (tile < a.tiles) fill(j, tile);
     }
@@ -374,6 +377,14 @@ __global__ void __launch_bounds__(kW * 32, 1) slice_iq2_i8_kernel(const __grid_c
 
   // ---- x fragments of this warp's slice: lane l converts elements 8l..8l+7 (group l >> 2) ----
   uint4 xv = ldg128(a.x + warp * 256 + 8 * lane);
+  if (pre < a.stages) {
+    __syncthreads();  // every warp's x load is issued before the remaining stages' copies
+    if (warp == 0)
+      for (int j = pre; j < a.stages; ++j) {
+        const int tile = blockIdx.x + j * gridDim.x;
+        if (tile < a.tiles) fill(j, tile);
+      }
+  }
   if (a.gamma != nullptr) {
     // fused (Skip)RmsNorm: thread t holds chunk t of the 4096-element row, the layout of the
     // standalone kernel's 512 threads, so the mean of squares (and every output bit) is the same

@@ -53,12 +53,11 @@ struct I8RowsX {
 // r = p + (1.5 * 2^23 + 128) rounds p to an integer (nearest, ties to even) whose low 16 bits are
 // those of x_int + 128: byte 1 is the high limb (x_int + 128) >> 8 and byte 0 ^ 0x80 the low limb
 // x_int mod 256.
-template <int kNR, bool kOff = true>
-__device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice, I8RowsX<kNR, kOff>& f) {
+// The load half: the lane's activation words (issued at once; i8_rows_x_cvt consumes them).
+template <int kNR>
+__device__ __forceinline__ void i8_rows_x_load(const bf16* x, int R, int K, int slice, uint2 (&xv)[kNR][8]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const bool odd = (g & 1) != 0;
-  const float magic = 12582912.0f + 128.0f;
-  uint2 xv[kNR][8];
 #pragma unroll
   for (int m = 0; m < kNR; ++m) {
     const int xr = 4 * m + (g >> 1);
@@ -68,6 +67,21 @@ __device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice
                                                                8 * t + (odd ? 4 : 0)))
                         : make_uint2(0u, 0u);
   }
+}
+template <int kNR, bool kOff = true>
+__device__ __forceinline__ void i8_rows_x_cvt(const uint2 (&xv)[kNR][8], I8RowsX<kNR, kOff>& f);
+template <int kNR, bool kOff = true>
+__device__ __forceinline__ void i8_rows_x(const bf16* x, int R, int K, int slice, I8RowsX<kNR, kOff>& f) {
+  uint2 xv[kNR][8];
+  i8_rows_x_load<kNR>(x, R, K, slice, xv);
+  i8_rows_x_cvt<kNR, kOff>(xv, f);
+}
+// The conversion half.
+template <int kNR, bool kOff>
+__device__ __forceinline__ void i8_rows_x_cvt(const uint2 (&xv)[kNR][8], I8RowsX<kNR, kOff>& f) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const bool odd = (g & 1) != 0;
+  const float magic = 12582912.0f + 128.0f;
 #pragma unroll
   for (int m = 0; m < kNR; ++m) {
 #pragma unroll
