@@ -42,6 +42,12 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// 2^n for -149 <= n <= 127, exactly (the IEEE single layout: exponent field n + 127 for normal numbers,
+// one significand bit for subnormal ones); a few integer instructions where ldexpf is a library call.
+__device__ __forceinline__ float pow2i(int n) {
+  return __uint_as_float(n >= -126 ? static_cast<uint32_t>(n + 127) << 23 : 1u << (n + 149));
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kRbWarps * 32, 1) iq2_rowblock_kernel(const Ro
     *reinterpret_cast<uint2*>(gw + j0) = make_uint2(hw[0], hw[1]);
     *reinterpret_cast<uint2*>(gw + 8 + j0) = make_uint2(lw[0], lw[1]);
     if ((i & 3) == 0) {
-      xsc[grp] = ldexpf(1.0f, emax - 141);
+      xsc[grp] = pow2i(emax - 141);
       xof[grp] = 64 * xsum;
     }
   }

@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
   const int g = lane >> 2, t = lane & 3;
   // z fragments of this warp's phase-1 slice (the single row's z, slice tw of H = 1024)
   I8XFrag zf;
-  i8_x_frag(zv, zf);
+  i8_x_frag<true>(zv, zf);
   const int slices2 = a.I / 256;
   // The warps of a team meet only through counters (as in moe_pairs_kernel): the last warp to
   // count itself into an item's slot sums it, stores the row, publishes and refills the stage.
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kMoeR1Warps * 32, 1) moe_r1_i8_kernel(const Mo
         for (int j = 1; j < kHPre; ++j)
           if (i == j) xv = hv[j];
         if (i >= kHPre) xv = __ldcg(reinterpret_cast<const uint4*>(hp + sl * 256 + 8 * lane));
-        i8_x_frag(xv, hf);
+        i8_x_frag<true>(xv, hf);
         uint2 rc[4];
         uint32_t dbits;
         i8_records_any(st, r0, r1, static_cast<uint32_t>(sl) * 66u, rc, dbits);

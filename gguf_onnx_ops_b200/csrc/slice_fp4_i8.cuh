@@ -90,8 +90,8 @@ __device__ __forceinline__ void f4_x_frag(const uint2 xv, F4XFrag& f) {
     f.bl1[j] = dhi ? l : 0u;
   }
   const int e0 = __shfl_sync(0xffffffffu, emax, 4 * (2 * t)), e1 = __shfl_sync(0xffffffffu, emax, 4 * (2 * t + 1));
-  f.xs0 = ldexpf(1.0f, e0 - 141);  // 2^(E - 14), E = emax - 127
-  f.xs1 = ldexpf(1.0f, e1 - 141);
+  f.xs0 = pow2i(e0 - 141);  // 2^(E - 14), E = emax - 127
+  f.xs1 = pow2i(e1 - 141);
 }
 
 // gguf-py's UE4M3 scale value times 0.5 (the factor of the doubled magnitudes), exact in fp32: byte

@@ -110,7 +110,7 @@ __device__ __forceinline__ void i8_rows_x_cvt(const uint2 (&xv)[kNR][8], I8RowsX
       f.b[m][j][0] = odd ? other : hi;  // elements 8t..8t+3
       f.b[m][j][1] = odd ? lo : other;  // elements 8t+4..8t+7
       // this lane's C columns (2t, 2t+1) are activation row 4m + t, converted by quads 2t, 2t + 1 (lane 8t)
-      f.xs[m][j] = ldexpf(1.0f, __shfl_sync(0xffffffffu, emax, 8 * t) - 140);  // 2^(E - 13), E = emax - 127
+      f.xs[m][j] = pow2i(__shfl_sync(0xffffffffu, emax, 8 * t) - 140);  // 2^(E - 13), E = emax - 127
       if constexpr (kOff) {
         int xsum = static_cast<int>(rsum - 4u * (0x4B400000u + 128u));  // sum of x_int (mod 2^32, exact)
         xsum += __shfl_xor_sync(0xffffffffu, xsum, 4);

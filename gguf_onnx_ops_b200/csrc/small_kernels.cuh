@@ -16,6 +16,7 @@ namespace gguf_b200 {
 // (src/bolt_ops.cu:459-510).
 // ---------------------------------------------------------------------------------------------
 constexpr int kRouteCtas = 8, kRouteRows = 8, kRouteWarps = 16;
+static_assert(kRouteRows < kRouteWarps, "CTA 0's warps past the selecting ones write the scores output");
 constexpr int kRouteMaxE = 512;  // experts the router takes (the op contract)
 constexpr int kRoutePre = 4;  // 256-element chunks of a warp's first gate row fetched before the dependency wait
 
@@ -230,13 +231,19 @@ __global__ void __cluster_dims__(kRouteCtas, 1, 1) __launch_bounds__(kRouteWarps
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == 0 && r < nrows) {
         const float sg = 1.0f / (1.0f + expf(-v));
-        scores[static_cast<int64_t>(row0 + r) * E + e] = sg;
         st_shared_cluster_f32(map_shared_cta0(&s_sc[r][e]), sg);  // CTA 0's copy for the top-k
       }
     }
   }
   cluster_sync_all();  // every CTA's remote score stores are visible in CTA 0 (release / acquire)
-  if (rank != 0 || warp >= nrows) return;
+  if (rank != 0) return;
+  // The scores output is written from CTA 0's copy by the warps that select nothing, after the
+  // barrier, so that the barrier's release does not wait for global stores (C3 R = 4: 36.3 -> 34.8 µs).
+  if (warp >= nrows) {
+    for (int i = (warp - nrows) * 32 + lane; i < nrows * E; i += (kRouteWarps - nrows) * 32)
+      scores[static_cast<int64_t>(row0 + i / E) * E + i % E] = s_sc[i / E][i % E];
+    return;
+  }
   const int row = row0 + warp;
   if (E <= 128) route_select<4>(s_sc[warp], reinterpret_cast<const float(&)[4]>(bv), row, E, topk, scale, idx_out, w_out);
   else if (E <= 256) route_select<8>(s_sc[warp], reinterpret_cast<const float(&)[8]>(bv), row, E, topk, scale, idx_out, w_out);
