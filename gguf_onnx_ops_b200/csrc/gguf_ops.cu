@@ -580,7 +580,10 @@ int try_q8s_rows(const void* x, const void* w, const void* scales, void* y, int 
   }
 }
 
-// NVFP4 2 <= R <= 8 kNB on the bf16 tensor cores with the activation rows as MMA columns
+// Tiles per SM from which the few-row NVFP4 kernel takes f16 operands (slice_fp4_rows.cuh, kF16).
+constexpr int kFp4F16MinRounds = 4;
+
+// NVFP4 2 <= R <= 8 kNB on the f16 / bf16 tensor cores with the activation rows as MMA columns
 // (slice_fp4_rows.cuh): 16 whole rows per stage at pitch row bytes + 32; with kNB = 2 the second
 // set of 8 rows is packed into 4 KB of shared memory per warp, ahead of the stages.
 template <int kW, int kNB = 1>
@@ -607,9 +610,11 @@ int run_slice_fp4_rows(const void* x, const void* w, const float* gscale, void* 
   const size_t smem = a.off_bar + 2 * a.stages * 8;
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
-  static std::atomic<uint64_t> done{0};
-  auto kern = slice_fp4_rows_kernel<kW, false, kNB>;
-  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  static std::atomic<uint64_t> done{0}, done16{0};
+  // f16 operands for one activation set when the launch is long enough to repay their x prologue
+  const bool f16 = kNB == 1 && a.tiles >= kFp4F16MinRounds * sms;
+  auto kern = f16 ? slice_fp4_rows_kernel<kW, false, kNB, kNB == 1> : slice_fp4_rows_kernel<kW, false, kNB, false>;
+  if ((rc = ensure_smem(kern, smem, f16 ? done16 : done))) return rc;
   cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row NVFP4 GEMV launch", e);
   return GGUF_OK;
@@ -648,9 +653,10 @@ int run_slice_fp4s_rows(const void* x, const void* w, const void* scales, const 
   const size_t smem = a.off_bar + 2 * a.stages * 8;
   int sms = 0, rc;
   if ((rc = current_sms(&sms))) return rc;
-  static std::atomic<uint64_t> done{0};
-  auto kern = slice_fp4_rows_kernel<kW, true>;
-  if ((rc = ensure_smem(kern, smem, done))) return rc;
+  static std::atomic<uint64_t> done{0}, done16{0};
+  const bool f16 = a.tiles >= kFp4F16MinRounds * sms;
+  auto kern = f16 ? slice_fp4_rows_kernel<kW, true, 1, true> : slice_fp4_rows_kernel<kW, true, 1, false>;
+  if ((rc = ensure_smem(kern, smem, f16 ? done16 : done))) return rc;
   cudaError_t e = launch(kern, dim3(std::min(a.tiles, sms)), dim3(kW * 32), smem, s, a);
   if (e != cudaSuccess) return cuda_fail("few-row Nvfp4Gemv gguf=0 launch", e);
   return GGUF_OK;
