@@ -340,6 +340,37 @@ def test_nvfp4_few_row_kernel(cuda, R, N, K):
     assert_device_ok()
 
 
+@pytest.mark.parametrize("R", [2, 5, 8])
+@pytest.mark.parametrize("K", [4096, 5120])
+def test_nvfp4_few_row_f16_operands(cuda, R, K):
+    """Launches of at least 4 tiles per SM take the few-row NVFP4 kernel's f16 operands (hardware E2M1
+    conversion, per-row power-of-two x scaling): against the oracle and the generic engine, with a
+    ragged last tile, every scale byte present and a row of large and one of tiny activations."""
+    import torch
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    N = 16 * 4 * sms + 37
+    g = I.rng(K + 7 * R)
+    w = I.nvfp4_weights(g, N, K, 0, 255)
+    x = I.bf16_normal(g, (R, K), 2.0)
+    big = I.bf16_normal(g, (1, K), 3000.0)
+    tiny = I.bf16_normal(g, (1, K), 2.0 ** -100)
+    x[0], x[R - 1] = big[0], tiny[0]
+    extra = {"gscale": np.array([0.37], np.float32)}
+    y = run_gemv("nvfp4", x, w, extra, cuda)
+    assert np.isfinite(y).all()
+    ref = oracle_y("nvfp4", x, w, extra, np.arange(N))
+    for r in range(R):  # each activation row on its own scale
+        assert rel(y[r], ref[r]) < TOL, r
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_gemv("nvfp4", x, w, extra, cuda)
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+    assert_device_ok()
+
+
 @pytest.mark.parametrize("K", [2048, 4096, 5120, 6144, 8192])
 def test_nvfp4_single_row_integer_kernel(cuda, K):
     """The single-row NVFP4 kernels (bf16 slice, the default, and the integer-decode variant, mode 4)

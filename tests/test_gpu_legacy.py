@@ -140,6 +140,28 @@ def test_legacy_reference_shapes(cuda):
         assert rel(y.float().cpu().numpy(), O.gemv_ref(x, deq(layout, w, s))) < TOL, (layout, R, N, K)
 
 
+@pytest.mark.parametrize("R", [2, 8])
+def test_fp4_split_few_row_f16_operands(cuda, R):
+    """Nvfp4Gemv gguf=0 on launches of at least 4 tiles per SM (the few-row kernel's f16 operands)
+    against the oracle and the generic engine."""
+    import torch
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    N, K = 16 * 4 * sms + 21, 4096
+    g = I.rng(31 * R)
+    w, sc = I.legacy_case("fp4", g, N, K)
+    x = I.bf16_normal(g, (R, K), 2.0)
+    y = run_layout("fp4", x, w, sc, cuda).float().cpu().numpy()
+    assert np.isfinite(y).all()
+    assert rel(y, O.gemv_ref(x, deq("fp4", w, sc))) < TOL
+    ops.set_fast_paths(False)
+    try:
+        y_gen = run_layout("fp4", x, w, sc, cuda).float().cpu().numpy()
+    finally:
+        ops.set_fast_paths(True)
+    assert rel(y, y_gen) < 2e-3
+
+
 def test_fp4_every_scale_byte(cuda):
     """Every non-NaN e4m3fn scale byte (both signs, subnormals) decodes exactly."""
     g = I.rng(9)
