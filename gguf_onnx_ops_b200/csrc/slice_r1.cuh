@@ -23,11 +23,13 @@
 //             epilogue subtracts 2304 * sum(x of the group) and scales by d.  32 MMAs per slice.
 //   NVFP4   : slice = 4 blocks = two halves of 8 sub-blocks of 16 (group = sub-block).  f16 operands:
 //             each nibble byte (element j low, j + 8 high) goes through sm_100's E2M1 converter
-//             (cvt.rn.f16x2.e2m1x2) and one f16x2 multiply by the sub-block's UE4M3 scale (exact:
-//             <= 6 significant bits, >= 2^-10); x is scaled per slice by 2^s (max |x| 2^s < 2^15,
-//             exact in f16) and the epilogue multiplies by 2^-s and gscale.  16 MMAs per slice.
-//             (The former decode, bf16 patterns (n * 0x1040) & 0x81C0 times scale * 2^110, took
-//             four instructions per pair; C2 R = 1: 12.45 -> 10.81 µs.)
+//             (cvt.rn.f16x2.e2m1x2), one instruction per element pair; x is scaled per slice by 2^s
+//             (max |x| 2^s < 2^15, exact in f16).  The block-diagonal B puts each sub-block in its own
+//             C column, so the UE4M3 scales are applied to the C cells in fp32 after each half's
+//             MMAs (a 256-entry float table), and the epilogue multiplies by 2^-s and gscale.  16 MMAs
+//             per slice.  (Before: the bf16 patterns (n * 0x1040) & 0x81C0 times scale * 2^110, four
+//             instructions per pair, C2 R = 1 12.45 µs; the converter with an f16x2 scale multiply per
+//             pair, 10.80 µs; now 10.07 µs.)
 //
 // Stage = one 16-row tile with the full K (per-row bulk copies into a padded stride).  The kW
 // partial sums of a tile are combined through a double-buffered shared-memory array (one named
@@ -79,7 +81,7 @@ struct SliceFmt<kFmtQ8> {
 };
 template <>
 struct SliceFmt<kFmtFP4> {
-  static constexpr int kSliceBytes = 4 * 36, kLut = 512;
+  static constexpr int kSliceBytes = 4 * 36, kLut = 1024;
 };
 
 // 8 bytes at a 2-byte aligned offset; `al` = offset is 4-byte aligned (warp-uniform)
@@ -196,9 +198,9 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
   if constexpr (F == kFmtIQ2) {  // codebook replicated 8x: conflict-free 16-byte lookups
     fill_iq2_lut_bf16<kW * 32>(smem, threadIdx.x);
   } else if constexpr (F == kFmtFP4) {
-    uint16_t* sl = reinterpret_cast<uint16_t*>(smem);
-    for (int i = threadIdx.x; i < 256; i += kW * 32)
-      sl[i] = __half_as_ushort(__float2half_rn(__uint_as_float(fp4_scale_bf16_bits(i) << 16) * 0x1p-110f));
+    // UE4M3 scale byte -> its value (the bf16 pattern of scale * 2^110, times 2^-110: exact)
+    float* slf = reinterpret_cast<float*>(smem);
+    for (int i = threadIdx.x; i < 256; i += kW * 32) slf[i] = __uint_as_float(fp4_scale_bf16_bits(i) << 16) * 0x1p-110f;
   }
   if constexpr (SliceFmt<F>::kLut > 0) named_bar_sync(1, kW * 32);
 
@@ -385,37 +387,41 @@ __global__ void __launch_bounds__((kW + 1) * 32, 1) slice_r1_kernel(const SliceA
         acc1 = fmaf(d10, (c[0][2] + c[1][2]) - xoff[j][0], acc1);
         acc1 = fmaf(d11, (c[0][3] + c[1][3]) - xoff[j][1], acc1);
       } else {  // NVFP4
+        // bare E2M1 values into the MMA; C column c of half h is one sub-block (block 2h + (c >> 2),
+        // sub-block c & 3), so lane (g, t)'s cells (columns 2t, 2t+1) take the scales of block
+        // 2h + (t >> 1), sub-blocks 2 (t & 1) and 2 (t & 1) + 1, applied in fp32 after the half's MMAs
+        const float* slf = reinterpret_cast<const float*>(smem);
+        float y0 = 0.f, y1 = 0.f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          // records: group t = block 2h sub-block t, group t+4 = block 2h+1 sub-block t
           uint2 nb[4];
-          uint32_t S[4];
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             const uint32_t bo = (r < 2 ? r0 : r1) + so + 36u * static_cast<uint32_t>(2 * h + (r & 1));
             const uint32_t* w = reinterpret_cast<const uint32_t*>(st + bo + 4u + 8u * t);
             nb[r] = make_uint2(w[0], w[1]);
-            const uint32_t sv = fp4lut[st[bo + t]];
-            S[r] = sv | (sv << 16);
           }
+          const uint32_t sbo = so + 36u * static_cast<uint32_t>(2 * h + (t >> 1)) + 2u * static_cast<uint32_t>(t & 1);
+          const uint32_t sb0 = ld_u16(st, r0 + sbo), sb1 = ld_u16(st, r1 + sbo);
+          float ch[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int ui = 0; ui < 2; ++ui) {
             uint32_t A[4][4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-              e2m1x4_to_f16x2(ui ? nb[r].y : nb[r].x, A[r]);
-#pragma unroll
-              for (int k = 0; k < 4; ++k) A[r][k] = hmul2_f16_bits(A[r][k], S[r]);
-            }
+            for (int r = 0; r < 4; ++r) e2m1x4_to_f16x2(ui ? nb[r].y : nb[r].x, A[r]);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int bi = 8 * h + 4 * ui + k;
-              mma_f16_16816(c[k & 1], A[0][k], A[2][k], A[1][k], A[3][k], xa[j][bi], xb[j][bi], c[k & 1]);
+              mma_f16_16816(ch[k & 1], A[0][k], A[2][k], A[1][k], A[3][k], xa[j][bi], xb[j][bi], ch[k & 1]);
             }
           }
+          y0 = fmaf(ch[0][0] + ch[1][0], slf[sb0 & 0xFFu], y0);
+          y0 = fmaf(ch[0][1] + ch[1][1], slf[sb0 >> 8], y0);
+          y1 = fmaf(ch[0][2] + ch[1][2], slf[sb1 & 0xFFu], y1);
+          y1 = fmaf(ch[0][3] + ch[1][3], slf[sb1 >> 8], y1);
         }
-        acc0 += ((c[0][0] + c[1][0]) + (c[0][1] + c[1][1])) * xinv[j];
-        acc1 += ((c[0][2] + c[1][2]) + (c[0][3] + c[1][3])) * xinv[j];
+        acc0 += y0 * xinv[j];
+        acc1 += y1 * xinv[j];
       }
     }
     __syncwarp();
